@@ -1,0 +1,667 @@
+// Lloyd k-means on sm_100a: nearest-centre assignment on the tensor core and
+// a deterministic centroid update.
+//
+// Assignment (peco/kernels/kmeans.cu:139-175, peco/clustering.py:66-73):
+//   label = argmin_c ||c||^2 - 2 x.c, lowest index on ties.
+// The tokens of a PECO call are bf16, so x is exact as a bf16 MMA operand;
+// each centroid is rounded once to bf16 and S = X C^T is accumulated in fp32
+// in TMEM (tcgen05.mma, M=128 tokens, N<=256 centroids per chunk).  Rounding
+// c to bf16 moves each distance by at most
+//   E = 2^-7.9 ||x|| max||c||   (+ a tiny fp32 term),
+// so the epilogue keeps every centroid whose approximate distance lies within
+// 2E of the best one and recomputes those candidates exactly in fp32 on the
+// CUDA cores.  The label therefore equals the fp32 argmin except where two
+// fp32 distances tie to rounding level.  fp32 inputs (the legacy entry point)
+// are split into bf16 hi + lo operands and accumulated by two MMAs.
+//
+// Update (peco/kernels/kmeans.cu:179-196, peco/clustering.py:74-80): tokens
+// are stably sorted by label (counting sort), then one warp per cluster sums
+// its tokens in ascending token order in fp32 -- the accumulation order of the
+// reference's CPU scatter_add -- and divides by the count; empty clusters keep
+// their previous centre.  No atomics: the result is deterministic and, for
+// identical labels, bit-identical to the reference's CPU centroids.
+#include "common.cuh"
+#include "../../include/peco_b200.h"
+#include "internal.h"
+
+namespace peco {
+namespace {
+
+constexpr int kTileM = 128;
+constexpr int kProdWarps = 4, kEpiWarps = 4;
+constexpr int kAssignThreads = 32 * (kProdWarps + 1 + kEpiWarps);
+constexpr int kMaxCand = 8;
+constexpr float kBoundScale = 0.0045f;  // > 2^-7.9 (bf16 centroid rounding + fp32 accumulation)
+
+struct AssignJob {
+  const void* x;            // token rows, bf16 or fp32, row length D
+  long long head_rows;      // rows between consecutive heads in x
+  int tokens;               // tokens per head
+  int clusters;             // centroids per head
+  const float* centers;     // [B, C, D]
+  const float* norms;       // [B, C] squared centroid norms
+  int32_t* labels;          // [B, tokens]
+};
+
+struct AssignJobs {
+  AssignJob job[2];
+};
+
+struct __align__(8) AssignBars {
+  uint64_t a_full[2], a_empty[2], b_full[2], b_empty[2], acc_full[2], acc_empty[2];
+  uint32_t tmem_base;
+  int abort_flag;
+  float cmax;
+};
+
+__host__ __device__ constexpr int round16(int v) { return (v + 15) & ~15; }
+
+struct AssignGeom {
+  int nc;        // centroids per chunk (multiple of 16, <= 256)
+  int nchunks;
+  int a_bytes;   // one A slot (hi [+ lo])
+  int b_bytes;   // one B slot
+  int nbslots;   // B ring: 1 when the single chunk stays resident, else 2 (1 if smem is short)
+  int naslots;   // A ring: 2 (1 if smem is short)
+  int tmem_cols;
+  int smem;      // dynamic smem bytes
+};
+
+__host__ __device__ inline AssignGeom assign_geom(int C, int D, bool xf32) {
+  AssignGeom g;
+  g.nc = round16(C < 256 ? C : 256);
+  g.nchunks = (C + g.nc - 1) / g.nc;
+  g.a_bytes = kTileM * D * 2 * (xf32 ? 2 : 1);
+  g.b_bytes = g.nc * D * 2;
+  g.nbslots = g.nchunks == 1 ? 1 : 2;
+  g.naslots = 2;
+  while (1024 + g.nbslots * g.b_bytes + g.naslots * g.a_bytes > 225 * 1024 && (g.nbslots > 1 || g.naslots > 1)) {
+    if (g.nbslots > 1) g.nbslots = 1;
+    else g.naslots = 1;
+  }
+  int cols = 2 * g.nc;
+  int p = 32;
+  while (p < cols) p <<= 1;
+  g.tmem_cols = p;
+  g.smem = 1024 + g.nbslots * g.b_bytes + g.naslots * g.a_bytes;
+  return g;
+}
+
+// swizzled 16-byte chunk store into a K-major panel tile (panel = 64 columns,
+// rows 128 bytes apart, ``panel_bytes`` between panels)
+__device__ __forceinline__ void store_row_chunk(unsigned char* tile, int row, int chunk, uint4 v, int panel_bytes) {
+  const int panel = chunk >> 3, c = chunk & 7;
+  *reinterpret_cast<uint4*>(tile + panel * panel_bytes + row * 128 + ((c ^ (row & 7)) << 4)) = v;
+}
+
+__device__ __forceinline__ uint4 load_row_chunk(const unsigned char* tile, int row, int chunk, int panel_bytes) {
+  const int panel = chunk >> 3, c = chunk & 7;
+  return *reinterpret_cast<const uint4*>(tile + panel * panel_bytes + row * 128 + ((c ^ (row & 7)) << 4));
+}
+
+template <int D, bool XF32>
+__global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const AssignJobs jobs, int tiles_per_cta,
+                                                                        unsigned* status) {
+  const AssignJob& J = jobs.job[blockIdx.z];
+  const int head = blockIdx.y;
+  const int C = J.clusters;
+  const int ntiles = (J.tokens + kTileM - 1) / kTileM;
+  const int t_begin = blockIdx.x * tiles_per_cta;
+  if (t_begin >= ntiles) return;
+  const int t_end = min(ntiles, t_begin + tiles_per_cta);
+  const int my_tiles = t_end - t_begin;
+  const AssignGeom G = assign_geom(C, D, XF32);
+
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* bslot[2] = {base, base + (G.nbslots > 1 ? G.b_bytes : 0)};
+  unsigned char* aslot0 = base + G.nbslots * G.b_bytes;
+  __shared__ AssignBars sb;
+  __shared__ float xnorm[2][kTileM];
+  volatile int* abort_flag = &sb.abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* cen = J.centers + static_cast<long long>(head) * C * D;
+  const float* norms = J.norms + static_cast<long long>(head) * C;
+  const int NA = G.naslots, NB = G.nbslots;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sb.a_full[i], 32 * kProdWarps);
+      mbar_init(&sb.a_empty[i], kEpiWarps);
+      mbar_init(&sb.b_full[i], 32 * kProdWarps);
+      mbar_init(&sb.b_empty[i], 1);
+      mbar_init(&sb.acc_full[i], 1);
+      mbar_init(&sb.acc_empty[i], kEpiWarps);
+    }
+    sb.abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == kProdWarps) {
+    tmem_alloc(&sb.tmem_base, G.tmem_cols);
+    tmem_relinquish();
+  }
+  // max centroid norm of this head (bound scale)
+  if (warp == 0) {
+    float m = 0.0f;
+    for (int c = lane; c < C; c += 32) m = fmaxf(m, norms[c]);
+    m = warp_max(m);
+    if (lane == 0) sb.cmax = sqrtf(m);
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sb.tmem_base;
+  const int a_panel = kTileM * 128;         // bytes per 64-column panel of an A tile
+  const int b_panel = G.nc * 128;
+
+  if (warp < kProdWarps) {
+    // ------------------------------------------------------------ producers
+    const int tid = threadIdx.x;  // 0..127
+    bool ok = true;
+    auto load_b = [&](int chunk, unsigned char* dst) {
+      // rows of this chunk: c = chunk*nc + j for j in [0, nc); thread handles j = tid, tid+128
+      for (int j = tid; j < G.nc; j += 32 * kProdWarps) {
+        const int c = chunk * G.nc + j;
+        const float* src = cen + static_cast<long long>(c) * D;
+#pragma unroll 4
+        for (int ch = 0; ch < D / 8; ++ch) {
+          uint4 v = make_uint4(0, 0, 0, 0);
+          if (c < C) {
+            const float4 a = reinterpret_cast<const float4*>(src)[2 * ch];
+            const float4 b = reinterpret_cast<const float4*>(src)[2 * ch + 1];
+            v.x = pack_bf16x2(a.x, a.y);
+            v.y = pack_bf16x2(a.z, a.w);
+            v.z = pack_bf16x2(b.x, b.y);
+            v.w = pack_bf16x2(b.z, b.w);
+          }
+          store_row_chunk(dst, j, ch, v, b_panel);
+        }
+      }
+      fence_async_smem();
+    };
+    if (G.nchunks == 1) {
+      load_b(0, bslot[0]);
+      mbar_arrive(&sb.b_full[0]);
+    }
+    for (int i = 0; i < my_tiles && ok; ++i) {
+      const int tile = t_begin + i;
+      const int s = i % NA, use = i / NA;
+      if (use > 0) ok = mbar_wait(&sb.a_empty[s], (use - 1) & 1, abort_flag, status);
+      if (!ok) break;
+      unsigned char* a_hi = aslot0 + s * G.a_bytes;
+      unsigned char* a_lo = a_hi + kTileM * D * 2;
+      const int row = tid;
+      const int tok = tile * kTileM + row;
+      float ss = 0.0f;
+      if (tok < J.tokens) {
+        const long long grow = static_cast<long long>(head) * J.head_rows + tok;
+        if (XF32) {
+          const float* src = static_cast<const float*>(J.x) + grow * D;
+#pragma unroll 4
+          for (int ch = 0; ch < D / 8; ++ch) {
+            const float4 a = reinterpret_cast<const float4*>(src)[2 * ch];
+            const float4 b = reinterpret_cast<const float4*>(src)[2 * ch + 1];
+            const float f[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+            uint4 hi, lo;
+            uint32_t* hw = reinterpret_cast<uint32_t*>(&hi);
+            uint32_t* lw = reinterpret_cast<uint32_t*>(&lo);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float h0 = __bfloat162float(__float2bfloat16_rn(f[2 * e]));
+              const float h1 = __bfloat162float(__float2bfloat16_rn(f[2 * e + 1]));
+              hw[e] = pack_bf16x2(h0, h1);
+              lw[e] = pack_bf16x2(f[2 * e] - h0, f[2 * e + 1] - h1);
+              ss = fmaf(f[2 * e], f[2 * e], ss);
+              ss = fmaf(f[2 * e + 1], f[2 * e + 1], ss);
+            }
+            store_row_chunk(a_hi, row, ch, hi, a_panel);
+            store_row_chunk(a_lo, row, ch, lo, a_panel);
+          }
+        } else {
+          const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(J.x) + grow * D;
+#pragma unroll 4
+          for (int ch = 0; ch < D / 8; ++ch) {
+            const uint4 v = reinterpret_cast<const uint4*>(src)[ch];
+            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = __bfloat1622float2(h[e]);
+              ss = fmaf(f.x, f.x, ss);
+              ss = fmaf(f.y, f.y, ss);
+            }
+            store_row_chunk(a_hi, row, ch, v, a_panel);
+          }
+        }
+      } else {
+        for (int ch = 0; ch < D / 8; ++ch) {
+          store_row_chunk(a_hi, row, ch, make_uint4(0, 0, 0, 0), a_panel);
+          if (XF32) store_row_chunk(a_lo, row, ch, make_uint4(0, 0, 0, 0), a_panel);
+        }
+      }
+      xnorm[s][row] = sqrtf(ss);
+      fence_async_smem();
+      mbar_arrive(&sb.a_full[s]);
+      if (G.nchunks > 1) {
+        for (int k = 0; k < G.nchunks && ok; ++k) {
+          const int g = i * G.nchunks + k;
+          const int bs = g % NB, bu = g / NB;
+          if (bu > 0) ok = mbar_wait(&sb.b_empty[bs], (bu - 1) & 1, abort_flag, status);
+          if (!ok) break;
+          load_b(k, bslot[bs]);
+          mbar_arrive(&sb.b_full[bs]);
+        }
+      }
+    }
+  } else if (warp == kProdWarps) {
+    // ------------------------------------------------------------------ MMA
+    if (lane == 0) {
+      const uint32_t idesc = instr_desc(128, G.nc, 1, false, false);
+      bool ok = true;
+      int last_g = -1;
+      if (G.nchunks == 1) ok = mbar_wait(&sb.b_full[0], 0, abort_flag, status);
+      for (int i = 0; i < my_tiles && ok; ++i) {
+        const int s = i % NA;
+        ok = mbar_wait(&sb.a_full[s], (i / NA) & 1, abort_flag, status);
+        if (!ok) break;
+        const uint32_t a_hi = smem_u32(aslot0 + s * G.a_bytes);
+        const uint32_t a_lo = a_hi + kTileM * D * 2;
+        for (int k = 0; k < G.nchunks && ok; ++k) {
+          const int g = i * G.nchunks + k;
+          const int as = g & 1, au = g >> 1;
+          if (au > 0) ok = mbar_wait(&sb.acc_empty[as], (au - 1) & 1, abort_flag, status);
+          int bs = 0;
+          if (ok && G.nchunks > 1) {
+            bs = g % NB;
+            ok = mbar_wait(&sb.b_full[bs], (g / NB) & 1, abort_flag, status);
+          }
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t b = smem_u32(bslot[bs]);
+          const uint32_t acc = tmem + as * G.nc;
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off_a = (kk >> 2) * a_panel + (kk & 3) * 32;
+            const uint32_t off_b = (kk >> 2) * b_panel + (kk & 3) * 32;
+            umma_ss(acc, smem_desc(a_hi + off_a, 16, 1024), smem_desc(b + off_b, 16, 1024), idesc, kk > 0 ? 1u : 0u);
+          }
+          if (XF32) {
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint32_t off_a = (kk >> 2) * a_panel + (kk & 3) * 32;
+              const uint32_t off_b = (kk >> 2) * b_panel + (kk & 3) * 32;
+              umma_ss(acc, smem_desc(a_lo + off_a, 16, 1024), smem_desc(b + off_b, 16, 1024), idesc, 1u);
+            }
+          }
+          umma_commit(&sb.acc_full[as]);
+          if (G.nchunks > 1) umma_commit(&sb.b_empty[bs]);
+          last_g = g;
+        }
+      }
+      if (last_g >= 0) mbar_wait(&sb.acc_full[last_g & 1], (last_g >> 1) & 1, abort_flag, status);
+    }
+  } else {
+    // ------------------------------------------------------------- epilogue
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const float cmax = sb.cmax;
+    bool ok = true;
+    for (int i = 0; i < my_tiles && ok; ++i) {
+      const int tile = t_begin + i;
+      const int s = i % NA;
+      ok = mbar_wait(&sb.a_full[s], (i / NA) & 1, abort_flag, status);
+      if (!ok) break;
+      const float xn = xnorm[s][r];
+      const float E = kBoundScale * xn * cmax + 1e-6f * (cmax * cmax + 2.0f * xn * cmax);
+      const float E2 = 2.0f * E;
+      float best = INFINITY;
+      float cd[kMaxCand];
+      int ci[kMaxCand];
+      int ncand = 0;
+      for (int k = 0; k < G.nchunks && ok; ++k) {
+        const int g = i * G.nchunks + k;
+        const int as = g & 1;
+        ok = mbar_wait(&sb.acc_full[as], (g >> 1) & 1, abort_flag, status);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t acc = tmem + as * G.nc + lane_off;
+        for (int c0 = 0; c0 < G.nc; c0 += 32) {
+          uint32_t v[32];
+          tmem_ld32(acc + c0, v);
+          tmem_ld_wait();
+          const int cb = k * G.nc + c0;
+          float d[32];
+          float mn = INFINITY;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int c = cb + j;
+            d[j] = (c < C) ? fmaf(-2.0f, __uint_as_float(v[j]), __ldg(norms + c)) : INFINITY;
+            mn = fminf(mn, d[j]);
+          }
+          best = fminf(best, mn);
+          const float thr = best + E2;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (d[j] <= thr) {
+#pragma unroll
+              for (int q = 0; q < kMaxCand; ++q)
+                if (q == ncand) {
+                  cd[q] = d[j];
+                  ci[q] = cb + j;
+                }
+              ++ncand;
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sb.acc_empty[as]);
+      }
+      if (!ok) break;
+      // exact fp32 recompute of the candidates
+      const int tok = tile * kTileM + r;
+      if (tok < J.tokens) {
+        const long long grow = static_cast<long long>(head) * J.head_rows + tok;
+        const unsigned char* a_hi = aslot0 + s * G.a_bytes;
+        auto exact = [&](int c) -> float {
+          const float* cr = cen + static_cast<long long>(c) * D;
+          float dot = 0.0f;
+          if (XF32) {
+            const float* xr = static_cast<const float*>(J.x) + grow * D;
+#pragma unroll 8
+            for (int e = 0; e < D; ++e) dot = fmaf(xr[e], cr[e], dot);
+          } else {
+#pragma unroll 2
+            for (int ch = 0; ch < D / 8; ++ch) {
+              const uint4 u = load_row_chunk(a_hi, r, ch, a_panel);
+              const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+              const float4 c0 = reinterpret_cast<const float4*>(cr)[2 * ch];
+              const float4 c1 = reinterpret_cast<const float4*>(cr)[2 * ch + 1];
+              const float cc[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 f = __bfloat1622float2(h[e]);
+                dot = fmaf(f.x, cc[2 * e], dot);
+                dot = fmaf(f.y, cc[2 * e + 1], dot);
+              }
+            }
+          }
+          return __fsub_rn(norms[c], 2.0f * dot);
+        };
+        int label = 0;
+        float bd = INFINITY;
+        const float thr = best + E2;
+        if (ncand <= kMaxCand) {
+#pragma unroll
+          for (int q = 0; q < kMaxCand; ++q) {
+            if (q < ncand && cd[q] <= thr) {
+              const float e = exact(ci[q]);
+              if (e < bd) {
+                bd = e;
+                label = ci[q];
+              }
+            }
+          }
+        } else {
+          for (int c = 0; c < C; ++c) {
+            const float e = exact(c);
+            if (e < bd) {
+              bd = e;
+              label = c;
+            }
+          }
+        }
+        J.labels[static_cast<long long>(head) * J.tokens + tok] = label;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sb.a_empty[s]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kProdWarps) {
+    tc_fence_after();
+    tmem_dealloc(tmem, G.tmem_cols);
+  }
+}
+
+// ||c||^2 per centroid (fp32, one warp per centroid); writes norms [rows].
+__global__ void center_norms_kernel(const float* __restrict__ centers, float* __restrict__ norms, long long rows,
+                                    int dims) {
+  const long long w = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= rows) return;
+  const float* c = centers + w * dims;
+  float s = 0.0f;
+  for (int d = lane; d < dims; d += 32) s = fmaf(c[d], c[d], s);
+  s = warp_sum(s);
+  if (lane == 0) norms[w] = s;
+}
+
+// Centroid update, one warp per cluster.  x rows of head b are
+// x + (b * head_rows + t) * D.  Also writes ||mean||^2 for the next assignment.
+struct UpdateJob {
+  const void* x;
+  long long head_rows;
+  int tokens;
+  int clusters;
+  const int32_t* perm;      // [B, tokens] stable sort by label
+  const int32_t* offsets;   // [B, C+1]
+  const float* previous;    // [B, C, D]
+  float* means;             // [B, C, D]
+  float* sums;              // optional [B, C, D]
+  float* norms;             // optional [B, C]
+};
+struct UpdateJobs {
+  UpdateJob job[2];
+};
+
+template <int D, typename T>
+__global__ void kmeans_update_kernel(const UpdateJobs jobs, int bh, unsigned* status) {
+  const UpdateJob& J = jobs.job[blockIdx.y];
+  const long long w = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= static_cast<long long>(bh) * J.clusters) return;
+  const int head = static_cast<int>(w / J.clusters);
+  const int c = static_cast<int>(w - static_cast<long long>(head) * J.clusters);
+  constexpr int E = D / 32;  // elements per lane
+  const int start = J.offsets[static_cast<long long>(head) * (J.clusters + 1) + c];
+  int end = J.offsets[static_cast<long long>(head) * (J.clusters + 1) + c + 1];
+  const int32_t* perm = J.perm + static_cast<long long>(head) * J.tokens;
+  const T* xb = static_cast<const T*>(J.x) + static_cast<long long>(head) * J.head_rows * D + lane * E;
+  float acc[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) acc[e] = 0.0f;
+  int i = start;
+  // four rows in flight, accumulated strictly in ascending token order
+  bool bad = start < 0 || end > J.tokens || start > end;
+  if (bad) end = start;
+  for (; i + 4 <= end; i += 4) {
+    float v[4][E];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      int t = perm[i + u];
+      if (t < 0 || t >= J.tokens) {
+        bad = true;
+        t = 0;
+      }
+      const T* row = xb + static_cast<long long>(t) * D;
+#pragma unroll
+      for (int e = 0; e < E; ++e) v[u][e] = to_f32<T>(row[e]);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int e = 0; e < E; ++e) acc[e] = __fadd_rn(acc[e], v[u][e]);
+  }
+  for (; i < end; ++i) {
+    int t = perm[i];
+    if (t < 0 || t >= J.tokens) {
+      bad = true;
+      t = 0;
+    }
+    const T* row = xb + static_cast<long long>(t) * D;
+#pragma unroll
+    for (int e = 0; e < E; ++e) acc[e] = __fadd_rn(acc[e], to_f32<T>(row[e]));
+  }
+  if (bad && lane == 0) record_status(status, kDevBadIndex);
+  const int n = end - start;
+  const long long o = (static_cast<long long>(head) * J.clusters + c) * D + lane * E;
+  float nsq = 0.0f;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const float m = n > 0 ? __fdiv_rn(acc[e], static_cast<float>(n)) : J.previous[o + e];
+    J.means[o + e] = m;
+    if (J.sums) J.sums[o + e] = acc[e];
+    nsq = fmaf(m, m, nsq);
+  }
+  if (J.norms) {
+    nsq = warp_sum(nsq);
+    if (lane == 0) J.norms[static_cast<long long>(head) * J.clusters + c] = nsq;
+  }
+}
+
+template <int D, bool XF32>
+int launch_assign_t(const AssignJobs& jobs, int njobs, int bh, cudaStream_t stream) {
+  int max_smem = 0, max_chunks = 0, max_tiles = 0;
+  for (int j = 0; j < njobs; ++j) {
+    const AssignGeom g = assign_geom(jobs.job[j].clusters, D, XF32);
+    max_smem = max(max_smem, g.smem);
+    max_chunks = max(max_chunks, g.nchunks);
+    max_tiles = max(max_tiles, (jobs.job[j].tokens + kTileM - 1) / kTileM);
+  }
+  if (max_smem > 227 * 1024) return kErrUnsupported;
+  // spread tiles so that ~2 waves of CTAs cover every (job, head)
+  long long ctas_wanted = 2LL * kNumSMs;
+  int per_head = static_cast<int>((ctas_wanted + static_cast<long long>(bh) * njobs - 1) / (static_cast<long long>(bh) * njobs));
+  per_head = max(1, min(per_head, max_tiles));
+  int tiles_per_cta = (max_tiles + per_head - 1) / per_head;
+  if (max_chunks == 1) tiles_per_cta = max(tiles_per_cta, 2);  // amortise the resident centroid load
+  const int grid_x = (max_tiles + tiles_per_cta - 1) / tiles_per_cta;
+  cudaError_t e = cudaFuncSetAttribute(kmeans_assign_kernel<D, XF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  dim3 grid(grid_x, bh, njobs);
+  kmeans_assign_kernel<D, XF32><<<grid, kAssignThreads, max_smem, stream>>>(jobs, tiles_per_cta, device_status_ptr());
+  return launch_status();
+}
+
+int launch_norms(const float* centers, float* norms, long long rows, int dims, cudaStream_t stream) {
+  const long long threads = rows * 32;
+  const int blocks = static_cast<int>((threads + 255) / 256);
+  center_norms_kernel<<<blocks, 256, 0, stream>>>(centers, norms, rows, dims);
+  return launch_status();
+}
+
+template <typename T>
+int launch_update_t(const UpdateJobs& jobs, int njobs, int bh, int dims, int max_clusters, cudaStream_t stream) {
+  const long long warps = static_cast<long long>(bh) * max_clusters;
+  dim3 grid(static_cast<unsigned>((warps * 32 + 255) / 256), njobs);
+  if (dims == 128) kmeans_update_kernel<128, T><<<grid, 256, 0, stream>>>(jobs, bh, device_status_ptr());
+  else if (dims == 64) kmeans_update_kernel<64, T><<<grid, 256, 0, stream>>>(jobs, bh, device_status_ptr());
+  else return kErrUnsupported;
+  return launch_status();
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// fused fixed-iteration k-means over bf16 tokens (one or two independent
+// problems per launch, e.g. the Q and K clusterings of one PECO call)
+// ---------------------------------------------------------------------------
+int kmeans_fit_bf16(int njobs, const KmeansProblem* probs, int bh, int dims, int iters, cudaStream_t stream) {
+  if (njobs < 1 || njobs > 2 || bh < 1 || iters < 1) return kErrInvalidValue;
+  if (dims != 64 && dims != 128) return kErrUnsupported;
+  int rc = 0;
+  int maxc = 0;
+  for (int j = 0; j < njobs; ++j) {
+    const KmeansProblem& p = probs[j];
+    if (p.clusters < 1 || p.tokens < 1 || p.clusters > p.tokens) return kErrInvalidValue;
+    maxc = max(maxc, p.clusters);
+    // norms of the initial centres
+    rc = launch_norms(p.centers_a, p.norms, static_cast<long long>(bh) * p.clusters, dims, stream);
+    if (rc) return rc;
+  }
+  for (int it = 0; it < iters; ++it) {
+    AssignJobs aj{};
+    UpdateJobs uj{};
+    for (int j = 0; j < njobs; ++j) {
+      const KmeansProblem& p = probs[j];
+      // ping-pong so that the last iteration writes centers_out
+      const bool even_left = ((iters - 1 - it) & 1) == 0;
+      const float* cur = (it == 0) ? p.centers_a : (even_left ? p.centers_b : p.centers_out);
+      float* nxt = even_left ? p.centers_out : p.centers_b;  // in-place is safe: each lane reads then writes
+      aj.job[j] = {p.x, p.head_rows, p.tokens, p.clusters, cur, p.norms, p.labels};
+      uj.job[j] = {p.x, p.head_rows, p.tokens, p.clusters, p.perm, p.offsets, cur, nxt, nullptr, p.norms};
+    }
+    rc = dims == 128 ? launch_assign_t<128, false>(aj, njobs, bh, stream) : launch_assign_t<64, false>(aj, njobs, bh, stream);
+    if (rc) return rc;
+    for (int j = 0; j < njobs; ++j) {
+      const KmeansProblem& p = probs[j];
+      rc = launch_stable_sort(p.labels, p.tokens, bh, p.tokens, p.clusters, p.perm, p.counts, p.offsets, stream);
+      if (rc) return rc;
+    }
+    rc = launch_update_t<__nv_bfloat16>(uj, njobs, bh, dims, maxc, stream);
+    if (rc) return rc;
+  }
+  return 0;
+}
+
+}  // namespace peco
+
+using namespace peco;
+
+// Drop-in for peco/kernels/kmeans.cu:139-175.  ``scratch`` is not needed by the
+// tensor-core path and is left untouched; ``center_norms`` receives ||c||^2.
+extern "C" int peco_assign_tokens_to_centers(const float* x, const float* centers, int32_t* labels, float* scratch,
+                                             float* center_norms, int batch, int tokens, int dims, int clusters,
+                                             int chunk_size, void* stream_ptr) {
+  (void)scratch;
+  (void)chunk_size;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  if (batch < 1 || tokens < 1 || clusters < 1 || dims < 1) return kErrInvalidValue;
+  if (dims != 64 && dims != 128) return kErrUnsupported;
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(centers)) & 15) return kErrInvalidValue;
+  int rc = launch_norms(centers, center_norms, static_cast<long long>(batch) * clusters, dims, stream);
+  if (rc) return rc;
+  AssignJobs jobs{};
+  jobs.job[0] = {x, tokens, tokens, clusters, centers, center_norms, labels};
+  return dims == 128 ? launch_assign_t<128, true>(jobs, 1, batch, stream) : launch_assign_t<64, true>(jobs, 1, batch, stream);
+}
+
+// Drop-in for peco/kernels/kmeans.cu:179-196: writes sums, counts and means
+// (empty clusters keep ``previous``).  The stable sort needs batch*tokens +
+// batch*(clusters+1) ints of scratch, taken from the stream-ordered pool.
+extern "C" int peco_recompute_cluster_centers(const float* x, const int32_t* labels, const float* previous,
+                                              float* sums, int32_t* counts, float* means, int batch, int tokens,
+                                              int dims, int clusters, void* stream_ptr) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  if (batch < 1 || tokens < 1 || clusters < 1 || dims < 1) return kErrInvalidValue;
+  if (dims != 64 && dims != 128) return kErrUnsupported;
+  const size_t n_perm = static_cast<size_t>(batch) * tokens, n_off = static_cast<size_t>(batch) * (clusters + 1);
+  void* scratch = nullptr;
+  cudaError_t e = cudaMallocAsync(&scratch, (n_perm + n_off) * sizeof(int32_t), stream);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  int32_t* perm = static_cast<int32_t*>(scratch);
+  int32_t* offsets = perm + n_perm;
+  int rc = launch_stable_sort(labels, tokens, batch, tokens, clusters, perm, counts, offsets, stream);
+  if (!rc) {
+    UpdateJobs uj{};
+    uj.job[0] = {x, tokens, tokens, clusters, perm, offsets, previous, means, sums, nullptr};
+    rc = launch_update_t<float>(uj, 1, batch, dims, clusters, stream);
+  }
+  cudaError_t f = cudaFreeAsync(scratch, stream);
+  if (!rc && f != cudaSuccess) rc = static_cast<int>(f);
+  return rc;
+}
+
+extern "C" int peco_kmeans_fit(const void* q_x, long long q_head_rows, int q_tokens, int q_clusters, int32_t* q_labels,
+                               const float* q_init, float* q_centers, float* q_work, float* q_norms, int32_t* q_counts,
+                               int32_t* q_offsets, int32_t* q_perm, const void* k_x, long long k_head_rows, int k_tokens,
+                               int k_clusters, int32_t* k_labels, const float* k_init, float* k_centers, float* k_work,
+                               float* k_norms, int32_t* k_counts, int32_t* k_offsets, int32_t* k_perm, int bh, int dims,
+                               int iters, void* stream) {
+  KmeansProblem p[2];
+  p[0] = {q_x, q_head_rows, q_tokens, q_clusters, q_init, q_work, q_centers, q_norms, q_labels, q_counts, q_offsets, q_perm};
+  p[1] = {k_x, k_head_rows, k_tokens, k_clusters, k_init, k_work, k_centers, k_norms, k_labels, k_counts, k_offsets, k_perm};
+  const int njobs = k_x ? 2 : 1;
+  return kmeans_fit_bf16(njobs, p, bh, dims, iters, static_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,534 @@
+// Token reorder, stable counting sort and Base-Offset PE quantization.
+//
+// Memory-bound passes (HBM roofline): every row is moved with 16-byte vector
+// accesses, one half-warp (D=128, bf16) per token row, and the fused
+// quantize+gather pass reads each input row once and writes each packed row
+// once.  Quantization arithmetic uses explicitly rounded IEEE intrinsics
+// (__fsub_rn/__fdiv_rn/__fmul_rn/__fadd_rn, rintf) so no multiply-add is ever
+// contracted; this reproduces the reference's fp32 torch evaluation bit for
+// bit (peco/quantization.py:111-118, 134-136).
+#include "common.cuh"
+#include "../../include/peco_b200.h"
+#include "internal.h"
+
+namespace peco {
+namespace {
+
+// ---------------------------------------------------------------------------
+// legacy reorder (peco/kernels/kmeans.cu:92-107, 200-217)
+// ---------------------------------------------------------------------------
+// Forward: out[bh, j] = in[bh, idx[bh, j]];  inverse: out[bh, idx[bh, j]] = in[bh, j].
+// One thread moves one 16-byte chunk; rows are row_chunks chunks long.
+template <bool INVERSE>
+__global__ void reorder_rows_vec(const uint4* __restrict__ in, const int32_t* __restrict__ idx, uint4* __restrict__ out,
+                                 int tokens, int row_chunks, long long total_chunks, unsigned* status) {
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total_chunks;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long row = i / row_chunks;
+    const int c = static_cast<int>(i - row * row_chunks);
+    const long long head = row / tokens;
+    const int t = idx[row];
+    if (t < 0 || t >= tokens) {
+      if (c == 0) record_status(status, kDevBadIndex);
+      continue;
+    }
+    const long long mapped = (head * tokens + t) * row_chunks + c;
+    if (INVERSE) out[mapped] = in[i];
+    else out[i] = in[mapped];
+  }
+}
+
+template <typename T, bool INVERSE>
+__global__ void reorder_rows_scalar(const T* __restrict__ in, const int32_t* __restrict__ idx, T* __restrict__ out,
+                                    int tokens, int dims, long long total, unsigned* status) {
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long row = i / dims;
+    const int d = static_cast<int>(i - row * dims);
+    const long long head = row / tokens;
+    const int t = idx[row];
+    if (t < 0 || t >= tokens) {
+      if (d == 0) record_status(status, kDevBadIndex);
+      continue;
+    }
+    const long long mapped = (head * tokens + t) * dims + d;
+    if (INVERSE) out[mapped] = in[i];
+    else out[i] = in[mapped];
+  }
+}
+
+inline int grid_for(long long n, int threads) {
+  long long b = (n + threads - 1) / threads;
+  const long long cap = static_cast<long long>(kNumSMs) * 16;
+  return static_cast<int>(b < 1 ? 1 : (b > cap ? cap : b));
+}
+
+// ---------------------------------------------------------------------------
+// stable counting sort of labels (the argsort of peco/clustering.py:105)
+// ---------------------------------------------------------------------------
+// One CTA per row (head).  Tokens are split into P contiguous partitions, one
+// warp per partition; per-partition histograms give every (partition, label)
+// a base offset in label-major order, and each warp then places its tokens in
+// ascending order.  The result equals a stable argsort: within a label, lower
+// token index first.  Optionally also emits counts [C] and offsets [C+1].
+constexpr int kSortThreads = 1024;
+
+__global__ void __launch_bounds__(kSortThreads) stable_sort_labels_kernel(
+    const int32_t* __restrict__ labels, long long label_stride, int tokens, int clusters, int parts,
+    int32_t* __restrict__ indices, int32_t* __restrict__ counts, int32_t* __restrict__ offsets,
+    unsigned* status) {
+  extern __shared__ int32_t sm[];
+  int32_t* hist = sm;                         // [parts][clusters]
+  int32_t* colsum = sm + parts * clusters;    // [clusters]
+  __shared__ int32_t warp_tot[32];
+  const int row = blockIdx.x;
+  const int32_t* lab = labels + row * label_stride;
+  int32_t* out_idx = indices + static_cast<long long>(row) * tokens;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const unsigned lt_mask = (1u << lane) - 1u;
+
+  for (int i = threadIdx.x; i < parts * clusters; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  const int plen = (tokens + parts - 1) / parts;
+  // phase 1: per-partition histograms (warp-aggregated, no atomics: one leader per label)
+  if (warp < parts) {
+    const int p0 = warp * plen, p1 = min(tokens, p0 + plen);
+    for (int base = p0; base < p1; base += 32) {
+      const int t = base + lane;
+      int l = (t < p1) ? lab[t] : -1;
+      if (l >= clusters || (t < p1 && l < 0)) {
+        record_status(status, kDevBadIndex);
+        l = -1;
+      }
+      const unsigned peers = __match_any_sync(0xffffffffu, l);
+      if (l >= 0 && (peers & lt_mask) == 0) hist[warp * clusters + l] += __popc(peers);
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+  // phase 2: column sums -> counts; exclusive scan over labels -> offsets
+  for (int c = threadIdx.x; c < clusters; c += blockDim.x) {
+    int s = 0;
+    for (int p = 0; p < parts; ++p) s += hist[p * clusters + c];
+    colsum[c] = s;
+  }
+  __syncthreads();
+  // block-wide exclusive scan of colsum (chunked: each thread owns a contiguous run)
+  const int per = (clusters + blockDim.x - 1) / blockDim.x;
+  const int c0 = threadIdx.x * per, c1 = min(clusters, c0 + per);
+  int local = 0;
+  for (int c = c0; c < c1; ++c) local += colsum[c];
+  int incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int v = warp_tot[lane];
+    int inc = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += u;
+    }
+    warp_tot[lane] = inc - v;  // exclusive warp offsets
+  }
+  __syncthreads();
+  int run = warp_tot[warp] + incl - local;  // exclusive prefix for c0
+  for (int c = c0; c < c1; ++c) {
+    const int n = colsum[c];
+    if (counts) counts[static_cast<long long>(row) * clusters + c] = n;
+    if (offsets) offsets[static_cast<long long>(row) * (clusters + 1) + c] = run;
+    int b = run;
+    for (int p = 0; p < parts; ++p) {  // hist becomes per-partition base offsets
+      const int h = hist[p * clusters + c];
+      hist[p * clusters + c] = b;
+      b += h;
+    }
+    run += n;
+  }
+  if (offsets && threadIdx.x == blockDim.x - 1) offsets[static_cast<long long>(row) * (clusters + 1) + clusters] = run;
+  __syncthreads();
+  // phase 3: stable placement
+  if (warp < parts) {
+    const int p0 = warp * plen, p1 = min(tokens, p0 + plen);
+    for (int base = p0; base < p1; base += 32) {
+      const int t = base + lane;
+      int l = (t < p1) ? lab[t] : -1;
+      if (l >= clusters || l < 0) l = -1;
+      const unsigned peers = __match_any_sync(0xffffffffu, l);
+      int pos = 0;
+      if (l >= 0) pos = hist[warp * clusters + l] + __popc(peers & lt_mask);
+      __syncwarp();
+      if (l >= 0) {
+        out_idx[pos] = t;
+        if ((peers & lt_mask) == 0) hist[warp * clusters + l] += __popc(peers);
+      }
+      __syncwarp();
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Base-Offset quantization of one token row (peco/quantization.py:96-136)
+// ---------------------------------------------------------------------------
+// A group of G lanes (G = D/8) holds one row, 8 consecutive elements per lane.
+template <int G>
+struct RowQuant {
+  // in: x[8], c[8] (fp32); out: xhat[8], code[8]; low/scale returned by ref.
+  __device__ __forceinline__ static void run(const float (&x)[8], const float (&c)[8], float levels,
+                                             float (&xhat)[8], float (&code)[8], float& low, float& scale) {
+    float r[8];
+    float lo = INFINITY, hi = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      r[i] = __fsub_rn(x[i], c[i]);
+      lo = fminf(lo, r[i]);
+      hi = fmaxf(hi, r[i]);
+    }
+#pragma unroll
+    for (int o = G / 2; o; o >>= 1) {
+      lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+      hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+    }
+    const float raw = __fdiv_rn(__fsub_rn(hi, lo), levels);
+    const float sc = raw > 0.0f ? raw : 1.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float q = rintf(__fdiv_rn(__fsub_rn(r[i], lo), sc));
+      q = fminf(fmaxf(q, 0.0f), levels);
+      code[i] = q;
+      xhat[i] = __fadd_rn(c[i], __fadd_rn(lo, __fmul_rn(sc, q)));
+    }
+    low = lo;
+    scale = sc;
+  }
+};
+
+template <typename T>
+struct Vec8;  // 8 elements of T
+template <>
+struct Vec8<__nv_bfloat16> {
+  __device__ __forceinline__ static void load(const __nv_bfloat16* p, float (&v)[8]) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(h[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  }
+  __device__ __forceinline__ static void store(__nv_bfloat16* p, const float (&v)[8]) {
+    uint4 u;
+    uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+    *reinterpret_cast<uint4*>(p) = u;
+  }
+};
+template <>
+struct Vec8<__half> {
+  __device__ __forceinline__ static void load(const __half* p, float (&v)[8]) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __half22float2(h[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  }
+  __device__ __forceinline__ static void store(__half* p, const float (&v)[8]) {
+    uint4 u;
+    uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[i] = pack_f16x2(v[2 * i], v[2 * i + 1]);
+    *reinterpret_cast<uint4*>(p) = u;
+  }
+};
+template <>
+struct Vec8<float> {
+  __device__ __forceinline__ static void load(const float* p, float (&v)[8]) {
+    const float4 a = reinterpret_cast<const float4*>(p)[0];
+    const float4 b = reinterpret_cast<const float4*>(p)[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+  __device__ __forceinline__ static void store(float* p, const float (&v)[8]) {
+    reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+  }
+};
+
+// Stand-alone Base-Offset pass over [BH, N, D]: mode 0 = fake quantize
+// (write x_hat), mode 1 = encode (codes, low, scale), mode 2 = decode.
+template <typename T, int D>
+__global__ void base_offset_kernel(int mode, const T* __restrict__ x, const int32_t* __restrict__ labels,
+                                   const float* __restrict__ centroids, T* __restrict__ out,
+                                   uint8_t* __restrict__ codes, float* __restrict__ low_out,
+                                   float* __restrict__ scale_out, int bh, int tokens, int clusters, int bits,
+                                   unsigned* status) {
+  constexpr int G = D / 8;
+  const float levels = static_cast<float>((1 << bits) - 1);
+  const long long rows = static_cast<long long>(bh) * tokens;
+  const int sub = threadIdx.x % G;
+  const long long first = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) / G;
+  const long long step = static_cast<long long>(gridDim.x) * blockDim.x / G;
+  for (long long row = first; row < rows; row += step) {
+    const long long head = row / tokens;
+    int lab = labels[row];
+    const bool bad = lab < 0 || lab >= clusters;
+    if (bad) {
+      if (sub == 0) record_status(status, kDevBadIndex);
+      lab = 0;
+    }
+    const float* cen = centroids + (head * clusters + lab) * D + sub * 8;
+    float c[8];
+    {
+      const float4 a = reinterpret_cast<const float4*>(cen)[0];
+      const float4 b = reinterpret_cast<const float4*>(cen)[1];
+      c[0] = a.x; c[1] = a.y; c[2] = a.z; c[3] = a.w;
+      c[4] = b.x; c[5] = b.y; c[6] = b.z; c[7] = b.w;
+    }
+    float xh[8], q[8];
+    if (mode == 2) {  // decode: x_hat = C[label] + (low + scale * code)
+      const float lo = low_out[row], sc = scale_out[row];
+      const uint2 cc = *reinterpret_cast<const uint2*>(codes + row * D + sub * 8);
+      const uint8_t* cb = reinterpret_cast<const uint8_t*>(&cc);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) xh[i] = __fadd_rn(c[i], __fadd_rn(lo, __fmul_rn(sc, static_cast<float>(cb[i]))));
+      if (!bad) Vec8<T>::store(out + row * D + sub * 8, xh);
+      continue;
+    }
+    float xv[8];
+    Vec8<T>::load(x + row * D + sub * 8, xv);
+    float lo, sc;
+    RowQuant<G>::run(xv, c, levels, xh, q, lo, sc);
+    if (bad) continue;
+    if (mode == 0) {
+      Vec8<T>::store(out + row * D + sub * 8, xh);
+    } else {
+      uint2 cc;
+      uint8_t* cb = reinterpret_cast<uint8_t*>(&cc);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) cb[i] = static_cast<uint8_t>(q[i]);
+      *reinterpret_cast<uint2*>(codes + row * D + sub * 8) = cc;
+      if (sub == 0) {
+        low_out[row] = lo;
+        scale_out[row] = sc;
+      }
+    }
+  }
+}
+
+// Fused pass of one PECO call: for each of Q, K, V and each packed row j of
+// a head, read source row perm[j] of the video tokens (x_hat for Q/K when
+// bits > 0, plain copy for V), write it to packed row j; text rows (j >= Nv)
+// are copied unchanged.  Q/K/V are [BH, S, D] with the video tokens first.
+struct GatherJob {
+  const __nv_bfloat16* src;
+  __nv_bfloat16* dst;
+  const int32_t* perm;       // [BH, Nv]
+  const int32_t* labels;     // [BH, Nv] or null (no quantization)
+  const float* centroids;    // [BH, C, D]
+  int clusters;
+};
+struct GatherJobs {
+  GatherJob job[3];
+};
+
+template <int D>
+__global__ void quant_gather_kernel(GatherJobs jobs, int bh, int seq, int video, int bits, unsigned* status) {
+  constexpr int G = D / 8;
+  const GatherJob& J = jobs.job[blockIdx.y];
+  const float levels = static_cast<float>((1 << bits) - 1);
+  const long long rows = static_cast<long long>(bh) * seq;
+  const int sub = threadIdx.x % G;
+  const long long first = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) / G;
+  const long long step = static_cast<long long>(gridDim.x) * blockDim.x / G;
+  for (long long row = first; row < rows; row += step) {
+    const long long head = row / seq;
+    const int j = static_cast<int>(row - head * seq);
+    __nv_bfloat16* dst = J.dst + row * D + sub * 8;
+    if (j >= video) {
+      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(J.src + row * D + sub * 8);
+      continue;
+    }
+    int t = J.perm[head * video + j];
+    if (t < 0 || t >= video) {
+      if (sub == 0) record_status(status, kDevBadIndex);
+      continue;
+    }
+    const __nv_bfloat16* src = J.src + (head * seq + t) * D + sub * 8;
+    if (!J.labels || bits == 0) {
+      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+      continue;
+    }
+    int lab = J.labels[head * video + t];
+    if (lab < 0 || lab >= J.clusters) {
+      if (sub == 0) record_status(status, kDevBadIndex);
+      continue;
+    }
+    const float* cen = J.centroids + (head * J.clusters + lab) * D + sub * 8;
+    float c[8], xv[8], xh[8], q[8];
+    const float4 a = reinterpret_cast<const float4*>(cen)[0];
+    const float4 b = reinterpret_cast<const float4*>(cen)[1];
+    c[0] = a.x; c[1] = a.y; c[2] = a.z; c[3] = a.w;
+    c[4] = b.x; c[5] = b.y; c[6] = b.z; c[7] = b.w;
+    Vec8<__nv_bfloat16>::load(src, xv);
+    float lo, sc;
+    RowQuant<G>::run(xv, c, levels, xh, q, lo, sc);
+    Vec8<__nv_bfloat16>::store(dst, xh);
+  }
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// host launchers
+// ---------------------------------------------------------------------------
+int launch_stable_sort(const int32_t* labels, long long label_stride, int rows, int tokens, int clusters,
+                       int32_t* indices, int32_t* counts, int32_t* offsets, cudaStream_t stream) {
+  if (rows < 1 || tokens < 1 || clusters < 1) return kErrInvalidValue;
+  int parts = 32;
+  while (parts > 1 && static_cast<long long>(parts) * clusters * 4 + clusters * 4 > 160 * 1024) parts >>= 1;
+  const size_t smem = (static_cast<size_t>(parts) * clusters + clusters) * sizeof(int32_t);
+  if (smem > 200 * 1024) return kErrUnsupported;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(stable_sort_labels_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
+  stable_sort_labels_kernel<<<rows, kSortThreads, smem, stream>>>(labels, label_stride, tokens, clusters, parts,
+                                                                  indices, counts, offsets, device_status_ptr());
+  return launch_status();
+}
+
+int launch_quant_gather(const void* q, const void* k, const void* v, void* qp, void* kp, void* vp,
+                        const int32_t* q_perm, const int32_t* k_perm, const int32_t* q_labels,
+                        const int32_t* k_labels, const float* q_cen, const float* k_cen, int cq, int ck, int bh,
+                        int seq, int video, int dims, int bits, cudaStream_t stream) {
+  GatherJobs jobs;
+  jobs.job[0] = {static_cast<const __nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(qp), q_perm,
+                 bits ? q_labels : nullptr, q_cen, cq};
+  jobs.job[1] = {static_cast<const __nv_bfloat16*>(k), static_cast<__nv_bfloat16*>(kp), k_perm,
+                 bits ? k_labels : nullptr, k_cen, ck};
+  jobs.job[2] = {static_cast<const __nv_bfloat16*>(v), static_cast<__nv_bfloat16*>(vp), k_perm, nullptr, nullptr, 0};
+  const long long rows = static_cast<long long>(bh) * seq;
+  const int threads = 256;
+  const int rows_per_block = threads / (dims / 8);
+  long long blocks = (rows + rows_per_block - 1) / rows_per_block;
+  const long long cap = static_cast<long long>(kNumSMs) * 8;
+  if (blocks > cap) blocks = cap;
+  dim3 grid(static_cast<unsigned>(blocks), 3);
+  if (dims == 128)
+    quant_gather_kernel<128><<<grid, threads, 0, stream>>>(jobs, bh, seq, video, bits, device_status_ptr());
+  else if (dims == 64)
+    quant_gather_kernel<64><<<grid, threads, 0, stream>>>(jobs, bh, seq, video, bits, device_status_ptr());
+  else
+    return kErrUnsupported;
+  return launch_status();
+}
+
+}  // namespace peco
+
+using namespace peco;
+
+extern "C" int peco_reorder_token_features(const void* input, const int32_t* indices, void* output,
+                                           int batch_heads, int tokens, int dims, int item_size, int inverse,
+                                           void* stream_ptr) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  if (batch_heads < 0 || tokens < 0 || dims < 0 || (item_size != 2 && item_size != 4)) return kErrInvalidValue;
+  const long long total = static_cast<long long>(batch_heads) * tokens * dims;
+  if (total == 0) return 0;
+  const long long row_bytes = static_cast<long long>(dims) * item_size;
+  const bool vec = (row_bytes % 16 == 0) && (reinterpret_cast<uintptr_t>(input) % 16 == 0) &&
+                   (reinterpret_cast<uintptr_t>(output) % 16 == 0);
+  unsigned* st = device_status_ptr();
+  if (vec) {
+    const int rc = static_cast<int>(row_bytes / 16);
+    const long long chunks = static_cast<long long>(batch_heads) * tokens * rc;
+    const int g = grid_for(chunks, 256);
+    if (inverse)
+      reorder_rows_vec<true><<<g, 256, 0, stream>>>(static_cast<const uint4*>(input), indices,
+                                                    static_cast<uint4*>(output), tokens, rc, chunks, st);
+    else
+      reorder_rows_vec<false><<<g, 256, 0, stream>>>(static_cast<const uint4*>(input), indices,
+                                                     static_cast<uint4*>(output), tokens, rc, chunks, st);
+  } else {
+    const int g = grid_for(total, 256);
+    if (item_size == 2) {
+      if (inverse)
+        reorder_rows_scalar<uint16_t, true><<<g, 256, 0, stream>>>(static_cast<const uint16_t*>(input), indices,
+                                                                  static_cast<uint16_t*>(output), tokens, dims,
+                                                                  total, st);
+      else
+        reorder_rows_scalar<uint16_t, false><<<g, 256, 0, stream>>>(static_cast<const uint16_t*>(input), indices,
+                                                                   static_cast<uint16_t*>(output), tokens, dims,
+                                                                   total, st);
+    } else {
+      if (inverse)
+        reorder_rows_scalar<uint32_t, true><<<g, 256, 0, stream>>>(static_cast<const uint32_t*>(input), indices,
+                                                                  static_cast<uint32_t*>(output), tokens, dims,
+                                                                  total, st);
+      else
+        reorder_rows_scalar<uint32_t, false><<<g, 256, 0, stream>>>(static_cast<const uint32_t*>(input), indices,
+                                                                   static_cast<uint32_t*>(output), tokens, dims,
+                                                                   total, st);
+    }
+  }
+  return launch_status();
+}
+
+extern "C" int peco_sort_labels(const int32_t* labels, int32_t* indices, int32_t* counts, int32_t* offsets,
+                                int rows, int tokens, int clusters, void* stream) {
+  return launch_stable_sort(labels, tokens, rows, tokens, clusters, indices, counts, offsets,
+                            static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int peco_base_offset(int mode, const void* x, const int32_t* labels, const float* centroids, void* out,
+                                uint8_t* codes, float* offset_min, float* scale, int bh, int tokens, int dims,
+                                int clusters, int bits, int dtype, void* stream_ptr) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  if (mode < 0 || mode > 2 || bh < 0 || tokens < 0 || clusters < 1 || (bits != 4 && bits != 8))
+    return kErrInvalidValue;
+  if (dims != 64 && dims != 128) return kErrUnsupported;
+  const long long rows = static_cast<long long>(bh) * tokens;
+  if (rows == 0) return 0;
+  const int threads = 256;
+  const int rpb = threads / (dims / 8);
+  long long blocks = (rows + rpb - 1) / rpb;
+  const long long cap = static_cast<long long>(kNumSMs) * 8;
+  if (blocks > cap) blocks = cap;
+  unsigned* st = device_status_ptr();
+#define PECO_BO_LAUNCH(T, DD)                                                                                \
+  base_offset_kernel<T, DD><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(                          \
+      mode, static_cast<const T*>(x), labels, centroids, static_cast<T*>(out), codes, offset_min, scale, bh, \
+      tokens, clusters, bits, st)
+  if (dtype == 0) {
+    if (dims == 128) PECO_BO_LAUNCH(__half, 128); else PECO_BO_LAUNCH(__half, 64);
+  } else if (dtype == 1) {
+    if (dims == 128) PECO_BO_LAUNCH(__nv_bfloat16, 128); else PECO_BO_LAUNCH(__nv_bfloat16, 64);
+  } else if (dtype == 2) {
+    if (dims == 128) PECO_BO_LAUNCH(float, 128); else PECO_BO_LAUNCH(float, 64);
+  } else {
+    return kErrInvalidValue;
+  }
+#undef PECO_BO_LAUNCH
+  return launch_status();
+}
+
+extern "C" int peco_quantize_gather(const void* q, const void* k, const void* v, void* q_packed, void* k_packed,
+                                    void* v_packed, const int32_t* q_indices, const int32_t* k_indices,
+                                    const int32_t* q_labels, const int32_t* k_labels, const float* q_centroids,
+                                    const float* k_centroids, int q_clusters, int k_clusters, int bh, int seq,
+                                    int video, int dims, int bits, void* stream) {
+  if (bh < 1 || seq < 1 || video < 0 || video > seq || (bits != 0 && bits != 4 && bits != 8)) return kErrInvalidValue;
+  return launch_quant_gather(q, k, v, q_packed, k_packed, v_packed, q_indices, k_indices, q_labels, k_labels,
+                             q_centroids, k_centroids, q_clusters, k_clusters, bh, seq, video, dims, bits,
+                             static_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,184 @@
+"""GPU parity of the k-means kernels (tcgen05 assignment, deterministic update).
+
+Tolerance: labels bit-exact except at fp32 distance ties -- every single-step
+mismatch must be a tie (distance gap below 1e-5 relative in float64), and a
+full fit may differ on at most 0.1% of tokens.  Given identical labels the
+centroids are bit-identical to the reference's CPU update (same fp32 order).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import peco_oracle as O
+from peco_b200 import synthetic
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+@pytest.fixture(autouse=True)
+def _clean_status():
+    from peco_b200 import _native
+    _native.device_status(clear=True)
+    yield
+    torch.cuda.synchronize()
+    assert _native.device_status(clear=True) == 0
+
+
+def assert_labels_tie_exact(x, centers, got, ref):
+    """Mismatches allowed only where the reference's best two distances tie."""
+    diff = got != ref
+    if not diff.any():
+        return
+    xd, cd = x.double(), centers.double()
+    dist = cd.square().sum(-1).unsqueeze(1) - 2 * torch.bmm(xd, cd.transpose(1, 2))
+    dg = dist.gather(-1, got.long().unsqueeze(-1)).squeeze(-1)
+    dr = dist.gather(-1, ref.long().unsqueeze(-1)).squeeze(-1)
+    scale = dist.abs().amax(-1) + 1.0
+    gap = (dg - dr).abs() / scale
+    assert (gap[diff] < 1e-5).all(), f"{int(diff.sum())} label mismatches, max rel gap {gap[diff].max():.3g}"
+
+
+def video(x, nv):
+    b, h, s, d = x.shape
+    return x[:, :, :nv].reshape(b * h, nv, d)
+
+
+def test_assign_fp32_matches_reference_first_step(golden):
+    from peco_b200 import clustering_cuda
+    w = synthetic.workload("cpu-plumbing")
+    gd = golden("cpu_plumbing")
+    q, _, _ = synthetic.make_inputs(w, seed=0)
+    x = video(q, w.video_tokens).float().contiguous()
+    c0 = torch.from_numpy(gd["q_init"])
+    labels = torch.empty((2, w.video_tokens), dtype=torch.int32, device=DEV)
+    norms = torch.empty((2, 32), device=DEV)
+    scratch = torch.empty((1024, 32), device=DEV)
+    clustering_cuda.assign_tokens_to_centers(x.to(DEV), c0.to(DEV), labels, scratch, norms, 1024)
+    ref = torch.from_numpy(gd["q_labels_iter1"])
+    assert_labels_tie_exact(x, c0, labels.cpu(), ref)
+    torch.testing.assert_close(norms.cpu(), c0.square().sum(-1), rtol=1e-6, atol=1e-5)
+
+
+def test_recompute_bit_exact_given_labels(golden):
+    from peco_b200 import clustering_cuda
+    w = synthetic.workload("cpu-plumbing")
+    gd = golden("cpu_plumbing")
+    _, k, _ = synthetic.make_inputs(w, seed=0)
+    x = video(k, w.video_tokens).float().contiguous()
+    lab = torch.from_numpy(gd["k_labels"])
+    prev = torch.from_numpy(gd["k_init"])
+    means, counts, sums = O.update_centers(x, lab, prev)
+    dm, ds = torch.empty_like(prev, device=DEV), torch.empty_like(prev, device=DEV)
+    dc = torch.empty((2, 64), dtype=torch.int32, device=DEV)
+    clustering_cuda.recompute_cluster_centers(x.to(DEV), lab.to(DEV), prev.to(DEV), ds, dc, dm)
+    assert torch.equal(dc.cpu(), counts)
+    assert torch.equal(ds.cpu(), sums)
+    assert torch.equal(dm.cpu(), means)
+
+
+@pytest.mark.parametrize("tag", ["q", "k"])
+def test_fit_fp32_path_matches_reference(golden, tag):
+    from peco_b200 import clustering
+    w = synthetic.workload("cpu-plumbing")
+    gd = golden("cpu_plumbing")
+    q, k, _ = synthetic.make_inputs(w, seed=0)
+    x = video(q if tag == "q" else k, w.video_tokens).float().contiguous()
+    c = w.q_clusters if tag == "q" else w.k_clusters
+    lab, cen, cnt, it = clustering.fit_token_clusters(x.to(DEV), c, max_iters=w.iters, tol=0,
+                                                      init_centroids=torch.from_numpy(gd[f"{tag}_init"]).to(DEV))
+    assert it == w.iters
+    ref_lab = torch.from_numpy(gd[f"{tag}_labels"])
+    mism = (lab.cpu() != ref_lab).float().mean().item()
+    assert mism <= 1e-3
+    if mism == 0:
+        assert torch.equal(cnt.cpu(), torch.from_numpy(gd[f"{tag}_counts"]))
+        assert torch.equal(cen.cpu(), torch.from_numpy(gd[f"{tag}_centroids"]))
+
+
+@pytest.mark.parametrize("tag", ["q", "k"])
+def test_fused_bf16_fit_matches_reference(golden, tag):
+    from peco_b200 import clustering
+    gd = golden("small_bf16")
+    raw = torch.from_numpy(gd["inputs"]).view(torch.bfloat16)
+    x = video(raw[0:1] if tag == "q" else raw[1:2], 432).contiguous()
+    c = 16 if tag == "q" else 32
+    lab, cen, cnt, _ = clustering.fit_token_clusters(x.to(DEV), c, max_iters=5, tol=0,
+                                                     init_centroids=torch.from_numpy(gd[f"{tag}_init"]).to(DEV))
+    assert torch.equal(lab.cpu(), torch.from_numpy(gd[f"{tag}_labels"]))
+    assert torch.equal(cnt.cpu(), torch.from_numpy(gd[f"{tag}_counts"]))
+    assert torch.equal(cen.cpu(), torch.from_numpy(gd[f"{tag}_centroids"]))
+
+
+def test_fused_pair_on_sequence_prefix(golden):
+    """Q and K fitted together straight from the video prefix of [1,H,S,D]."""
+    from peco_b200 import clustering
+    gd = golden("small_bf16")
+    raw = torch.from_numpy(gd["inputs"]).view(torch.bfloat16)
+    q, k = raw[0:1].contiguous().to(DEV), raw[1:2].contiguous().to(DEV)
+    s = q.shape[2]
+    qb, kb = clustering.kmeans_fit_pair(q, s, 432, torch.from_numpy(gd["q_init"]).to(DEV), k, s, 432,
+                                        torch.from_numpy(gd["k_init"]).to(DEV), 2, 128, 5)
+    assert torch.equal(qb.labels.cpu(), torch.from_numpy(gd["q_labels"]))
+    assert torch.equal(kb.labels.cpu(), torch.from_numpy(gd["k_labels"]))
+    assert torch.equal(qb.centers.cpu(), torch.from_numpy(gd["q_centroids"]))
+    assert torch.equal(kb.centers.cpu(), torch.from_numpy(gd["k_centroids"]))
+    assert torch.equal(qb.perm.cpu(), torch.from_numpy(gd["q_indices"]))
+    assert torch.equal(kb.perm.cpu(), torch.from_numpy(gd["k_indices"]))
+    off = qb.offsets.cpu()
+    assert torch.equal(off[:, 1:] - off[:, :-1], qb.counts.cpu())
+
+
+def test_edge_ties_and_empty_clusters(golden):
+    from peco_b200 import clustering
+    e = golden("edge")
+    x = torch.from_numpy(e["x"])
+    init = torch.from_numpy(e["init"])
+    for xx in (x.to(torch.bfloat16), x):  # fused bf16 path and fp32 drop-in path
+        lab, cen, cnt, _ = clustering.fit_token_clusters(xx.to(DEV), 10, max_iters=3, tol=0,
+                                                         init_centroids=init.to(DEV))
+        assert torch.equal(lab.cpu(), torch.from_numpy(e["labels"]))
+        assert torch.equal(cnt.cpu(), torch.from_numpy(e["counts"]))
+        assert torch.equal(cen.cpu(), torch.from_numpy(e["centroids"]))
+
+
+@pytest.mark.parametrize("clusters,dtype", [(500, torch.bfloat16), (500, torch.float32), (300, torch.bfloat16),
+                                            (100, torch.bfloat16)])
+def test_chunked_centroid_counts(clusters, dtype):
+    """More than 256 centroids (several N chunks) and non-multiple-of-16 counts."""
+    from peco_b200 import clustering
+    w = synthetic.workload("hv480", heads=2, grid=(2, 30, 45))
+    q, _, _ = synthetic.make_inputs(w, seed=3)
+    x = video(q, w.video_tokens).to(dtype).contiguous()
+    init = synthetic.init_centroids(x, clusters, "strided")
+    lab, cen, cnt, _ = clustering.fit_token_clusters(x.to(DEV), clusters, max_iters=2, tol=0,
+                                                     init_centroids=init.to(DEV))
+    rl, rc, rn = O.fit_token_clusters(x.float(), clusters, 2, init)
+    assert (lab.cpu() != rl).float().mean().item() <= 1e-3
+    # one isolated step from the same centres is tie-exact
+    from peco_b200 import clustering_cuda
+    one = torch.empty_like(lab)
+    clustering_cuda.assign_tokens_to_centers(x.float().to(DEV), init.to(DEV), one,
+                                             torch.empty((1, 1), device=DEV),
+                                             torch.empty((2, clusters), device=DEV), 1024)
+    assert_labels_tie_exact(x.float(), init, one.cpu(), O.assign_labels(x.float(), init))
+
+
+def test_headline_shape_subset():
+    """4 heads of the HV-480 workload, 5 iterations of Q (128) and K (256)."""
+    from peco_b200 import clustering
+    w = synthetic.workload("hv480")
+    q, k, _ = synthetic.make_inputs(w, seed=0, heads=4)
+    nv = w.video_tokens
+    for x, c in ((q, w.q_clusters), (k, w.k_clusters)):
+        xv = video(x, nv).contiguous()
+        init = synthetic.init_centroids(xv, c, w.init)
+        lab, cen, cnt, _ = clustering.fit_token_clusters(xv.to(DEV), c, max_iters=w.iters, tol=0,
+                                                         init_centroids=init.to(DEV))
+        rl, rc, rn = O.fit_token_clusters(xv, c, w.iters, init)
+        mism = (lab.cpu() != rl).float().mean().item()
+        assert mism <= 1e-3, mism
+        if mism == 0:
+            assert torch.equal(cen.cpu(), rc)
