@@ -37,7 +37,26 @@ constexpr int kRing = 4;       // mask ring depth
 constexpr int kThreads = 192;  // 6 warps
 constexpr uint32_t kTmemCols = 256;
 
+#ifdef PECO_ATTN_TRACE
+// Debug builds record per-CTA progress: trace[cta*8 + role] = stage code.
+#define ATTN_TRACE(slot, value)                                                                   \
+  do {                                                                                            \
+    if (args.trace) {                                                                             \
+      volatile unsigned* t_ = args.trace + (static_cast<long long>(blockIdx.y) * gridDim.x + blockIdx.x) * 8; \
+      t_[slot] = (value);                                                                         \
+      __threadfence_system();                                                                     \
+    }                                                                                             \
+  } while (0)
+#else
+#define ATTN_TRACE(slot, value) \
+  do {                          \
+  } while (0)
+#endif
+
 struct AttnArgs {
+#ifdef PECO_ATTN_TRACE
+  unsigned* trace;
+#endif
   const uint8_t* map;      // [BH, GQ, GK]
   const int* ws;           // planner output, ws_stride ints per head
   void* out;               // [BH, SO, D]
@@ -207,6 +226,7 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_tc(const __grid_
     sh.abort_flag = 0;
     fence_barrier_init();
   }
+  if (threadIdx.x == 0) ATTN_TRACE(0, 1);
   if (warp == 1) {
     tmem_alloc(&sh.tmem_base, kTmemCols);
     tmem_relinquish();
@@ -214,6 +234,7 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_tc(const __grid_
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sh.tmem_base;
+  if (threadIdx.x == 0) ATTN_TRACE(0, 2);
   const uint32_t tmem_s = tmem;          // S: columns [0,128); P aliases [0,64)
   const uint32_t tmem_o = tmem + 128;    // O: columns [128, 128+D)
 
@@ -245,7 +266,7 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_tc(const __grid_
       }
       const int slot = tile % kRing;
       const uint32_t ph = (tile / kRing) & 1;
-      if (ok && tile >= kRing) ok = mbar_wait(&sh.mask_empty[slot], ph ^ 1, abort_flag, args.status);
+      if (ok && tile >= kRing) ok = mbar_wait_warp(&sh.mask_empty[slot], ph ^ 1, abort_flag, args.status);
       unsigned vm = 0;
       // mask words: bit j of word i -> key row 32 i + j valid
       {
@@ -269,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_tc(const __grid_
       __syncwarp();
       if (lane == 0 && ok) mbar_arrive(&sh.mask_full[slot]);
       // K boxes
-      if (ok && tile > 0) ok = mbar_wait(&sh.k_empty, (tile - 1) & 1, abort_flag, args.status);
+      if (ok && tile > 0) ok = mbar_wait_warp(&sh.k_empty, (tile - 1) & 1, abort_flag, args.status);
       if (lane == 0 && ok) mbar_arrive_expect_tx(&sh.k_full, L::kTileBytes);
       __syncwarp();
       if (ok && lane < kBoxes) {
@@ -278,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_tc(const __grid_
           tma_load_2d(k_tile + lane * L::kBoxBytes + p * 1024, &tmap_k, 64 * p, box_row, &sh.k_full);
       }
       // V boxes (the V tile is free once the previous P.V finished)
-      if (ok && tile > 0) ok = mbar_wait(&sh.v_empty, (tile - 1) & 1, abort_flag, args.status);
+      if (ok && tile > 0) ok = mbar_wait_warp(&sh.v_empty, (tile - 1) & 1, abort_flag, args.status);
       if (lane == 0 && ok) mbar_arrive_expect_tx(&sh.v_full, L::kTileBytes);
       __syncwarp();
       if (ok && lane < kBoxes) {
@@ -289,6 +310,7 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_tc(const __grid_
       ++tile;
       nbox = 0;
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if (lane == 0) ATTN_TRACE(1, 0x100u + tile);
     };
     auto add_box = [&](int row, int valid) {
       if (nbox == kBoxes) emit_tile(false);
@@ -342,10 +364,11 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_tc(const __grid_
       }
     }
     // drain: wait for the loads this warp issued before the CTA exits
-    if (tile > 0 && lane == 0) {
-      mbar_wait(&sh.k_full, (tile - 1) & 1, abort_flag, args.status);
-      mbar_wait(&sh.v_full, (tile - 1) & 1, abort_flag, args.status);
+    if (tile > 0) {
+      mbar_wait_warp(&sh.k_full, (tile - 1) & 1, abort_flag, args.status);
+      mbar_wait_warp(&sh.v_full, (tile - 1) & 1, abort_flag, args.status);
     }
+    __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA
     if (lane == 0) {
@@ -374,6 +397,7 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_tc(const __grid_
         }
         umma_commit(&sh.s_full);
         umma_commit(&sh.k_empty);
+        ATTN_TRACE(2, 0x100u + t);
         ok = mbar_wait(&sh.p_full, t & 1, abort_flag, args.status);
         if (ok) ok = mbar_wait(&sh.v_full, t & 1, abort_flag, args.status);
         if (!ok) break;
@@ -385,12 +409,14 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_tc(const __grid_
         }
         umma_commit(&sh.pv_done);
         umma_commit(&sh.v_empty);
+        ATTN_TRACE(2, 0x200u + t);
         ++issued;
         if (fl & 1u) break;
       }
       // drain our MMAs before TMEM is released
       if (issued > 0) mbar_wait(&sh.pv_done, (issued - 1) & 1, abort_flag, args.status);
     }
+    __syncwarp();
   } else {
     // -------------------------------------------------------------- softmax
     const int quarter = warp & 3;                  // TMEM lane quarter of this warp
@@ -401,7 +427,7 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_tc(const __grid_
     int t = 0;
     for (;; ++t) {
       const int slot = t % kRing;
-      ok = mbar_wait(&sh.mask_full[slot], (t / kRing) & 1, abort_flag, args.status);
+      ok = mbar_wait_warp(&sh.mask_full[slot], (t / kRing) & 1, abort_flag, args.status);
       if (!ok) break;
       const uint32_t fl = sh.flags[slot];
       const uint32_t mw0 = sh.mask[slot][0], mw1 = sh.mask[slot][1], mw2 = sh.mask[slot][2], mw3 = sh.mask[slot][3];
@@ -411,15 +437,16 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_tc(const __grid_
         empty = true;
         break;
       }
-      ok = mbar_wait(&sh.s_full, t & 1, abort_flag, args.status);
+      if (lane == 0) ATTN_TRACE(3 + quarter, 0x100u + t);
+      ok = mbar_wait_warp(&sh.s_full, t & 1, abort_flag, args.status);
       if (!ok) break;
       tc_fence_after();
+      if (lane == 0) ATTN_TRACE(3 + quarter, 0x200u + t);
       float s[kBN];
 #pragma unroll
       for (int c = 0; c < kBN / 32; ++c) {
         uint32_t v[32];
-        tmem_ld32(tmem_s + lane_off + c * 32, v);
-        tmem_ld_wait();
+        tmem_ld32_sync(tmem_s + lane_off + c * 32, v);
 #pragma unroll
         for (int j = 0; j < 32; ++j) s[c * 32 + j] = __uint_as_float(v[j]);
       }
@@ -431,29 +458,29 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_tc(const __grid_
         s[j] = valid ? s[j] * args.scale_log2 : -INFINITY;
         mx = fmaxf(mx, s[j]);
       }
-      if (mx > m + 8.0f || (m == -INFINITY && mx > -INFINITY)) {
-        // grow the running max; rescale O (previous P.V already complete:
-        // this tile's QK^T was issued only after it finished)
-        if (m != -INFINITY) {
-          const float f = exp2f(m - mx);
-          l *= f;
+      // grow the running max lazily (only by > 8 in log2 units); rescaling O
+      // is warp-collective because tcgen05.ld/st are .sync.aligned.  The
+      // previous P.V is complete: this tile's QK^T was issued after it.
+      const bool grow = (mx > m + 8.0f) || (m == -INFINITY && mx > -INFINITY);
+      const bool rescale_me = grow && m != -INFINITY;
+      if (__any_sync(0xffffffffu, rescale_me)) {
+        const float f = rescale_me ? exp2f(m - mx) : 1.0f;
+        l *= f;
 #pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t v[32];
-            tmem_ld32(tmem_o + lane_off + c * 32, v);
-            tmem_ld_wait();
-            uint32_t lo[16], hi[16];
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32_sync(tmem_o + lane_off + c * 32, v);
+          uint32_t lo[16], hi[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              lo[j] = __float_as_uint(__uint_as_float(v[j]) * f);
-              hi[j] = __float_as_uint(__uint_as_float(v[16 + j]) * f);
-            }
-            tmem_st16(tmem_o + lane_off + c * 32, lo);
-            tmem_st16(tmem_o + lane_off + c * 32 + 16, hi);
+          for (int j = 0; j < 16; ++j) {
+            lo[j] = __float_as_uint(__uint_as_float(v[j]) * f);
+            hi[j] = __float_as_uint(__uint_as_float(v[16 + j]) * f);
           }
+          tmem_st16(tmem_o + lane_off + c * 32, lo);
+          tmem_st16(tmem_o + lane_off + c * 32 + 16, hi);
         }
-        m = mx;
       }
+      if (grow) m = mx;
       const float mref = (m == -INFINITY) ? 0.0f : m;
       float sum = 0.0f;
       uint32_t packed[kBN / 2];
@@ -475,31 +502,33 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_tc(const __grid_
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
+      if (lane == 0) ATTN_TRACE(3 + quarter, 0x300u + t);
       if (lane == 0) mbar_arrive(&sh.p_full);
       if (fl & 1u) break;
     }
     // epilogue
     const bool have_o = ok && !empty;
-    if (have_o) ok = mbar_wait(&sh.pv_done, t & 1, abort_flag, args.status);
+    if (have_o) ok = mbar_wait_warp(&sh.pv_done, t & 1, abort_flag, args.status);
     tc_fence_after();
+    if (lane == 0) ATTN_TRACE(3 + quarter, 0x400u + (ok ? 1u : 0u));
+    // TMEM reads are warp-collective; only the stores depend on the row
+    using T = typename std::conditional<AB == 1, __nv_bfloat16, __half>::type;
+    T* dst = nullptr;
     if (r < q_count && (ok || empty)) {
       const int prow = q_start + r;
       long long orow = prow;
       if (args.perm && prow < args.video) orow = args.perm[static_cast<long long>(head) * args.video + prow];
-      using T = typename std::conditional<AB == 1, __nv_bfloat16, __half>::type;
-      T* dst = static_cast<T*>(args.out) + (static_cast<long long>(head) * args.out_rows + orow) * D;
-      if (orow < 0 || orow >= args.out_rows) {
-        record_status(args.status, kDevBadIndex);
-      } else if (!have_o || !(l > 0.0f)) {
+      if (orow < 0 || orow >= args.out_rows) record_status(args.status, kDevBadIndex);
+      else dst = static_cast<T*>(args.out) + (static_cast<long long>(head) * args.out_rows + orow) * D;
+    }
+    __syncwarp();
+    if (have_o && ok) {
+      const float inv = l > 0.0f ? 1.0f / l : 0.0f;
 #pragma unroll
-        for (int c = 0; c < D / 8; ++c) reinterpret_cast<uint4*>(dst)[c] = make_uint4(0, 0, 0, 0);
-      } else {
-        const float inv = 1.0f / l;
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t v[32];
-          tmem_ld32(tmem_o + lane_off + c * 32, v);
-          tmem_ld_wait();
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32_sync(tmem_o + lane_off + c * 32, v);
+        if (dst) {
 #pragma unroll
           for (int j = 0; j < 32; j += 8) {
             uint4 pk;
@@ -513,17 +542,25 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_tc(const __grid_
           }
         }
       }
-    } else if (r < q_count && !ok) {
-      // aborted: leave the row as is, the status word reports the failure
+    } else if (dst && empty) {
+#pragma unroll
+      for (int c = 0; c < D / 8; ++c) reinterpret_cast<uint4*>(dst)[c] = make_uint4(0, 0, 0, 0);
     }
+    __syncwarp();
   }
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) ATTN_TRACE(0, 3);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
+  if (threadIdx.x == 32) ATTN_TRACE(0, 4);
 }
+
+#ifdef PECO_ATTN_TRACE
+unsigned* g_attn_trace = nullptr;
+#endif
 
 bool make_rows_map(CUtensorMap* m, const void* base, long long rows, int dims, int box_rows, int dtype) {
   const uint64_t gdims[2] = {static_cast<uint64_t>(dims), static_cast<uint64_t>(rows)};
@@ -572,6 +609,9 @@ int launch_sparse_attention(const void* q, const void* k, const void* v, const u
   int rc = launch_status();
   if (rc) return rc;
   AttnArgs a;
+#ifdef PECO_ATTN_TRACE
+  a.trace = g_attn_trace;
+#endif
   a.map = map;
   a.ws = ws;
   a.out = out;

@@ -37,8 +37,12 @@ enum DeviceStatusBits : unsigned {
 };
 
 // A wait longer than this is treated as lost: ~1 s, far above any legitimate
-// TMA or MMA latency.
-constexpr unsigned long long kWaitTimeoutNs = 1000000000ull;
+// TMA or MMA latency.  A spin-count bound backs it up.
+#ifndef PECO_WAIT_TIMEOUT_NS
+#define PECO_WAIT_TIMEOUT_NS 1000000000ull
+#endif
+constexpr unsigned long long kWaitTimeoutNs = PECO_WAIT_TIMEOUT_NS;
+constexpr uint32_t kWaitMaxSpins = 1u << 27;
 
 __device__ __forceinline__ void record_status(unsigned* status, unsigned bits) {
   if (status) atomicOr(status, bits);
@@ -106,13 +110,26 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 63u) == 0) {
       if (*abort_flag) return false;
-      if (globaltimer() - t0 > kWaitTimeoutNs) {
+      if (globaltimer() - t0 > kWaitTimeoutNs || it > kWaitMaxSpins) {
         *abort_flag = 1;
         record_status(status, kDevTimeout);
         return false;
       }
     }
   }
+}
+
+// Warp-wide bounded wait: lane 0 polls, the result is broadcast and the warp
+// reconverges (__syncwarp also orders the memory the producer published), so
+// .sync.aligned instructions that follow (tcgen05.ld/st, barriers) always see
+// a converged warp.  Every lane of the warp must call it.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                               unsigned* status) {
+  int ok = 1;
+  if (lane_id() == 0) ok = mbar_wait(bar, parity, abort_flag, status) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  return ok != 0;
 }
 
 // ---- TMA (tensor maps are __grid_constant__ kernel parameters) --------------
@@ -195,6 +212,22 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 }
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// TMEM load followed by its wait in one statement, so no use of the
+// destination registers can be scheduled before the data has arrived.
+__device__ __forceinline__ void tmem_ld32_sync(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
 
 // Warp-collective TMEM store of 16 consecutive 32-bit columns per lane.
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {

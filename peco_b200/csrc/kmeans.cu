@@ -185,7 +185,7 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
     for (int i = 0; i < my_tiles && ok; ++i) {
       const int tile = t_begin + i;
       const int s = i % NA, use = i / NA;
-      if (use > 0) ok = mbar_wait(&sb.a_empty[s], (use - 1) & 1, abort_flag, status);
+      if (use > 0) ok = mbar_wait_warp(&sb.a_empty[s], (use - 1) & 1, abort_flag, status);
       if (!ok) break;
       unsigned char* a_hi = aslot0 + s * G.a_bytes;
       unsigned char* a_lo = a_hi + kTileM * D * 2;
@@ -244,7 +244,7 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
         for (int k = 0; k < G.nchunks && ok; ++k) {
           const int g = i * G.nchunks + k;
           const int bs = g % NB, bu = g / NB;
-          if (bu > 0) ok = mbar_wait(&sb.b_empty[bs], (bu - 1) & 1, abort_flag, status);
+          if (bu > 0) ok = mbar_wait_warp(&sb.b_empty[bs], (bu - 1) & 1, abort_flag, status);
           if (!ok) break;
           load_b(k, bslot[bs]);
           mbar_arrive(&sb.b_full[bs]);
@@ -298,6 +298,7 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
       }
       if (last_g >= 0) mbar_wait(&sb.acc_full[last_g & 1], (last_g >> 1) & 1, abort_flag, status);
     }
+    __syncwarp();
   } else {
     // ------------------------------------------------------------- epilogue
     const int quarter = warp & 3;
@@ -308,7 +309,7 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
     for (int i = 0; i < my_tiles && ok; ++i) {
       const int tile = t_begin + i;
       const int s = i % NA;
-      ok = mbar_wait(&sb.a_full[s], (i / NA) & 1, abort_flag, status);
+      ok = mbar_wait_warp(&sb.a_full[s], (i / NA) & 1, abort_flag, status);
       if (!ok) break;
       const float xn = xnorm[s][r];
       const float E = kBoundScale * xn * cmax + 1e-6f * (cmax * cmax + 2.0f * xn * cmax);
@@ -320,14 +321,14 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
       for (int k = 0; k < G.nchunks && ok; ++k) {
         const int g = i * G.nchunks + k;
         const int as = g & 1;
-        ok = mbar_wait(&sb.acc_full[as], (g >> 1) & 1, abort_flag, status);
+        ok = mbar_wait_warp(&sb.acc_full[as], (g >> 1) & 1, abort_flag, status);
         if (!ok) break;
         tc_fence_after();
         const uint32_t acc = tmem + as * G.nc + lane_off;
         for (int c0 = 0; c0 < G.nc; c0 += 32) {
           uint32_t v[32];
-          tmem_ld32(acc + c0, v);
-          tmem_ld_wait();
+          __syncwarp();
+          tmem_ld32_sync(acc + c0, v);
           const int cb = k * G.nc + c0;
           float d[32];
           float mn = INFINITY;
@@ -416,6 +417,7 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
       if (lane == 0) mbar_arrive(&sb.a_empty[s]);
     }
   }
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
   if (warp == kProdWarps) {
