@@ -154,6 +154,9 @@ const char* peco_error_string(int code);
 
 int peco_library_version(void);
 
+/* Number of kernels this library has launched in the process so far. */
+unsigned long long peco_launch_count(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -40,8 +40,10 @@ _SIGNATURES = {
     "peco_cluster_error_message": [I],
     "peco_attention_error_string": [I],
     "peco_library_version": [],
+    "peco_launch_count": [],
 }
 _RESTYPES = {
+    "peco_launch_count": ctypes.c_ulonglong,
     "peco_attention_workspace_stride": LL,
     "peco_error_string": ctypes.c_char_p,
     "peco_cluster_error_message": ctypes.c_char_p,

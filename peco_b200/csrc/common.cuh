@@ -329,7 +329,12 @@ bool encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t ran
 // library); kernels OR DeviceStatusBits into it.
 unsigned* device_status_ptr();
 
+// Counts kernel launches issued by the library (read with peco_launch_count()).
+void note_launch();
+
+// Status of the launch just issued; every launch site calls it exactly once.
 inline int launch_status() {
+  note_launch();
   cudaError_t e = cudaGetLastError();
   return static_cast<int>(e);
 }

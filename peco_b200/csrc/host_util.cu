@@ -1,5 +1,6 @@
 // Host utilities: TMA tensor-map encoding, the device status word and error
 // strings shared by all C-ABI entry points.
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -20,6 +21,8 @@ using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, voi
                               CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeFn g_encode = nullptr;
 std::once_flag g_encode_once;
+
+std::atomic<unsigned long long> g_launches{0};
 
 constexpr int kMaxDevices = 64;
 unsigned* g_status_ptr[kMaxDevices] = {};
@@ -49,6 +52,8 @@ bool encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t ran
                         swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
+
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 unsigned* device_status_ptr() {
   int dev = 0;
@@ -94,3 +99,5 @@ extern "C" int peco_device_status(unsigned* out, int clear, void* stream_ptr) {
 }
 
 extern "C" int peco_library_version(void) { return 1; }
+
+extern "C" unsigned long long peco_launch_count(void) { return peco::g_launches.load(std::memory_order_relaxed); }

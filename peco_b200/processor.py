@@ -107,6 +107,10 @@ class PecoAttention:
         self.context = context
         self.q_centroids = None
         self.k_centroids = None
+        # Optional list; when set, each sparse call appends a dict of CUDA
+        # events recorded on the current stream at the stage boundaries
+        # (kmeans, select, quantize_gather, attention) for profiling.
+        self.stage_events = None
 
     def reset(self):
         self.q_centroids = self.k_centroids = None
@@ -167,7 +171,14 @@ class PecoAttention:
         cq, ck = self.config.num_q_centroids, self.config.num_k_centroids
         if cq > video or ck > video:
             raise ValueError("more clusters than video tokens")
+        ev = None
+        if self.stage_events is not None:
+            ev = {n: torch.cuda.Event(enable_timing=True) for n in ("start", "kmeans", "select", "gather", "attention")}
+            self.stage_events.append(ev)
+            ev["start"].record()
         qb, kb = self._update_cluster_state(q[:, :, :video], k[:, :, :video])
+        if ev:
+            ev["kmeans"].record()
         dev = q.device
         gq, gk = cq + 2, ck + 2
         emap = torch.empty((1, h, gq, gk), dtype=torch.bool, device=dev)
@@ -181,6 +192,8 @@ class PecoAttention:
                 _native.ptr(kb.counts), _native.ptr(emap), _native.ptr(qs_ext), _native.ptr(ks_ext), h, cq, ck, d,
                 float(self.config.top_p), int(minimum), int(valid_text), int(text_length), stream)
             _native.check(st, "peco_select_text_partition")
+            if ev:
+                ev["select"].record()
             qp, kp, vp = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
             stream = _native.stream_of(dev, q, k, v, qp, kp, vp)
             st = lib.peco_quantize_gather(
@@ -189,6 +202,8 @@ class PecoAttention:
                 _native.ptr(self.q_centroids), _native.ptr(self.k_centroids), cq, ck, h, s, video, d,
                 int(self.config.base_offset_bits), stream)
             _native.check(st, "peco_quantize_gather")
+            if ev:
+                ev["gather"].record()
             out = torch.empty_like(q)
             stride = int(lib.peco_attention_workspace_stride(s, gq, gk))
             ws = torch.empty(h * stride, dtype=torch.int32, device=dev)
@@ -198,6 +213,8 @@ class PecoAttention:
                 _native.ptr(ks_ext), _native.ptr(out), _native.ptr(ws), h, s, s, d, gq, gk, _native.ptr(qb.perm),
                 video, stream)
             _native.check(st, "peco_sparse_attention_restore")
+            if ev:
+                ev["attention"].record()
         return out
 
     @torch.no_grad()
