@@ -194,6 +194,8 @@ class PecoAttention:
             _native.check(st, "peco_select_text_partition")
             if ev:
                 ev["select"].record()
+            if getattr(self, "keep_partition", False):
+                self.last_partition = (emap, qs_ext, ks_ext)
             qp, kp, vp = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
             stream = _native.stream_of(dev, q, k, v, qp, kp, vp)
             st = lib.peco_quantize_gather(
