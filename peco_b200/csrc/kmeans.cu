@@ -3,16 +3,19 @@
 //
 // Assignment (peco/kernels/kmeans.cu:139-175, peco/clustering.py:66-73):
 //   label = argmin_c ||c||^2 - 2 x.c, lowest index on ties.
-// The tokens of a PECO call are bf16, so x is exact as a bf16 MMA operand;
-// each centroid is rounded once to bf16 and S = X C^T is accumulated in fp32
-// in TMEM (tcgen05.mma, M=128 tokens, N<=256 centroids per chunk).  Rounding
-// c to bf16 moves each distance by at most
-//   E = 2^-7.9 ||x|| max||c||   (+ a tiny fp32 term),
-// so the epilogue keeps every centroid whose approximate distance lies within
-// 2E of the best one and recomputes those candidates exactly in fp32 on the
-// CUDA cores.  The label therefore equals the fp32 argmin except where two
-// fp32 distances tie to rounding level.  fp32 inputs (the legacy entry point)
-// are split into bf16 hi + lo operands and accumulated by two MMAs.
+// The tokens of a PECO call are bf16, so x is exact as a bf16 MMA operand.
+// Each fp32 centroid is split into two bf16 terms, c = c_hi + c_lo + r with
+// |r| <= 2^-16 |c|, and S = X (C_hi + C_lo)^T is accumulated in fp32 in TMEM
+// (tcgen05.mma, M=128 tokens, N<=256 centroids per chunk; both terms go into
+// the same accumulator).  The computed distance is then within
+//   E = 2^-12 ||x|| max||c|| + 2^-20 (max||c||^2 + 2 ||x|| max||c||)
+// of the fp32 distance (split residual, fp32 accumulation and the final
+// subtraction, with a 4x margin).  The epilogue keeps every centroid within
+// 2E of the best one: a single survivor is the fp32 argmin outright; several
+// survivors (near-ties) are recomputed exactly in fp32 on the CUDA cores and
+// the lowest index wins ties.  Labels therefore equal the fp32 argmin except
+// where two fp32 distances tie to rounding level.  fp32 inputs (the drop-in
+// entry point) also split x into bf16 hi + lo (three MMA terms).
 //
 // Update (peco/kernels/kmeans.cu:179-196, peco/clustering.py:74-80): tokens
 // are stably sorted by label (counting sort), then one warp per cluster sums
@@ -27,11 +30,16 @@
 namespace peco {
 namespace {
 
+#ifdef PECO_KMEANS_STATS
+__device__ unsigned long long g_kstats[8];
+#endif
+
 constexpr int kTileM = 128;
 constexpr int kProdWarps = 4, kEpiWarps = 4;
 constexpr int kAssignThreads = 32 * (kProdWarps + 1 + kEpiWarps);
 constexpr int kMaxCand = 8;
-constexpr float kBoundScale = 0.0045f;  // > 2^-7.9 (bf16 centroid rounding + fp32 accumulation)
+constexpr float kBoundScale = 2.44140625e-4f;   // 2^-12
+constexpr float kBoundTiny = 9.5367431640625e-7f;  // 2^-20
 
 struct AssignJob {
   const void* x;            // token rows, bf16 or fp32, row length D
@@ -59,11 +67,12 @@ __host__ __device__ constexpr int round16(int v) { return (v + 15) & ~15; }
 struct AssignGeom {
   int nc;        // centroids per chunk (multiple of 16, <= 256)
   int nchunks;
-  int a_bytes;   // one A slot (hi [+ lo])
-  int b_bytes;   // one B slot
+  int a_bytes;   // one A slot: x as bf16 (hi [+ lo] for fp32 inputs)
+  int b_bytes;   // one B slot: a centroid chunk as bf16 hi + lo
   int nbslots;   // B ring: 1 when the single chunk stays resident, else 2 (1 if smem is short)
   int naslots;   // A ring: 2 (1 if smem is short)
   int tmem_cols;
+  int norms_off; // byte offset of the staged centroid norms
   int smem;      // dynamic smem bytes
 };
 
@@ -72,10 +81,12 @@ __host__ __device__ inline AssignGeom assign_geom(int C, int D, bool xf32) {
   g.nc = round16(C < 256 ? C : 256);
   g.nchunks = (C + g.nc - 1) / g.nc;
   g.a_bytes = kTileM * D * 2 * (xf32 ? 2 : 1);
-  g.b_bytes = g.nc * D * 2;
+  g.b_bytes = 2 * g.nc * D * 2;
   g.nbslots = g.nchunks == 1 ? 1 : 2;
   g.naslots = 2;
-  while (1024 + g.nbslots * g.b_bytes + g.naslots * g.a_bytes > 225 * 1024 && (g.nbslots > 1 || g.naslots > 1)) {
+  const int norm_bytes = ((C * 4) + 1023) & ~1023;
+  while (1024 + g.nbslots * g.b_bytes + g.naslots * g.a_bytes + norm_bytes > 225 * 1024 &&
+         (g.nbslots > 1 || g.naslots > 1)) {
     if (g.nbslots > 1) g.nbslots = 1;
     else g.naslots = 1;
   }
@@ -83,7 +94,8 @@ __host__ __device__ inline AssignGeom assign_geom(int C, int D, bool xf32) {
   int p = 32;
   while (p < cols) p <<= 1;
   g.tmem_cols = p;
-  g.smem = 1024 + g.nbslots * g.b_bytes + g.naslots * g.a_bytes;
+  g.norms_off = g.nbslots * g.b_bytes + g.naslots * g.a_bytes;
+  g.smem = 1024 + g.norms_off + norm_bytes;
   return g;
 }
 
@@ -97,6 +109,19 @@ __device__ __forceinline__ void store_row_chunk(unsigned char* tile, int row, in
 __device__ __forceinline__ uint4 load_row_chunk(const unsigned char* tile, int row, int chunk, int panel_bytes) {
   const int panel = chunk >> 3, c = chunk & 7;
   return *reinterpret_cast<const uint4*>(tile + panel * panel_bytes + row * 128 + ((c ^ (row & 7)) << 4));
+}
+
+// bf16 hi/lo split of 8 fp32 values: hi = rn(v), lo = rn(v - hi)
+__device__ __forceinline__ void split8(const float (&f)[8], uint4& hi, uint4& lo) {
+  uint32_t* hw = reinterpret_cast<uint32_t*>(&hi);
+  uint32_t* lw = reinterpret_cast<uint32_t*>(&lo);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float h0 = __bfloat162float(__float2bfloat16_rn(f[2 * e]));
+    const float h1 = __bfloat162float(__float2bfloat16_rn(f[2 * e + 1]));
+    hw[e] = pack_bf16x2(h0, h1);
+    lw[e] = pack_bf16x2(f[2 * e] - h0, f[2 * e + 1] - h1);
+  }
 }
 
 template <int D, bool XF32>
@@ -116,6 +141,7 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* bslot[2] = {base, base + (G.nbslots > 1 ? G.b_bytes : 0)};
   unsigned char* aslot0 = base + G.nbslots * G.b_bytes;
+  float* cn = reinterpret_cast<float*>(base + G.norms_off);  // squared centroid norms of this head
   __shared__ AssignBars sb;
   __shared__ float xnorm[2][kTileM];
   volatile int* abort_flag = &sb.abort_flag;
@@ -140,10 +166,12 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
     tmem_alloc(&sb.tmem_base, G.tmem_cols);
     tmem_relinquish();
   }
+  for (int c = threadIdx.x; c < C; c += blockDim.x) cn[c] = norms[c];
+  __syncthreads();
   // max centroid norm of this head (bound scale)
   if (warp == 0) {
     float m = 0.0f;
-    for (int c = lane; c < C; c += 32) m = fmaxf(m, norms[c]);
+    for (int c = lane; c < C; c += 32) m = fmaxf(m, cn[c]);
     m = warp_max(m);
     if (lane == 0) sb.cmax = sqrtf(m);
   }
@@ -151,29 +179,32 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
   tc_fence_after();
   const uint32_t tmem = sb.tmem_base;
   const int a_panel = kTileM * 128;         // bytes per 64-column panel of an A tile
-  const int b_panel = G.nc * 128;
+  const int b_panel = G.nc * 128;           // bytes per 64-column panel of one B term
+  const int b_term = G.nc * D * 2;          // offset of the lo term in a B slot
 
   if (warp < kProdWarps) {
     // ------------------------------------------------------------ producers
     const int tid = threadIdx.x;  // 0..127
     bool ok = true;
     auto load_b = [&](int chunk, unsigned char* dst) {
-      // rows of this chunk: c = chunk*nc + j for j in [0, nc); thread handles j = tid, tid+128
+      // centroid rows j = tid, tid + 128 of this chunk, fp32 -> bf16 hi + lo
       for (int j = tid; j < G.nc; j += 32 * kProdWarps) {
         const int c = chunk * G.nc + j;
-        const float* src = cen + static_cast<long long>(c) * D;
-#pragma unroll 4
-        for (int ch = 0; ch < D / 8; ++ch) {
-          uint4 v = make_uint4(0, 0, 0, 0);
-          if (c < C) {
-            const float4 a = reinterpret_cast<const float4*>(src)[2 * ch];
-            const float4 b = reinterpret_cast<const float4*>(src)[2 * ch + 1];
-            v.x = pack_bf16x2(a.x, a.y);
-            v.y = pack_bf16x2(a.z, a.w);
-            v.z = pack_bf16x2(b.x, b.y);
-            v.w = pack_bf16x2(b.z, b.w);
+        const float4* src = reinterpret_cast<const float4*>(cen + static_cast<long long>(c) * D);
+#pragma unroll
+        for (int g = 0; g < D / 64; ++g) {
+          float4 buf[16];
+#pragma unroll
+          for (int u = 0; u < 16; ++u) buf[u] = c < C ? src[g * 16 + u] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const float f[8] = {buf[2 * u].x, buf[2 * u].y, buf[2 * u].z, buf[2 * u].w,
+                                buf[2 * u + 1].x, buf[2 * u + 1].y, buf[2 * u + 1].z, buf[2 * u + 1].w};
+            uint4 hi, lo;
+            split8(f, hi, lo);
+            store_row_chunk(dst, j, g * 8 + u, hi, b_panel);
+            store_row_chunk(dst + b_term, j, g * 8 + u, lo, b_panel);
           }
-          store_row_chunk(dst, j, ch, v, b_panel);
         }
       }
       fence_async_smem();
@@ -195,40 +226,39 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
       if (tok < J.tokens) {
         const long long grow = static_cast<long long>(head) * J.head_rows + tok;
         if (XF32) {
-          const float* src = static_cast<const float*>(J.x) + grow * D;
-#pragma unroll 4
-          for (int ch = 0; ch < D / 8; ++ch) {
-            const float4 a = reinterpret_cast<const float4*>(src)[2 * ch];
-            const float4 b = reinterpret_cast<const float4*>(src)[2 * ch + 1];
-            const float f[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-            uint4 hi, lo;
-            uint32_t* hw = reinterpret_cast<uint32_t*>(&hi);
-            uint32_t* lw = reinterpret_cast<uint32_t*>(&lo);
+          const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(J.x) + grow * D);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float h0 = __bfloat162float(__float2bfloat16_rn(f[2 * e]));
-              const float h1 = __bfloat162float(__float2bfloat16_rn(f[2 * e + 1]));
-              hw[e] = pack_bf16x2(h0, h1);
-              lw[e] = pack_bf16x2(f[2 * e] - h0, f[2 * e + 1] - h1);
-              ss = fmaf(f[2 * e], f[2 * e], ss);
-              ss = fmaf(f[2 * e + 1], f[2 * e + 1], ss);
+          for (int g = 0; g < D / 64; ++g) {
+            float4 buf[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) buf[u] = src[g * 16 + u];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              const float f[8] = {buf[2 * u].x, buf[2 * u].y, buf[2 * u].z, buf[2 * u].w,
+                                  buf[2 * u + 1].x, buf[2 * u + 1].y, buf[2 * u + 1].z, buf[2 * u + 1].w};
+#pragma unroll
+              for (int e = 0; e < 8; ++e) ss = fmaf(f[e], f[e], ss);
+              uint4 hi, lo;
+              split8(f, hi, lo);
+              store_row_chunk(a_hi, row, g * 8 + u, hi, a_panel);
+              store_row_chunk(a_lo, row, g * 8 + u, lo, a_panel);
             }
-            store_row_chunk(a_hi, row, ch, hi, a_panel);
-            store_row_chunk(a_lo, row, ch, lo, a_panel);
           }
         } else {
-          const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(J.x) + grow * D;
-#pragma unroll 4
+          const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(J.x) + grow * D);
+          uint4 buf[D / 8];
+#pragma unroll
+          for (int ch = 0; ch < D / 8; ++ch) buf[ch] = src[ch];
+#pragma unroll
           for (int ch = 0; ch < D / 8; ++ch) {
-            const uint4 v = reinterpret_cast<const uint4*>(src)[ch];
-            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&buf[ch]);
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const float2 f = __bfloat1622float2(h[e]);
               ss = fmaf(f.x, f.x, ss);
               ss = fmaf(f.y, f.y, ss);
             }
-            store_row_chunk(a_hi, row, ch, v, a_panel);
+            store_row_chunk(a_hi, row, ch, buf[ch], a_panel);
           }
         }
       } else {
@@ -275,21 +305,29 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
           }
           if (!ok) break;
           tc_fence_after();
-          const uint32_t b = smem_u32(bslot[bs]);
+          const uint32_t b_hi = smem_u32(bslot[bs]);
+          const uint32_t b_lo = b_hi + b_term;
           const uint32_t acc = tmem + as * G.nc;
+          // terms, smallest first: x.c_lo, [x_lo.c_hi], x.c_hi
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t off_a = (kk >> 2) * a_panel + (kk & 3) * 32;
             const uint32_t off_b = (kk >> 2) * b_panel + (kk & 3) * 32;
-            umma_ss(acc, smem_desc(a_hi + off_a, 16, 1024), smem_desc(b + off_b, 16, 1024), idesc, kk > 0 ? 1u : 0u);
+            umma_ss(acc, smem_desc(a_hi + off_a, 16, 1024), smem_desc(b_lo + off_b, 16, 1024), idesc, kk > 0 ? 1u : 0u);
           }
           if (XF32) {
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk) {
               const uint32_t off_a = (kk >> 2) * a_panel + (kk & 3) * 32;
               const uint32_t off_b = (kk >> 2) * b_panel + (kk & 3) * 32;
-              umma_ss(acc, smem_desc(a_lo + off_a, 16, 1024), smem_desc(b + off_b, 16, 1024), idesc, 1u);
+              umma_ss(acc, smem_desc(a_lo + off_a, 16, 1024), smem_desc(b_hi + off_b, 16, 1024), idesc, 1u);
             }
+          }
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off_a = (kk >> 2) * a_panel + (kk & 3) * 32;
+            const uint32_t off_b = (kk >> 2) * b_panel + (kk & 3) * 32;
+            umma_ss(acc, smem_desc(a_hi + off_a, 16, 1024), smem_desc(b_hi + off_b, 16, 1024), idesc, 1u);
           }
           umma_commit(&sb.acc_full[as]);
           if (G.nchunks > 1) umma_commit(&sb.b_empty[bs]);
@@ -312,12 +350,28 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
       ok = mbar_wait_warp(&sb.a_full[s], (i / NA) & 1, abort_flag, status);
       if (!ok) break;
       const float xn = xnorm[s][r];
-      const float E = kBoundScale * xn * cmax + 1e-6f * (cmax * cmax + 2.0f * xn * cmax);
-      const float E2 = 2.0f * E;
+      const float E2 = 2.0f * (kBoundScale * xn * cmax + kBoundTiny * (cmax * cmax + 2.0f * xn * cmax));
       float best = INFINITY;
       float cd[kMaxCand];
       int ci[kMaxCand];
       int ncand = 0;
+      bool overflow = false;
+      // keep entries within ``t`` (order preserved: slot m <= q)
+      auto prune = [&](float t) {
+        int m = 0;
+#pragma unroll
+        for (int q = 0; q < kMaxCand; ++q) {
+          const bool keep = q < ncand && cd[q] <= t;
+#pragma unroll
+          for (int p = 0; p < kMaxCand; ++p)
+            if (keep && p == m) {
+              cd[p] = cd[q];
+              ci[p] = ci[q];
+            }
+          m += keep ? 1 : 0;
+        }
+        ncand = m;
+      };
       for (int k = 0; k < G.nchunks && ok; ++k) {
         const int g = i * G.nchunks + k;
         const int as = g & 1;
@@ -335,7 +389,7 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int c = cb + j;
-            d[j] = (c < C) ? fmaf(-2.0f, __uint_as_float(v[j]), __ldg(norms + c)) : INFINITY;
+            d[j] = (c < C) ? fmaf(-2.0f, __uint_as_float(v[j]), cn[c]) : INFINITY;
             mn = fminf(mn, d[j]);
           }
           best = fminf(best, mn);
@@ -343,13 +397,18 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             if (d[j] <= thr) {
+              if (ncand == kMaxCand) prune(best + E2);
+              if (ncand < kMaxCand) {
 #pragma unroll
-              for (int q = 0; q < kMaxCand; ++q)
-                if (q == ncand) {
-                  cd[q] = d[j];
-                  ci[q] = cb + j;
-                }
-              ++ncand;
+                for (int q = 0; q < kMaxCand; ++q)
+                  if (q == ncand) {
+                    cd[q] = d[j];
+                    ci[q] = cb + j;
+                  }
+                ++ncand;
+              } else {
+                overflow = true;
+              }
             }
           }
         }
@@ -358,60 +417,87 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
         if (lane == 0) mbar_arrive(&sb.acc_empty[as]);
       }
       if (!ok) break;
-      // exact fp32 recompute of the candidates
       const int tok = tile * kTileM + r;
       if (tok < J.tokens) {
         const long long grow = static_cast<long long>(head) * J.head_rows + tok;
         const unsigned char* a_hi = aslot0 + s * G.a_bytes;
-        auto exact = [&](int c) -> float {
-          const float* cr = cen + static_cast<long long>(c) * D;
-          float dot = 0.0f;
-          if (XF32) {
-            const float* xr = static_cast<const float*>(J.x) + grow * D;
-#pragma unroll 8
-            for (int e = 0; e < D; ++e) dot = fmaf(xr[e], cr[e], dot);
-          } else {
+        prune(best + E2);
+        int label = ncand > 0 ? ci[0] : 0;
+        // exact fp32 distances of up to kMaxCand centroids ids[0..n), all
+        // dot products advanced together for memory-level parallelism
+        auto exact_group = [&](const int (&ids)[kMaxCand], int n, float& bd, int& bl) {
+          float dot[kMaxCand];
+#pragma unroll
+          for (int q = 0; q < kMaxCand; ++q) dot[q] = 0.0f;
 #pragma unroll 2
-            for (int ch = 0; ch < D / 8; ++ch) {
+          for (int ch = 0; ch < D / 8; ++ch) {
+            float xv[8];
+            if (XF32) {
+              const float4* xr = reinterpret_cast<const float4*>(static_cast<const float*>(J.x) + grow * D) + 2 * ch;
+              const float4 a = xr[0], b = xr[1];
+              xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w; xv[4] = b.x; xv[5] = b.y; xv[6] = b.z; xv[7] = b.w;
+            } else {
               const uint4 u = load_row_chunk(a_hi, r, ch, a_panel);
               const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-              const float4 c0 = reinterpret_cast<const float4*>(cr)[2 * ch];
-              const float4 c1 = reinterpret_cast<const float4*>(cr)[2 * ch + 1];
-              const float cc[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
                 const float2 f = __bfloat1622float2(h[e]);
-                dot = fmaf(f.x, cc[2 * e], dot);
-                dot = fmaf(f.y, cc[2 * e + 1], dot);
+                xv[2 * e] = f.x;
+                xv[2 * e + 1] = f.y;
+              }
+            }
+#pragma unroll
+            for (int q = 0; q < kMaxCand; ++q) {
+              if (q < n) {
+                const float4* cr = reinterpret_cast<const float4*>(cen + static_cast<long long>(ids[q]) * D) + 2 * ch;
+                const float4 a = cr[0], b = cr[1];
+                dot[q] = fmaf(xv[0], a.x, dot[q]);
+                dot[q] = fmaf(xv[1], a.y, dot[q]);
+                dot[q] = fmaf(xv[2], a.z, dot[q]);
+                dot[q] = fmaf(xv[3], a.w, dot[q]);
+                dot[q] = fmaf(xv[4], b.x, dot[q]);
+                dot[q] = fmaf(xv[5], b.y, dot[q]);
+                dot[q] = fmaf(xv[6], b.z, dot[q]);
+                dot[q] = fmaf(xv[7], b.w, dot[q]);
               }
             }
           }
-          return __fsub_rn(norms[c], 2.0f * dot);
-        };
-        int label = 0;
-        float bd = INFINITY;
-        const float thr = best + E2;
-        if (ncand <= kMaxCand) {
 #pragma unroll
           for (int q = 0; q < kMaxCand; ++q) {
-            if (q < ncand && cd[q] <= thr) {
-              const float e = exact(ci[q]);
-              if (e < bd) {
+            if (q < n) {
+              const float e = __fsub_rn(cn[ids[q]], 2.0f * dot[q]);
+              if (e < bd || (e == bd && ids[q] < bl)) {
                 bd = e;
-                label = ci[q];
+                bl = ids[q];
               }
             }
           }
-        } else {
-          for (int c = 0; c < C; ++c) {
-            const float e = exact(c);
-            if (e < bd) {
-              bd = e;
-              label = c;
-            }
+        };
+        if (overflow) {
+          // more than kMaxCand near-ties: exact scan over every centroid
+          float bd = INFINITY;
+          int bl = 0;
+          for (int c0 = 0; c0 < C; c0 += kMaxCand) {
+            int ids[kMaxCand];
+#pragma unroll
+            for (int q = 0; q < kMaxCand; ++q) ids[q] = min(c0 + q, C - 1);
+            exact_group(ids, min(kMaxCand, C - c0), bd, bl);
           }
+          label = bl;
+        } else if (ncand > 1) {
+          float bd = INFINITY;
+          int bl = 0x7fffffff;
+          exact_group(ci, ncand, bd, bl);
+          label = bl;
         }
         J.labels[static_cast<long long>(head) * J.tokens + tok] = label;
+#ifdef PECO_KMEANS_STATS
+        // debug builds: [0] tokens, [1] survivors after pruning, [2] overflows, [3] tokens needing a recompute
+        atomicAdd(&g_kstats[0], 1ull);
+        atomicAdd(&g_kstats[1], static_cast<unsigned long long>(ncand));
+        if (overflow) atomicAdd(&g_kstats[2], 1ull);
+        if (ncand > 1) atomicAdd(&g_kstats[3], 1ull);
+#endif
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&sb.a_empty[s]);
