@@ -418,78 +418,79 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
       }
       if (!ok) break;
       const int tok = tile * kTileM + r;
-      if (tok < J.tokens) {
-        const long long grow = static_cast<long long>(head) * J.head_rows + tok;
-        const unsigned char* a_hi = aslot0 + s * G.a_bytes;
-        prune(best + E2);
-        int label = ncand > 0 ? ci[0] : 0;
-        // exact fp32 distances of up to kMaxCand centroids ids[0..n), all
-        // dot products advanced together for memory-level parallelism
-        auto exact_group = [&](const int (&ids)[kMaxCand], int n, float& bd, int& bl) {
-          float dot[kMaxCand];
+      const bool valid = tok < J.tokens;
+      prune(best + E2);
+      int label = ncand > 0 ? ci[0] : 0;
+      // Near-ties are recomputed in exact fp32, one token at a time by the
+      // whole warp: lane l owns D/32 consecutive dimensions, so each
+      // candidate centroid row is one coalesced load, and all candidates of
+      // the token are in flight together.
+      unsigned amb = __ballot_sync(0xffffffffu, valid && (overflow || ncand > 1));
+      constexpr int E = D / 32;
+      const unsigned char* a_hi = aslot0 + s * G.a_bytes;
+      while (amb) {
+        const int src = __ffs(amb) - 1;
+        amb &= amb - 1;
+        const int stok = __shfl_sync(0xffffffffu, tok, src);
+        const int n = __shfl_sync(0xffffffffu, overflow ? -1 : ncand, src);
+        const long long grow = static_cast<long long>(head) * J.head_rows + stok;
+        float xv[E];
+        if (XF32) {
+          const float* xr = static_cast<const float*>(J.x) + grow * D + lane * E;
 #pragma unroll
-          for (int q = 0; q < kMaxCand; ++q) dot[q] = 0.0f;
-#pragma unroll 2
-          for (int ch = 0; ch < D / 8; ++ch) {
-            float xv[8];
-            if (XF32) {
-              const float4* xr = reinterpret_cast<const float4*>(static_cast<const float*>(J.x) + grow * D) + 2 * ch;
-              const float4 a = xr[0], b = xr[1];
-              xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w; xv[4] = b.x; xv[5] = b.y; xv[6] = b.z; xv[7] = b.w;
-            } else {
-              const uint4 u = load_row_chunk(a_hi, r, ch, a_panel);
-              const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+          for (int e = 0; e < E; ++e) xv[e] = xr[e];
+        } else {
+          const int srow = quarter * 32 + src;
+          const uint4 u = load_row_chunk(a_hi, srow, (lane * E) >> 3, a_panel);
+          const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u) + ((lane * E) & 7);
 #pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float2 f = __bfloat1622float2(h[e]);
-                xv[2 * e] = f.x;
-                xv[2 * e + 1] = f.y;
-              }
-            }
-#pragma unroll
-            for (int q = 0; q < kMaxCand; ++q) {
-              if (q < n) {
-                const float4* cr = reinterpret_cast<const float4*>(cen + static_cast<long long>(ids[q]) * D) + 2 * ch;
-                const float4 a = cr[0], b = cr[1];
-                dot[q] = fmaf(xv[0], a.x, dot[q]);
-                dot[q] = fmaf(xv[1], a.y, dot[q]);
-                dot[q] = fmaf(xv[2], a.z, dot[q]);
-                dot[q] = fmaf(xv[3], a.w, dot[q]);
-                dot[q] = fmaf(xv[4], b.x, dot[q]);
-                dot[q] = fmaf(xv[5], b.y, dot[q]);
-                dot[q] = fmaf(xv[6], b.z, dot[q]);
-                dot[q] = fmaf(xv[7], b.w, dot[q]);
-              }
-            }
-          }
-#pragma unroll
-          for (int q = 0; q < kMaxCand; ++q) {
-            if (q < n) {
-              const float e = __fsub_rn(cn[ids[q]], 2.0f * dot[q]);
-              if (e < bd || (e == bd && ids[q] < bl)) {
-                bd = e;
-                bl = ids[q];
-              }
-            }
+          for (int e = 0; e < E; ++e) xv[e] = __bfloat162float(h[e]);
+        }
+        float bd = INFINITY;
+        int bl = 0x7fffffff;
+        auto score = [&](int id, float partial) {
+          const float dot = warp_sum(partial);
+          const float e = __fsub_rn(cn[id], 2.0f * dot);
+          if (e < bd || (e == bd && id < bl)) {
+            bd = e;
+            bl = id;
           }
         };
-        if (overflow) {
-          // more than kMaxCand near-ties: exact scan over every centroid
-          float bd = INFINITY;
-          int bl = 0;
-          for (int c0 = 0; c0 < C; c0 += kMaxCand) {
-            int ids[kMaxCand];
+        if (n >= 0) {
+          float part[kMaxCand];
+          int ids[kMaxCand];
 #pragma unroll
-            for (int q = 0; q < kMaxCand; ++q) ids[q] = min(c0 + q, C - 1);
-            exact_group(ids, min(kMaxCand, C - c0), bd, bl);
+          for (int q = 0; q < kMaxCand; ++q) {
+            ids[q] = __shfl_sync(0xffffffffu, ci[q], src);
+            part[q] = 0.0f;
+            if (q < n) {
+              const float* cr = cen + static_cast<long long>(ids[q]) * D + lane * E;
+#pragma unroll
+              for (int e = 0; e < E; ++e) part[q] = fmaf(xv[e], cr[e], part[q]);
+            }
           }
-          label = bl;
-        } else if (ncand > 1) {
-          float bd = INFINITY;
-          int bl = 0x7fffffff;
-          exact_group(ci, ncand, bd, bl);
-          label = bl;
+#pragma unroll
+          for (int q = 0; q < kMaxCand; ++q)
+            if (q < n) score(ids[q], part[q]);
+        } else {
+          for (int c0 = 0; c0 < C; c0 += 4) {
+            float part[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              part[q] = 0.0f;
+              const int id = min(c0 + q, C - 1);
+              const float* cr = cen + static_cast<long long>(id) * D + lane * E;
+#pragma unroll
+              for (int e = 0; e < E; ++e) part[q] = fmaf(xv[e], cr[e], part[q]);
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              if (c0 + q < C) score(c0 + q, part[q]);
+          }
         }
+        if (lane == src) label = bl;
+      }
+      if (valid) {
         J.labels[static_cast<long long>(head) * J.tokens + tok] = label;
 #ifdef PECO_KMEANS_STATS
         // debug builds: [0] tokens, [1] survivors after pruning, [2] overflows, [3] tokens needing a recompute
@@ -543,6 +544,23 @@ struct UpdateJobs {
   UpdateJob job[2];
 };
 
+// E consecutive elements of a row as fp32, in one vector load when possible.
+template <typename T, int E>
+__device__ __forceinline__ void load_lane_elems(const T* row, float (&v)[E]) {
+  if constexpr (sizeof(T) == 2 && E == 4) {
+    const uint2 u = *reinterpret_cast<const uint2*>(row);
+    const T* h = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[e] = to_f32<T>(h[e]);
+  } else if constexpr (sizeof(T) == 4 && E == 4) {
+    const float4 f = *reinterpret_cast<const float4*>(row);
+    v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+  } else {
+#pragma unroll
+    for (int e = 0; e < E; ++e) v[e] = to_f32<T>(row[e]);
+  }
+}
+
 template <int D, typename T>
 __global__ void kmeans_update_kernel(const UpdateJobs jobs, int bh, unsigned* status) {
   const UpdateJob& J = jobs.job[blockIdx.y];
@@ -559,37 +577,37 @@ __global__ void kmeans_update_kernel(const UpdateJobs jobs, int bh, unsigned* st
   float acc[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) acc[e] = 0.0f;
-  int i = start;
-  // four rows in flight, accumulated strictly in ascending token order
   bool bad = start < 0 || end > J.tokens || start > end;
   if (bad) end = start;
-  for (; i + 4 <= end; i += 4) {
-    float v[4][E];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      int t = perm[i + u];
-      if (t < 0 || t >= J.tokens) {
+  // The cluster's token ids arrive 32 at a time in one coalesced load; rows
+  // are then fetched 8 at a time (all in flight) and added strictly in
+  // ascending token order.
+  for (int base = start; base < end; base += 32) {
+    int my_t = 0;
+    if (base + lane < end) {
+      my_t = perm[base + lane];
+      if (my_t < 0 || my_t >= J.tokens) {
         bad = true;
-        t = 0;
+        my_t = 0;
       }
-      const T* row = xb + static_cast<long long>(t) * D;
-#pragma unroll
-      for (int e = 0; e < E; ++e) v[u][e] = to_f32<T>(row[e]);
     }
+    const int cnt = min(32, end - base);
+    for (int j = 0; j < cnt; j += 8) {
+      float v[8][E];
 #pragma unroll
-    for (int u = 0; u < 4; ++u)
+      for (int u = 0; u < 8; ++u) {
+        const int t = __shfl_sync(0xffffffffu, my_t, (j + u) & 31);
+        if (j + u < cnt) {
+          const T* row = xb + static_cast<long long>(t) * D;
+          load_lane_elems<T, E>(row, v[u]);
+        }
+      }
 #pragma unroll
-      for (int e = 0; e < E; ++e) acc[e] = __fadd_rn(acc[e], v[u][e]);
-  }
-  for (; i < end; ++i) {
-    int t = perm[i];
-    if (t < 0 || t >= J.tokens) {
-      bad = true;
-      t = 0;
+      for (int u = 0; u < 8; ++u)
+        if (j + u < cnt)
+#pragma unroll
+          for (int e = 0; e < E; ++e) acc[e] = __fadd_rn(acc[e], v[u][e]);
     }
-    const T* row = xb + static_cast<long long>(t) * D;
-#pragma unroll
-    for (int e = 0; e < E; ++e) acc[e] = __fadd_rn(acc[e], to_f32<T>(row[e]));
   }
   if (bad && lane == 0) record_status(status, kDevBadIndex);
   const int n = end - start;
