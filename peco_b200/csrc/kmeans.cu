@@ -394,21 +394,30 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
           }
           best = fminf(best, mn);
           const float thr = best + E2;
+          // Candidates of this block as a bit mask; the (rare) pushes run in
+          // one compact loop instead of 32 unrolled copies.
+          unsigned m = 0;
+          if (mn <= thr) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (d[j] <= thr) {
-              if (ncand == kMaxCand) prune(best + E2);
-              if (ncand < kMaxCand) {
+            for (int j = 0; j < 32; ++j) m |= (d[j] <= thr ? 1u : 0u) << j;
+          }
+          while (m) {
+            const int j = __ffs(m) - 1;
+            m &= m - 1;
+            float dj = 0.0f;
 #pragma unroll
-                for (int q = 0; q < kMaxCand; ++q)
-                  if (q == ncand) {
-                    cd[q] = d[j];
-                    ci[q] = cb + j;
-                  }
-                ++ncand;
-              } else {
-                overflow = true;
-              }
+            for (int jj = 0; jj < 32; ++jj) dj = (jj == j) ? d[jj] : dj;
+            if (ncand == kMaxCand) prune(thr);
+            if (ncand < kMaxCand) {
+#pragma unroll
+              for (int q = 0; q < kMaxCand; ++q)
+                if (q == ncand) {
+                  cd[q] = dj;
+                  ci[q] = cb + j;
+                }
+              ++ncand;
+            } else {
+              overflow = true;
             }
           }
         }
