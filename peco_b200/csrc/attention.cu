@@ -8,20 +8,28 @@
 // share one key set, so masking is per key column only).  For each unit the
 // selected key groups become contiguous runs of the group-packed K/V; runs
 // are streamed as 8-row TMA boxes into 128-key tiles (rows of a box past the
-// run's end are masked).  Per tile:
-//   S = Q K^T           tcgen05.mma, A = Q (smem), B = K tile (smem), S in TMEM
-//   P = exp2(S*c - m)   4 softmax warps, thread = query row, online max with
-//                       lazy rescale of O (only when the max grows by > 8 in
-//                       log2 units); P written back to TMEM as 16-bit pairs
-//   O += P V            tcgen05.mma, A = P (TMEM), B = V tile (smem, MN-major)
-// Warp roles: warp 0 = TMA producer, warp 1 = MMA issuer (one thread) and
-// TMEM owner, warps 2-5 = softmax + epilogue.  Two CTAs share an SM (256
-// TMEM columns and ~100 KB smem each) so one CTA's softmax overlaps the
-// other's MMAs.  The epilogue optionally scatters rows through an inverse
-// permutation (fusing peco/clustering.py:127-136 into the output store).
+// run's end are masked).  Per tile t:
+//   S[t%2]  = Q K^T          tcgen05.mma, A = Q (smem), B = K tile (smem)
+//   P       = exp2(S*c - m)  4 softmax warps, thread = query row; online max
+//                            with lazy rescale of O (only when the max grows
+//                            by > 8 in log2 units); P overwrites S[t%2] in
+//                            TMEM as 16-bit pairs
+//   O[u%2] += P V            tcgen05.mma, A = P (TMEM), B = V tile (smem, MN-major)
+// The MMA issuer runs one tile ahead (QK of tile t+1 before PV of tile t), so
+// the tensor core computes the next scores while the softmax warps work on the
+// current ones; K/V tiles stream through a 2-stage ring, Q through 2 slots,
+// and O is double-buffered so a unit's epilogue overlaps the next unit.
 //
-// Every wait is bounded (common.cuh); on expiry the CTA records kDevTimeout
-// in the device status word, drains what it issued and exits.
+// CTAs are persistent (one per SM) and take units heaviest-first: the
+// planner lists every head's text groups (which attend to every key) before
+// its video clusters, and CTAs claim (unit, head) pairs in unit-major order
+// from a work counter in the workspace.
+//
+// Warp roles: warp 0 = TMA producer and scheduler, warp 1 = MMA issuer (one
+// thread) and TMEM owner, warps 2-5 = softmax + epilogue.  The epilogue can
+// scatter rows through an inverse permutation (fusing peco/clustering.py:
+// 127-136 into the output store).  Every wait is bounded (common.cuh); on
+// expiry the CTA records kDevTimeout in the device status word and unwinds.
 #include "common.cuh"
 #include "../../include/peco_b200.h"
 #include "internal.h"
@@ -33,16 +41,20 @@ constexpr int kBM = 128;       // query rows per unit
 constexpr int kBN = 128;       // keys per tile
 constexpr int kBox = 8;        // rows per TMA box
 constexpr int kBoxes = kBN / kBox;
-constexpr int kRing = 4;       // mask ring depth
+constexpr int kStages = 2;     // K/V ring depth
+constexpr int kRing = 8;       // tile-info ring depth
 constexpr int kThreads = 192;  // 6 warps
-constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kTmemCols = 512;  // S0 | S1 | O0 | O1, 128 columns each
+
+// tile-info flags
+constexpr uint32_t kFirst = 1u, kLast = 2u, kEmpty = 4u, kEnd = 8u;
 
 #ifdef PECO_ATTN_TRACE
-// Debug builds record per-CTA progress: trace[cta*8 + role] = stage code.
+// Debug builds record per-CTA progress: trace[cta*8 + slot] = value.
 #define ATTN_TRACE(slot, value)                                                                   \
   do {                                                                                            \
     if (args.trace) {                                                                             \
-      volatile unsigned* t_ = args.trace + (static_cast<long long>(blockIdx.y) * gridDim.x + blockIdx.x) * 8; \
+      volatile unsigned* t_ = args.trace + static_cast<long long>(blockIdx.x) * 8;                \
       t_[slot] = (value);                                                                         \
       __threadfence_system();                                                                     \
     }                                                                                             \
@@ -58,21 +70,30 @@ struct AttnArgs {
   unsigned* trace;
 #endif
   const uint8_t* map;      // [BH, GQ, GK]
-  const int* ws;           // planner output, ws_stride ints per head
-  void* out;               // [BH, SO, D]
+  int* ws;                 // planner output, ws_stride ints per head
+  void* out;               // [BH, out_rows, D]
   const int32_t* perm;     // optional [BH, video] inverse permutation for packed rows < video
-  int sq, sk, gq, gk, ws_stride;
+  int bh, sq, sk, gq, gk, ws_stride, max_units;
   int out_rows;            // rows per head of the output tensor
   int video;               // packed rows below this index go through perm
+  int dynamic_sched;       // claim units from the work counter (else a static stride)
   float scale_log2;        // log2(e) / sqrt(D)
   unsigned* status;
 };
 
+struct TileInfo {
+  uint32_t mask[4];        // key rows of the tile that are valid
+  int unit;                // virtual unit index (local * BH + head)
+  uint32_t flags;
+};
+
 struct __align__(8) Shared {
-  uint64_t q_full, k_full, k_empty, v_full, v_empty, s_full, p_full, pv_done;
-  uint64_t mask_full[kRing], mask_empty[kRing];
-  uint32_t mask[kRing][4];
-  uint32_t flags[kRing];   // bit0: last tile, bit1: unit has no keys
+  uint64_t q_full[2], q_empty[2];
+  uint64_t k_full[kStages], k_empty[kStages], v_full[kStages], v_empty[kStages];
+  uint64_t s_full[2], s_free[2], p_full[2];
+  uint64_t o_full[2], o_free[2];
+  uint64_t info_full[kRing], info_empty[kRing];
+  TileInfo info[kRing];
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -82,8 +103,16 @@ struct Layout {
   static constexpr int kTileBytes = kBN * D * 2;   // K or V tile, also the Q tile
   static constexpr int kBoxBytes = kBox * D * 2;   // one 8-row box (D/64 panels of 1 KB)
   static constexpr int kQPanel = kBM * 128;        // Q panel: 128 rows x 128 B
-  static constexpr int kSmem = 1024 + 3 * kTileBytes + static_cast<int>(sizeof(Shared));
+  static constexpr int kQ0 = 0;
+  static constexpr int kK0 = 2 * kTileBytes;
+  static constexpr int kV0 = kK0 + kStages * kTileBytes;
+  static constexpr int kShared = kV0 + kStages * kTileBytes;
+  static constexpr int kSmem = 1024 + kShared + static_cast<int>(sizeof(Shared));
 };
+
+__device__ __forceinline__ int* work_counter(const AttnArgs& a) {
+  return a.ws + static_cast<long long>(a.bh - 1) * a.ws_stride + (a.ws_stride - 1);
+}
 
 // ---------------------------------------------------------------------------
 // planner: clamped group prefixes and the unit list of every head
@@ -121,7 +150,7 @@ __device__ long long block_exclusive_scan(long long v, long long* tmp) {
 // dynamic smem: 2 * gq ints (clamped start and size of every query group)
 __global__ void __launch_bounds__(1024) attn_plan_kernel(const int* __restrict__ q_sizes, const int* __restrict__ k_sizes,
                                                          int* __restrict__ ws, int gq, int gk, int sq, int sk,
-                                                         int ws_stride) {
+                                                         int ws_stride, int zero_counter) {
   extern __shared__ int plan_sm[];
   int* gstart = plan_sm;
   int* gcount = plan_sm + gq;
@@ -137,6 +166,8 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(const int* __restrict__
   if (threadIdx.x == 0) {
     carry = 0;
     kp[0] = 0;
+    // work counter of the persistent attention kernel (last int of the last head)
+    if (zero_counter && head == gridDim.x - 1) w[ws_stride - 1] = 0;
   }
   __syncthreads();
   for (int c0 = 0; c0 < gk; c0 += blockDim.x) {
@@ -185,43 +216,40 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(const int* __restrict__
 }
 
 // ---------------------------------------------------------------------------
-// main kernel
+// main kernel (persistent)
 // ---------------------------------------------------------------------------
 template <int D, int AB>  // AB: 0 = fp16, 1 = bf16
-__global__ void __launch_bounds__(kThreads, 2) sparse_attention_tc(const __grid_constant__ CUtensorMap tmap_q,
+__global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_constant__ CUtensorMap tmap_q,
                                                                   const __grid_constant__ CUtensorMap tmap_k,
                                                                   const __grid_constant__ CUtensorMap tmap_v,
                                                                   const AttnArgs args) {
   using L = Layout<D>;
-  const int head = blockIdx.y;
-  const int* w = args.ws + static_cast<long long>(head) * args.ws_stride;
-  const int nunits = w[0];
-  if (static_cast<int>(blockIdx.x) >= nunits) return;
-  const int* kp = w + 1;
-  const int* unit = w + 2 + args.gk + 3 * blockIdx.x;
-  const int q_start = unit[0], q_count = unit[1], qg = unit[2];
-
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  unsigned char* q_tile = base;
-  unsigned char* k_tile = base + L::kTileBytes;
-  unsigned char* v_tile = base + 2 * L::kTileBytes;
-  Shared& sh = *reinterpret_cast<Shared*>(base + 3 * L::kTileBytes);
+  Shared& sh = *reinterpret_cast<Shared*>(base + L::kShared);
   volatile int* abort_flag = &sh.abort_flag;
-
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long total_units = static_cast<long long>(args.bh) * args.max_units;
+
   if (threadIdx.x == 0) {
-    mbar_init(&sh.q_full, 1);
-    mbar_init(&sh.k_full, 1);
-    mbar_init(&sh.k_empty, 1);
-    mbar_init(&sh.v_full, 1);
-    mbar_init(&sh.v_empty, 1);
-    mbar_init(&sh.s_full, 1);
-    mbar_init(&sh.p_full, 4);
-    mbar_init(&sh.pv_done, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sh.q_full[i], 1);
+      mbar_init(&sh.q_empty[i], 1);
+      mbar_init(&sh.s_full[i], 1);
+      mbar_init(&sh.s_free[i], 1);
+      mbar_init(&sh.p_full[i], 4);
+      mbar_init(&sh.o_full[i], 1);
+      mbar_init(&sh.o_free[i], 4);
+    }
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&sh.k_full[i], 1);
+      mbar_init(&sh.k_empty[i], 1);
+      mbar_init(&sh.v_full[i], 1);
+      mbar_init(&sh.v_empty[i], 1);
+    }
     for (int i = 0; i < kRing; ++i) {
-      mbar_init(&sh.mask_full[i], 1);
-      mbar_init(&sh.mask_empty[i], 5);  // MMA thread + 4 softmax warps
+      mbar_init(&sh.info_full[i], 1);
+      mbar_init(&sh.info_empty[i], 5);  // MMA thread + 4 softmax warps
     }
     sh.abort_flag = 0;
     fence_barrier_init();
@@ -234,250 +262,352 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_tc(const __grid_
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sh.tmem_base;
-  if (threadIdx.x == 0) ATTN_TRACE(0, 2);
-  const uint32_t tmem_s = tmem;          // S: columns [0,128); P aliases [0,64)
-  const uint32_t tmem_o = tmem + 128;    // O: columns [128, 128+D)
-
-  const uint8_t* map_row = args.map + (static_cast<long long>(head) * args.gq + qg) * args.gk;
-  const long long krow0 = static_cast<long long>(head) * args.sk;
 
   if (warp == 0) {
-    // ------------------------------------------------------------- producer
+    // ------------------------------------------------------- producer
     if (lane == 0) {
       prefetch_tensormap(&tmap_q);
       prefetch_tensormap(&tmap_k);
       prefetch_tensormap(&tmap_v);
-      mbar_arrive_expect_tx(&sh.q_full, L::kTileBytes);
-#pragma unroll
-      for (int p = 0; p < D / 64; ++p)
-        tma_load_2d(q_tile + p * L::kQPanel, &tmap_q, 64 * p, static_cast<int>(static_cast<long long>(head) * args.sq + q_start), &sh.q_full);
     }
-    // pending tile: box rows and valid counts live in lanes 0..15
-    int box_row = 0, box_valid = 0;  // for lane == box index
-    int nbox = 0;                    // boxes collected in the pending tile
-    int tile = 0;
     bool ok = true;
-    int run_s = 0, run_e = 0;        // pending merged run (lane-uniform)
-    auto emit_tile = [&](bool last) {
-      // pad unused boxes with in-bounds rows of this head, fully masked
-      if (lane >= nbox && lane < kBoxes) {
-        box_row = static_cast<int>(krow0);
-        box_valid = 0;
+    int tile = 0;      // K/V tiles issued by this CTA
+    int entry = 0;     // info entries pushed
+    int qunits = 0;    // non-empty units (Q slots used)
+    int claims = 0;
+    auto push_info = [&](const uint32_t (&mask)[4], int unit, uint32_t flags) {
+      const int slot = entry % kRing;
+      if (ok && entry >= kRing) ok = mbar_wait_warp(&sh.info_empty[slot], ((entry / kRing) - 1) & 1, abort_flag, args.status);
+      if (lane == 0 && ok) {
+        TileInfo& ti = sh.info[slot];
+        ti.mask[0] = mask[0];
+        ti.mask[1] = mask[1];
+        ti.mask[2] = mask[2];
+        ti.mask[3] = mask[3];
+        ti.unit = unit;
+        ti.flags = flags;
+        mbar_arrive(&sh.info_full[slot]);
       }
-      const int slot = tile % kRing;
-      const uint32_t ph = (tile / kRing) & 1;
-      if (ok && tile >= kRing) ok = mbar_wait_warp(&sh.mask_empty[slot], ph ^ 1, abort_flag, args.status);
-      unsigned vm = 0;
-      // mask words: bit j of word i -> key row 32 i + j valid
-      {
+      __syncwarp();
+      ++entry;
+    };
+    for (;;) {
+      // ---- claim a unit
+      long long v = 0;
+      if (args.dynamic_sched) {
+        int got = 0;
+        if (lane == 0) got = atomicAdd(work_counter(args), 1);
+        v = __shfl_sync(0xffffffffu, got, 0);
+      } else {
+        v = static_cast<long long>(blockIdx.x) + static_cast<long long>(claims) * gridDim.x;
+        ++claims;
+      }
+      if (v >= total_units || !ok) break;
+      const int head = static_cast<int>(v % args.bh);
+      const int local = static_cast<int>(v / args.bh);
+      const int* w = args.ws + static_cast<long long>(head) * args.ws_stride;
+      if (local >= w[0]) continue;
+      const int* kp = w + 1;
+      const int* rec = w + 2 + args.gk + 3 * local;
+      const int q_start = rec[0], qg = rec[2];
+      const uint8_t* map_row = args.map + (static_cast<long long>(head) * args.gq + qg) * args.gk;
+      const long long krow0 = static_cast<long long>(head) * args.sk;
+
+      // ---- stream the unit's key runs as 8-row boxes grouped into tiles
+      int box_row = 0, box_valid = 0;  // lane b holds box b of the pending tile
+      int nbox = 0;
+      int utiles = 0;
+      int run_s = 0, run_e = 0;
+      bool have_run = false;
+      auto emit_tile = [&](bool last) {
+        if (lane >= nbox && lane < kBoxes) {  // padding boxes: in-bounds rows, fully masked
+          box_row = static_cast<int>(krow0);
+          box_valid = 0;
+        }
+        if (utiles == 0) {
+          // first tile of a non-empty unit: load its Q tile
+          const int qs = qunits & 1;
+          if (ok && qunits >= 2) ok = mbar_wait_warp(&sh.q_empty[qs], ((qunits >> 1) - 1) & 1, abort_flag, args.status);
+          if (lane == 0 && ok) {
+            mbar_arrive_expect_tx(&sh.q_full[qs], L::kTileBytes);
+#pragma unroll
+            for (int p = 0; p < D / 64; ++p)
+              tma_load_2d(base + L::kQ0 + qs * L::kTileBytes + p * L::kQPanel, &tmap_q, 64 * p,
+                          static_cast<int>(static_cast<long long>(head) * args.sq + q_start), &sh.q_full[qs]);
+          }
+          __syncwarp();
+          ++qunits;
+        }
         const unsigned bits = (box_valid >= 8) ? 0xffu : ((1u << box_valid) - 1u);
-        unsigned word[4] = {0, 0, 0, 0};
+        uint32_t word[4] = {0, 0, 0, 0};
 #pragma unroll
-        for (int b = 0; b < kBoxes; ++b) {
-          const unsigned bb = __shfl_sync(0xffffffffu, bits, b);
-          word[b >> 2] |= bb << (8 * (b & 3));
-        }
-        vm = word[0];
-        if (lane == 0 && ok) {
-          sh.mask[slot][0] = word[0];
-          sh.mask[slot][1] = word[1];
-          sh.mask[slot][2] = word[2];
-          sh.mask[slot][3] = word[3];
-          sh.flags[slot] = last ? 1u : 0u;
-        }
-      }
-      (void)vm;
-      __syncwarp();
-      if (lane == 0 && ok) mbar_arrive(&sh.mask_full[slot]);
-      // K boxes
-      if (ok && tile > 0) ok = mbar_wait_warp(&sh.k_empty, (tile - 1) & 1, abort_flag, args.status);
-      if (lane == 0 && ok) mbar_arrive_expect_tx(&sh.k_full, L::kTileBytes);
-      __syncwarp();
-      if (ok && lane < kBoxes) {
+        for (int b = 0; b < kBoxes; ++b) word[b >> 2] |= __shfl_sync(0xffffffffu, bits, b) << (8 * (b & 3));
+        push_info(word, static_cast<int>(v), (utiles == 0 ? kFirst : 0u) | (last ? kLast : 0u));
+        const int st = tile % kStages;
+        const uint32_t ph = ((tile / kStages) - 1) & 1;
+        if (ok && tile >= kStages) ok = mbar_wait_warp(&sh.k_empty[st], ph, abort_flag, args.status);
+        if (lane == 0 && ok) mbar_arrive_expect_tx(&sh.k_full[st], L::kTileBytes);
+        __syncwarp();
+        if (ok && lane < kBoxes) {
 #pragma unroll
-        for (int p = 0; p < D / 64; ++p)
-          tma_load_2d(k_tile + lane * L::kBoxBytes + p * 1024, &tmap_k, 64 * p, box_row, &sh.k_full);
-      }
-      // V boxes (the V tile is free once the previous P.V finished)
-      if (ok && tile > 0) ok = mbar_wait_warp(&sh.v_empty, (tile - 1) & 1, abort_flag, args.status);
-      if (lane == 0 && ok) mbar_arrive_expect_tx(&sh.v_full, L::kTileBytes);
-      __syncwarp();
-      if (ok && lane < kBoxes) {
+          for (int p = 0; p < D / 64; ++p)
+            tma_load_2d(base + L::kK0 + st * L::kTileBytes + lane * L::kBoxBytes + p * 1024, &tmap_k, 64 * p, box_row,
+                        &sh.k_full[st]);
+        }
+        if (ok && tile >= kStages) ok = mbar_wait_warp(&sh.v_empty[st], ph, abort_flag, args.status);
+        if (lane == 0 && ok) mbar_arrive_expect_tx(&sh.v_full[st], L::kTileBytes);
+        __syncwarp();
+        if (ok && lane < kBoxes) {
 #pragma unroll
-        for (int p = 0; p < D / 64; ++p)
-          tma_load_2d(v_tile + lane * L::kBoxBytes + p * 1024, &tmap_v, 64 * p, box_row, &sh.v_full);
-      }
-      ++tile;
-      nbox = 0;
-      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-      if (lane == 0) ATTN_TRACE(1, 0x100u + tile);
-    };
-    auto add_box = [&](int row, int valid) {
-      if (nbox == kBoxes) emit_tile(false);
-      if (lane == nbox) {
-        box_row = row;
-        box_valid = valid;
-      }
-      ++nbox;
-    };
-    auto flush_run = [&]() {
-      for (int r = run_s; r < run_e && ok; r += kBox) add_box(static_cast<int>(krow0 + r), min(kBox, run_e - r));
-    };
-    bool have_run = false;
-    for (int c0 = 0; c0 < args.gk && ok; c0 += 32) {
-      const int c = c0 + lane;
-      int s = 0, e = 0;
-      bool sel = false;
-      if (c < args.gk) {
-        s = kp[c];
-        e = kp[c + 1];
-        sel = map_row[c] != 0 && e > s;
-      }
-      unsigned m = __ballot_sync(0xffffffffu, sel);
-      while (m && ok) {
-        const int b = __ffs(m) - 1;
-        m &= m - 1;
-        const int gs = __shfl_sync(0xffffffffu, s, b);
-        const int ge = __shfl_sync(0xffffffffu, e, b);
-        if (have_run && gs == run_e) {
-          run_e = ge;
-        } else {
-          if (have_run) flush_run();
-          run_s = gs;
-          run_e = ge;
-          have_run = true;
+          for (int p = 0; p < D / 64; ++p)
+            tma_load_2d(base + L::kV0 + st * L::kTileBytes + lane * L::kBoxBytes + p * 1024, &tmap_v, 64 * p, box_row,
+                        &sh.v_full[st]);
         }
-      }
-      if (*abort_flag) ok = false;
-      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-    }
-    if (have_run && ok) flush_run();
-    if (ok) {
-      if (tile == 0 && nbox == 0) {
-        // no key at all: announce an empty unit
-        if (lane == 0) {
-          sh.flags[0] = 3u;
-          mbar_arrive(&sh.mask_full[0]);
+        ++tile;
+        ++utiles;
+        nbox = 0;
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (lane == 0) ATTN_TRACE(1, 0x100u + tile);
+      };
+      auto add_box = [&](int row, int valid) {
+        if (nbox == kBoxes) emit_tile(false);
+        if (lane == nbox) {
+          box_row = row;
+          box_valid = valid;
         }
+        ++nbox;
+      };
+      auto flush_run = [&]() {
+        for (int r = run_s; r < run_e && ok; r += kBox) add_box(static_cast<int>(krow0 + r), min(kBox, run_e - r));
+      };
+      for (int c0 = 0; c0 < args.gk && ok; c0 += 32) {
+        const int c = c0 + lane;
+        int s = 0, e = 0;
+        bool sel = false;
+        if (c < args.gk) {
+          s = kp[c];
+          e = kp[c + 1];
+          sel = map_row[c] != 0 && e > s;
+        }
+        unsigned m = __ballot_sync(0xffffffffu, sel);
+        while (m && ok) {
+          const int b = __ffs(m) - 1;
+          m &= m - 1;
+          const int gs = __shfl_sync(0xffffffffu, s, b);
+          const int ge = __shfl_sync(0xffffffffu, e, b);
+          if (have_run && gs == run_e) {
+            run_e = ge;
+          } else {
+            if (have_run) flush_run();
+            run_s = gs;
+            run_e = ge;
+            have_run = true;
+          }
+        }
+        if (*abort_flag) ok = false;
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      }
+      if (have_run && ok) flush_run();
+      if (!ok) break;
+      if (utiles == 0 && nbox == 0) {
+        const uint32_t zero[4] = {0, 0, 0, 0};
+        push_info(zero, static_cast<int>(v), kEmpty);  // no key at all: rows are zero
       } else {
         emit_tile(true);
       }
     }
-    // drain: wait for the loads this warp issued before the CTA exits
-    if (tile > 0) {
-      mbar_wait_warp(&sh.k_full, (tile - 1) & 1, abort_flag, args.status);
-      mbar_wait_warp(&sh.v_full, (tile - 1) & 1, abort_flag, args.status);
-    }
+    const uint32_t zero[4] = {0, 0, 0, 0};
+    push_info(zero, -1, kEnd);
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA
     if (lane == 0) {
       constexpr uint32_t idesc_qk = instr_desc(128, kBN, AB, false, false);
       constexpr uint32_t idesc_pv = instr_desc(128, D, AB, false, true);
-      const uint32_t qa = smem_u32(q_tile), ka = smem_u32(k_tile), va = smem_u32(v_tile);
-      bool ok = mbar_wait(&sh.q_full, 0, abort_flag, args.status);
-      int issued = 0;  // PV commits issued
-      for (int t = 0; ok; ++t) {
-        const int slot = t % kRing;
-        ok = mbar_wait(&sh.mask_full[slot], (t / kRing) & 1, abort_flag, args.status);
-        if (!ok) break;
-        const uint32_t fl = sh.flags[slot];
-        mbar_arrive(&sh.mask_empty[slot]);
-        if (fl & 2u) break;
-        ok = mbar_wait(&sh.k_full, t & 1, abort_flag, args.status);
-        if (ok && t > 0) ok = mbar_wait(&sh.pv_done, (t - 1) & 1, abort_flag, args.status);
-        if (!ok) break;
+      bool ok = true;
+      int entry = 0, t = 0, qunits = 0, ounits = 0;
+      int cur = -1;           // tile whose P.V is pending
+      uint32_t cur_flags = 0;
+      int cur_oslot = 0;
+      auto issue_pv = [&]() {
+        const int b = cur & 1, st = cur % kStages;
+        ok = mbar_wait(&sh.p_full[b], (cur >> 1) & 1, abort_flag, args.status);
+        if (ok) ok = mbar_wait(&sh.v_full[st], (cur / kStages) & 1, abort_flag, args.status);
+        if (!ok) return;
         tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t koff = (kk >> 2) * 1024 + (kk & 3) * 32;
-          const uint64_t adesc = smem_desc(qa + (kk >> 2) * L::kQPanel + (kk & 3) * 32, 16, 1024);
-          const uint64_t bdesc = smem_desc(ka + koff, 16, L::kBoxBytes);
-          umma_ss(tmem_s, adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(&sh.s_full);
-        umma_commit(&sh.k_empty);
-        ATTN_TRACE(2, 0x100u + t);
-        ok = mbar_wait(&sh.p_full, t & 1, abort_flag, args.status);
-        if (ok) ok = mbar_wait(&sh.v_full, t & 1, abort_flag, args.status);
-        if (!ok) break;
-        tc_fence_after();
+        const uint32_t va = smem_u32(base + L::kV0 + st * L::kTileBytes);
+        const uint32_t o_addr = tmem + 256 + cur_oslot * 128;
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
           const uint64_t bdesc = smem_desc(va + kk * 2 * L::kBoxBytes, 1024, L::kBoxBytes);
-          umma_ts(tmem_o, tmem_s + kk * 8, bdesc, idesc_pv, (t > 0 || kk > 0) ? 1u : 0u);
+          umma_ts(o_addr, tmem + b * 128 + kk * 8, bdesc, idesc_pv, ((cur_flags & kFirst) && kk == 0) ? 0u : 1u);
         }
-        umma_commit(&sh.pv_done);
-        umma_commit(&sh.v_empty);
-        ATTN_TRACE(2, 0x200u + t);
-        ++issued;
-        if (fl & 1u) break;
+        umma_commit(&sh.s_free[b]);
+        umma_commit(&sh.v_empty[st]);
+        if (cur_flags & kLast) umma_commit(&sh.o_full[cur_oslot]);
+        ATTN_TRACE(2, 0x200u + cur);
+      };
+      for (;;) {
+        const int slot = entry % kRing;
+        ok = mbar_wait(&sh.info_full[slot], (entry / kRing) & 1, abort_flag, args.status);
+        if (!ok) break;
+        const uint32_t fl = sh.info[slot].flags;
+        mbar_arrive(&sh.info_empty[slot]);
+        ++entry;
+        if (fl & kEnd) break;
+        if (fl & kEmpty) continue;
+        // ---- S[t%2] = Q K^T for the next tile
+        const int b = t & 1, st = t % kStages;
+        ok = mbar_wait(&sh.k_full[st], (t / kStages) & 1, abort_flag, args.status);
+        if (ok && t >= 2) ok = mbar_wait(&sh.s_free[b], ((t >> 1) - 1) & 1, abort_flag, args.status);
+        const int qs = (fl & kFirst) ? (qunits & 1) : ((qunits - 1) & 1);
+        if (ok && (fl & kFirst)) {
+          ok = mbar_wait(&sh.q_full[qs], (qunits >> 1) & 1, abort_flag, args.status);
+          ++qunits;
+        }
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t qa = smem_u32(base + L::kQ0 + qs * L::kTileBytes);
+        const uint32_t ka = smem_u32(base + L::kK0 + st * L::kTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t adesc = smem_desc(qa + (kk >> 2) * L::kQPanel + (kk & 3) * 32, 16, 1024);
+          const uint64_t bdesc = smem_desc(ka + (kk >> 2) * 1024 + (kk & 3) * 32, 16, L::kBoxBytes);
+          umma_ss(tmem + b * 128, adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&sh.s_full[b]);
+        umma_commit(&sh.k_empty[st]);
+        if (fl & kLast) umma_commit(&sh.q_empty[qs]);
+        ATTN_TRACE(2, 0x100u + t);
+        // ---- O += P V for the previous tile
+        if (cur >= 0) {
+          issue_pv();
+          if (!ok) break;
+        }
+        cur = t;
+        cur_flags = fl;
+        if (fl & kFirst) {
+          cur_oslot = ounits & 1;
+          if (ounits >= 2) ok = mbar_wait(&sh.o_free[cur_oslot], ((ounits >> 1) - 1) & 1, abort_flag, args.status);
+          ++ounits;
+          if (!ok) break;
+        }
+        ++t;
       }
+      if (ok && cur >= 0) issue_pv();
       // drain our MMAs before TMEM is released
-      if (issued > 0) mbar_wait(&sh.pv_done, (issued - 1) & 1, abort_flag, args.status);
+      if (cur >= 0) mbar_wait(&sh.s_free[cur & 1], (cur >> 1) & 1, abort_flag, args.status);
     }
     __syncwarp();
   } else {
-    // -------------------------------------------------------------- softmax
+    // ----------------------------------------------- softmax + epilogue
+    using T = typename std::conditional<AB == 1, __nv_bfloat16, __half>::type;
     const int quarter = warp & 3;                  // TMEM lane quarter of this warp
     const int r = quarter * 32 + lane;             // query row within the unit
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     float m = -INFINITY, l = 0.0f;
-    bool ok = true, empty = false;
-    int t = 0;
-    for (;; ++t) {
-      const int slot = t % kRing;
-      ok = mbar_wait_warp(&sh.mask_full[slot], (t / kRing) & 1, abort_flag, args.status);
-      if (!ok) break;
-      const uint32_t fl = sh.flags[slot];
-      const uint32_t mw0 = sh.mask[slot][0], mw1 = sh.mask[slot][1], mw2 = sh.mask[slot][2], mw3 = sh.mask[slot][3];
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sh.mask_empty[slot]);
-      if (fl & 2u) {
-        empty = true;
-        break;
+    bool ok = true;
+    int entry = 0, t = 0, ounits = 0, oslot = 0;
+    // write this thread's row of unit v: O/l, or zero when ``zero``
+    auto write_row = [&](int v, bool have_o, float inv) {
+      const int head = v % args.bh, local = v / args.bh;
+      const int* rec = args.ws + static_cast<long long>(head) * args.ws_stride + 2 + args.gk + 3 * local;
+      const int q_start = rec[0], q_count = rec[1];
+      T* dst = nullptr;
+      if (r < q_count) {
+        const int prow = q_start + r;
+        long long orow = prow;
+        if (args.perm && prow < args.video) orow = args.perm[static_cast<long long>(head) * args.video + prow];
+        if (orow < 0 || orow >= args.out_rows) record_status(args.status, kDevBadIndex);
+        else dst = static_cast<T*>(args.out) + (static_cast<long long>(head) * args.out_rows + orow) * D;
       }
-      if (lane == 0) ATTN_TRACE(3 + quarter, 0x100u + t);
-      ok = mbar_wait_warp(&sh.s_full, t & 1, abort_flag, args.status);
+      __syncwarp();
+      if (have_o) {
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t vv[32];
+          tmem_ld32_sync(tmem + 256 + oslot * 128 + lane_off + c * 32, vv);
+          if (dst) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+              uint4 pk;
+              uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float a = __uint_as_float(vv[j + 2 * e]) * inv, bb = __uint_as_float(vv[j + 2 * e + 1]) * inv;
+                pw[e] = AB ? pack_bf16x2(a, bb) : pack_f16x2(a, bb);
+              }
+              reinterpret_cast<uint4*>(dst)[(c * 32 + j) / 8] = pk;
+            }
+          }
+        }
+      } else if (dst) {
+#pragma unroll
+        for (int c = 0; c < D / 8; ++c) reinterpret_cast<uint4*>(dst)[c] = make_uint4(0, 0, 0, 0);
+      }
+      __syncwarp();
+    };
+    for (;;) {
+      const int slot = entry % kRing;
+      ok = mbar_wait_warp(&sh.info_full[slot], (entry / kRing) & 1, abort_flag, args.status);
+      if (!ok) break;
+      const TileInfo ti = sh.info[slot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh.info_empty[slot]);
+      ++entry;
+      if (ti.flags & kEnd) break;
+      if (ti.flags & kEmpty) {
+        write_row(ti.unit, false, 0.0f);
+        continue;
+      }
+      if (ti.flags & kFirst) {
+        m = -INFINITY;
+        l = 0.0f;
+        oslot = ounits & 1;
+        ++ounits;
+      }
+      const int b = t & 1;
+      ok = mbar_wait_warp(&sh.s_full[b], (t >> 1) & 1, abort_flag, args.status);
       if (!ok) break;
       tc_fence_after();
-      if (lane == 0) ATTN_TRACE(3 + quarter, 0x200u + t);
       float s[kBN];
 #pragma unroll
       for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld32_sync(tmem_s + lane_off + c * 32, v);
+        uint32_t vv[32];
+        tmem_ld32_sync(tmem + b * 128 + lane_off + c * 32, vv);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) s[c * 32 + j] = __uint_as_float(v[j]);
+        for (int j = 0; j < 32; ++j) s[c * 32 + j] = __uint_as_float(vv[j]);
       }
-      const uint32_t mw[4] = {mw0, mw1, mw2, mw3};
       float mx = -INFINITY;
 #pragma unroll
       for (int j = 0; j < kBN; ++j) {
-        const bool valid = (mw[j >> 5] >> (j & 31)) & 1u;
+        const bool valid = (ti.mask[j >> 5] >> (j & 31)) & 1u;
         s[j] = valid ? s[j] * args.scale_log2 : -INFINITY;
         mx = fmaxf(mx, s[j]);
       }
       // grow the running max lazily (only by > 8 in log2 units); rescaling O
-      // is warp-collective because tcgen05.ld/st are .sync.aligned.  The
-      // previous P.V is complete: this tile's QK^T was issued after it.
+      // is warp-collective (tcgen05.ld/st are .sync.aligned) and needs the
+      // previous tile's P.V to be complete
       const bool grow = (mx > m + 8.0f) || (m == -INFINITY && mx > -INFINITY);
       const bool rescale_me = grow && m != -INFINITY;
       if (__any_sync(0xffffffffu, rescale_me)) {
+        ok = mbar_wait_warp(&sh.s_free[(t - 1) & 1], ((t - 1) >> 1) & 1, abort_flag, args.status);
+        if (!ok) break;
+        tc_fence_after();
         const float f = rescale_me ? exp2f(m - mx) : 1.0f;
         l *= f;
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
-          uint32_t v[32];
-          tmem_ld32_sync(tmem_o + lane_off + c * 32, v);
+          uint32_t vv[32];
+          tmem_ld32_sync(tmem + 256 + oslot * 128 + lane_off + c * 32, vv);
           uint32_t lo[16], hi[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            lo[j] = __float_as_uint(__uint_as_float(v[j]) * f);
-            hi[j] = __float_as_uint(__uint_as_float(v[16 + j]) * f);
+            lo[j] = __float_as_uint(__uint_as_float(vv[j]) * f);
+            hi[j] = __float_as_uint(__uint_as_float(vv[16 + j]) * f);
           }
-          tmem_st16(tmem_o + lane_off + c * 32, lo);
-          tmem_st16(tmem_o + lane_off + c * 32 + 16, hi);
+          tmem_st16(tmem + 256 + oslot * 128 + lane_off + c * 32, lo);
+          tmem_st16(tmem + 256 + oslot * 128 + lane_off + c * 32 + 16, hi);
         }
       }
       if (grow) m = mx;
@@ -497,54 +627,24 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_tc(const __grid_
         uint32_t part[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) part[j] = packed[c * 16 + j];
-        tmem_st16(tmem_s + lane_off + c * 16, part);
+        tmem_st16(tmem + b * 128 + lane_off + c * 16, part);
       }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
+      if (lane == 0) mbar_arrive(&sh.p_full[b]);
       if (lane == 0) ATTN_TRACE(3 + quarter, 0x300u + t);
-      if (lane == 0) mbar_arrive(&sh.p_full);
-      if (fl & 1u) break;
-    }
-    // epilogue
-    const bool have_o = ok && !empty;
-    if (have_o) ok = mbar_wait_warp(&sh.pv_done, t & 1, abort_flag, args.status);
-    tc_fence_after();
-    if (lane == 0) ATTN_TRACE(3 + quarter, 0x400u + (ok ? 1u : 0u));
-    // TMEM reads are warp-collective; only the stores depend on the row
-    using T = typename std::conditional<AB == 1, __nv_bfloat16, __half>::type;
-    T* dst = nullptr;
-    if (r < q_count && (ok || empty)) {
-      const int prow = q_start + r;
-      long long orow = prow;
-      if (args.perm && prow < args.video) orow = args.perm[static_cast<long long>(head) * args.video + prow];
-      if (orow < 0 || orow >= args.out_rows) record_status(args.status, kDevBadIndex);
-      else dst = static_cast<T*>(args.out) + (static_cast<long long>(head) * args.out_rows + orow) * D;
-    }
-    __syncwarp();
-    if (have_o && ok) {
-      const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld32_sync(tmem_o + lane_off + c * 32, v);
-        if (dst) {
-#pragma unroll
-          for (int j = 0; j < 32; j += 8) {
-            uint4 pk;
-            uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float a = __uint_as_float(v[j + 2 * e]) * inv, b = __uint_as_float(v[j + 2 * e + 1]) * inv;
-              pw[e] = AB ? pack_bf16x2(a, b) : pack_f16x2(a, b);
-            }
-            reinterpret_cast<uint4*>(dst)[(c * 32 + j) / 8] = pk;
-          }
-        }
+      ++t;
+      if (ti.flags & kLast) {
+        // epilogue of the unit: O[oslot] is final once its last P.V completes
+        ok = mbar_wait_warp(&sh.o_full[oslot], ((ounits - 1) >> 1) & 1, abort_flag, args.status);
+        if (!ok) break;
+        tc_fence_after();
+        write_row(ti.unit, true, l > 0.0f ? 1.0f / l : 0.0f);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh.o_free[oslot]);
       }
-    } else if (dst && empty) {
-#pragma unroll
-      for (int c = 0; c < D / 8; ++c) reinterpret_cast<uint4*>(dst)[c] = make_uint4(0, 0, 0, 0);
     }
     __syncwarp();
   }
@@ -555,7 +655,6 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_tc(const __grid_
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
-  if (threadIdx.x == 32) ATTN_TRACE(0, 4);
 }
 
 #ifdef PECO_ATTN_TRACE
@@ -570,18 +669,25 @@ bool make_rows_map(CUtensorMap* m, const void* base, long long rows, int dims, i
                            base, gdims, gstr, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+int num_sms() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return kNumSMs;
+  return n > 0 ? n : kNumSMs;
+}
+
 template <int D, int AB>
-int launch_main(const void* q, const void* k, const void* v, const AttnArgs& a, int bh, int max_units,
-                cudaStream_t stream) {
+int launch_main(const void* q, const void* k, const void* v, const AttnArgs& a, cudaStream_t stream) {
   CUtensorMap tq, tk, tv;
-  if (!make_rows_map(&tq, q, static_cast<long long>(bh) * a.sq, D, kBM, AB) ||
-      !make_rows_map(&tk, k, static_cast<long long>(bh) * a.sk, D, kBox, AB) ||
-      !make_rows_map(&tv, v, static_cast<long long>(bh) * a.sk, D, kBox, AB))
+  if (!make_rows_map(&tq, q, static_cast<long long>(a.bh) * a.sq, D, kBM, AB) ||
+      !make_rows_map(&tk, k, static_cast<long long>(a.bh) * a.sk, D, kBox, AB) ||
+      !make_rows_map(&tv, v, static_cast<long long>(a.bh) * a.sk, D, kBox, AB))
     return kErrTensorMap;
   const int smem = Layout<D>::kSmem;
   cudaError_t e = cudaFuncSetAttribute(sparse_attention_tc<D, AB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return static_cast<int>(e);
-  dim3 grid(max_units, bh);
+  const long long total = static_cast<long long>(a.bh) * a.max_units;
+  const int grid = static_cast<int>(total < num_sms() ? total : num_sms());
   sparse_attention_tc<D, AB><<<grid, kThreads, smem, stream>>>(tq, tk, tv, a);
   return launch_status();
 }
@@ -598,6 +704,7 @@ int launch_sparse_attention(const void* q, const void* k, const void* v, const u
   const long long max_units = (static_cast<long long>(sq) + kBM - 1) / kBM + gq;
   const long long need = 2 + gk + 3 * max_units;
   if (need > ws_stride) return kErrWorkspace;
+  if (static_cast<long long>(bh) * max_units > 2147483647LL) return kErrUnsupported;
   const size_t plan_smem = 2 * sizeof(int) * static_cast<size_t>(gq);
   if (plan_smem > 200 * 1024) return kErrUnsupported;
   if (plan_smem > 48 * 1024)
@@ -605,7 +712,10 @@ int launch_sparse_attention(const void* q, const void* k, const void* v, const u
   if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
        reinterpret_cast<uintptr_t>(out)) & 15)
     return kErrInvalidValue;
-  attn_plan_kernel<<<bh, 1024, plan_smem, stream>>>(q_sizes, k_sizes, ws, gq, gk, sq, sk, ws_stride);
+  // the work counter takes the last int of the last head's region when the
+  // workspace has room for it; otherwise CTAs take units with a fixed stride
+  const int dynamic = ws_stride >= need + 1 ? 1 : 0;
+  attn_plan_kernel<<<bh, 1024, plan_smem, stream>>>(q_sizes, k_sizes, ws, gq, gk, sq, sk, ws_stride, dynamic);
   int rc = launch_status();
   if (rc) return rc;
   AttnArgs a;
@@ -616,26 +726,27 @@ int launch_sparse_attention(const void* q, const void* k, const void* v, const u
   a.ws = ws;
   a.out = out;
   a.perm = perm;
+  a.bh = bh;
   a.sq = sq;
   a.sk = sk;
   a.gq = gq;
   a.gk = gk;
   a.ws_stride = ws_stride;
+  a.max_units = static_cast<int>(max_units);
   a.out_rows = sq;
   a.video = perm ? video : 0;
+  a.dynamic_sched = dynamic;
   a.scale_log2 = static_cast<float>(1.4426950408889634 / sqrt(static_cast<double>(d)));
   a.status = device_status_ptr();
-  if (d == 128)
-    return dtype ? launch_main<128, 1>(q, k, v, a, bh, static_cast<int>(max_units), stream)
-                 : launch_main<128, 0>(q, k, v, a, bh, static_cast<int>(max_units), stream);
-  return dtype ? launch_main<64, 1>(q, k, v, a, bh, static_cast<int>(max_units), stream)
-               : launch_main<64, 0>(q, k, v, a, bh, static_cast<int>(max_units), stream);
+  if (d == 128) return dtype ? launch_main<128, 1>(q, k, v, a, stream) : launch_main<128, 0>(q, k, v, a, stream);
+  return dtype ? launch_main<64, 1>(q, k, v, a, stream) : launch_main<64, 0>(q, k, v, a, stream);
 }
 
-// Workspace ints per head needed by launch_sparse_attention.
+// Workspace ints per head needed by launch_sparse_attention (the last one
+// of the last head holds the work counter).
 long long attention_ws_stride(int sq, int gq, int gk) {
   const long long max_units = (static_cast<long long>(sq) + kBM - 1) / kBM + gq;
-  return 2 + gk + 3 * max_units;
+  return 3 + gk + 3 * max_units;
 }
 
 }  // namespace peco
