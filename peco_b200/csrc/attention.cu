@@ -6,9 +6,10 @@
 //
 // Work unit: up to 128 query rows of ONE query group (all rows of a unit
 // share one key set, so masking is per key column only).  For each unit the
-// selected key groups become contiguous runs of the group-packed K/V; runs
-// are streamed as 8-row TMA boxes into 128-key tiles (rows of a box past the
-// run's end are masked).  Per tile t:
+// selected key groups become contiguous runs of the group-packed K/V; every
+// run is padded to whole 8-row groups, 16 groups make a 128-key tile, and
+// consecutive groups of a run are fetched by one TMA box of 8, 16, 32, 64 or
+// 128 rows (rows past a run's end are masked).  Per tile t:
 //   S[t%2]  = Q K^T          tcgen05.mma, A = Q (smem), B = K tile (smem)
 //   P       = exp2(S*c - m)  4 softmax warps, thread = query row; online max
 //                            with lazy rescale of O (only when the max grows
@@ -17,8 +18,9 @@
 //   O[u%2] += P V            tcgen05.mma, A = P (TMEM), B = V tile (smem, MN-major)
 // The MMA issuer runs one tile ahead (QK of tile t+1 before PV of tile t), so
 // the tensor core computes the next scores while the softmax warps work on the
-// current ones; K/V tiles stream through a 2-stage ring, Q through 2 slots,
-// and O is double-buffered so a unit's epilogue overlaps the next unit.
+// current ones.  K and V tiles stream through a 6-slot ring (three tiles in
+// flight), and O is double-buffered so a unit's epilogue overlaps the next
+// unit's MMAs.
 //
 // CTAs are persistent (one per SM) and take units heaviest-first: the
 // planner lists every head's text groups (which attend to every key) before
@@ -39,11 +41,12 @@ namespace {
 
 constexpr int kBM = 128;       // query rows per unit
 constexpr int kBN = 128;       // keys per tile
-constexpr int kBox = 8;        // rows per TMA box
-constexpr int kBoxes = kBN / kBox;
-constexpr int kStages = 2;     // K/V ring depth
+constexpr int kGroup = 8;      // rows per key group (the padding granule)
+constexpr int kGroups = kBN / kGroup;
+constexpr int kSlots = 6;      // K/V ring: slot of K(t) = 2t mod 6, V(t) = 2t+1 mod 6
 constexpr int kRing = 8;       // tile-info ring depth
 constexpr int kThreads = 192;  // 6 warps
+constexpr int kHeights = 5;    // TMA box heights 8 << h rows, h = 0..4
 constexpr uint32_t kTmemCols = 512;  // S0 | S1 | O0 | O1, 128 columns each
 
 // tile-info flags
@@ -81,6 +84,13 @@ struct AttnArgs {
   unsigned* status;
 };
 
+// TMA descriptors: Q (128-row boxes) and K/V with box heights 8 << h.
+struct AttnMaps {
+  CUtensorMap q;
+  CUtensorMap k[kHeights];
+  CUtensorMap v[kHeights];
+};
+
 struct TileInfo {
   uint32_t mask[4];        // key rows of the tile that are valid
   int unit;                // virtual unit index (local * BH + head)
@@ -88,8 +98,8 @@ struct TileInfo {
 };
 
 struct __align__(8) Shared {
-  uint64_t q_full[2], q_empty[2];
-  uint64_t k_full[kStages], k_empty[kStages], v_full[kStages], v_empty[kStages];
+  uint64_t q_full, q_empty;
+  uint64_t slot_full[kSlots], slot_empty[kSlots];
   uint64_t s_full[2], s_free[2], p_full[2];
   uint64_t o_full[2], o_free[2];
   uint64_t info_full[kRing], info_empty[kRing];
@@ -98,15 +108,15 @@ struct __align__(8) Shared {
   int abort_flag;
 };
 
+// Operand tiles (Q, K, V) share one layout: two 64-column panels of 128 rows
+// x 128 bytes (16 KB each, 128-byte swizzle), 8-row groups 1 KB apart.
 template <int D>
 struct Layout {
-  static constexpr int kTileBytes = kBN * D * 2;   // K or V tile, also the Q tile
-  static constexpr int kBoxBytes = kBox * D * 2;   // one 8-row box (D/64 panels of 1 KB)
-  static constexpr int kQPanel = kBM * 128;        // Q panel: 128 rows x 128 B
+  static constexpr int kTileBytes = kBN * D * 2;
+  static constexpr int kPanel = kBN * 128;
   static constexpr int kQ0 = 0;
-  static constexpr int kK0 = 2 * kTileBytes;
-  static constexpr int kV0 = kK0 + kStages * kTileBytes;
-  static constexpr int kShared = kV0 + kStages * kTileBytes;
+  static constexpr int kSlot0 = kTileBytes;
+  static constexpr int kShared = kSlot0 + kSlots * kTileBytes;
   static constexpr int kSmem = 1024 + kShared + static_cast<int>(sizeof(Shared));
 };
 
@@ -219,9 +229,7 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(const int* __restrict__
 // main kernel (persistent)
 // ---------------------------------------------------------------------------
 template <int D, int AB>  // AB: 0 = fp16, 1 = bf16
-__global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_constant__ CUtensorMap tmap_q,
-                                                                  const __grid_constant__ CUtensorMap tmap_k,
-                                                                  const __grid_constant__ CUtensorMap tmap_v,
+__global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_constant__ AttnMaps maps,
                                                                   const AttnArgs args) {
   using L = Layout<D>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -232,20 +240,18 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
   const long long total_units = static_cast<long long>(args.bh) * args.max_units;
 
   if (threadIdx.x == 0) {
+    mbar_init(&sh.q_full, 1);
+    mbar_init(&sh.q_empty, 1);
+    for (int i = 0; i < kSlots; ++i) {
+      mbar_init(&sh.slot_full[i], 1);
+      mbar_init(&sh.slot_empty[i], 1);
+    }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&sh.q_full[i], 1);
-      mbar_init(&sh.q_empty[i], 1);
       mbar_init(&sh.s_full[i], 1);
       mbar_init(&sh.s_free[i], 1);
       mbar_init(&sh.p_full[i], 4);
       mbar_init(&sh.o_full[i], 1);
       mbar_init(&sh.o_free[i], 4);
-    }
-    for (int i = 0; i < kStages; ++i) {
-      mbar_init(&sh.k_full[i], 1);
-      mbar_init(&sh.k_empty[i], 1);
-      mbar_init(&sh.v_full[i], 1);
-      mbar_init(&sh.v_empty[i], 1);
     }
     for (int i = 0; i < kRing; ++i) {
       mbar_init(&sh.info_full[i], 1);
@@ -254,6 +260,11 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
     sh.abort_flag = 0;
     fence_barrier_init();
   }
+  // K/V rows of padding groups are never loaded: zero the ring once so the
+  // tensor core only ever sees finite values there
+  for (int i = threadIdx.x; i < kSlots * L::kTileBytes / 16; i += blockDim.x)
+    reinterpret_cast<uint4*>(base + L::kSlot0)[i] = make_uint4(0, 0, 0, 0);
+  fence_async_smem();
   if (threadIdx.x == 0) ATTN_TRACE(0, 1);
   if (warp == 1) {
     tmem_alloc(&sh.tmem_base, kTmemCols);
@@ -266,14 +277,16 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
   if (warp == 0) {
     // ------------------------------------------------------- producer
     if (lane == 0) {
-      prefetch_tensormap(&tmap_q);
-      prefetch_tensormap(&tmap_k);
-      prefetch_tensormap(&tmap_v);
+      prefetch_tensormap(&maps.q);
+      for (int h = 0; h < kHeights; ++h) {
+        prefetch_tensormap(&maps.k[h]);
+        prefetch_tensormap(&maps.v[h]);
+      }
     }
     bool ok = true;
-    int tile = 0;      // K/V tiles issued by this CTA
+    int tile = 0;      // tiles issued by this CTA
     int entry = 0;     // info entries pushed
-    int qunits = 0;    // non-empty units (Q slots used)
+    int qloads = 0;    // Q tiles loaded
     int claims = 0;
     auto push_info = [&](const uint32_t (&mask)[4], int unit, uint32_t flags) {
       const int slot = entry % kRing;
@@ -290,6 +303,37 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
       }
       __syncwarp();
       ++entry;
+    };
+    // Fill ring item ``item`` (K or V of a tile) with the pending groups: lane
+    // g < ngroups holds the global row of group g; runs of groups with
+    // consecutive rows become power-of-two boxes issued by their first lane.
+    auto fill_slot = [&](int item, const CUtensorMap* hmaps, int grow, int ngroups) {
+      const int sl = item % kSlots, fill = item / kSlots;
+      if (ok && fill > 0) ok = mbar_wait_warp(&sh.slot_empty[sl], (fill - 1) & 1, abort_flag, args.status);
+      if (!ok) return;
+      if (lane == 0) mbar_arrive_expect_tx(&sh.slot_full[sl], static_cast<uint32_t>(ngroups) * kGroup * D * 2);
+      __syncwarp();
+      const int prev = __shfl_up_sync(0xffffffffu, grow, 1);
+      const bool cont = lane > 0 && lane < ngroups && grow == prev + kGroup;
+      const unsigned cmask = __ballot_sync(0xffffffffu, cont);
+      if (lane < ngroups && !cont) {
+        // this lane starts a segment: count its groups, then issue its boxes
+        int n = 1;
+        while (lane + n < ngroups && ((cmask >> (lane + n)) & 1u)) ++n;
+        int g = lane, row = grow;
+        for (int h = kHeights - 1; h >= 0; --h) {
+          const int cnt = 1 << h;
+          while (n >= cnt) {
+            unsigned char* dst = base + L::kSlot0 + sl * L::kTileBytes + g * (kGroup * 128);
+#pragma unroll
+            for (int p = 0; p < D / 64; ++p) tma_load_2d(dst + p * L::kPanel, &hmaps[h], 64 * p, row, &sh.slot_full[sl]);
+            g += cnt;
+            row += cnt * kGroup;
+            n -= cnt;
+          }
+        }
+      }
+      __syncwarp();
     };
     for (;;) {
       // ---- claim a unit
@@ -313,72 +357,50 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
       const uint8_t* map_row = args.map + (static_cast<long long>(head) * args.gq + qg) * args.gk;
       const long long krow0 = static_cast<long long>(head) * args.sk;
 
-      // ---- stream the unit's key runs as 8-row boxes grouped into tiles
-      int box_row = 0, box_valid = 0;  // lane b holds box b of the pending tile
-      int nbox = 0;
+      // ---- stream the unit's key runs as 8-row groups grouped into tiles
+      int grow = 0, gvalid = 0;  // lane g holds group g of the pending tile
+      int ngroups = 0;
       int utiles = 0;
       int run_s = 0, run_e = 0;
       bool have_run = false;
       auto emit_tile = [&](bool last) {
-        if (lane >= nbox && lane < kBoxes) {  // padding boxes: in-bounds rows, fully masked
-          box_row = static_cast<int>(krow0);
-          box_valid = 0;
-        }
+        fill_slot(2 * tile, maps.k, grow, ngroups);
+        fill_slot(2 * tile + 1, maps.v, grow, ngroups);
         if (utiles == 0) {
-          // first tile of a non-empty unit: load its Q tile
-          const int qs = qunits & 1;
-          if (ok && qunits >= 2) ok = mbar_wait_warp(&sh.q_empty[qs], ((qunits >> 1) - 1) & 1, abort_flag, args.status);
+          // first tile of a non-empty unit: its Q tile, once the previous
+          // unit's last QK has released the buffer (its K/V are already in flight)
+          if (ok && qloads > 0) ok = mbar_wait_warp(&sh.q_empty, (qloads - 1) & 1, abort_flag, args.status);
           if (lane == 0 && ok) {
-            mbar_arrive_expect_tx(&sh.q_full[qs], L::kTileBytes);
+            mbar_arrive_expect_tx(&sh.q_full, L::kTileBytes);
 #pragma unroll
             for (int p = 0; p < D / 64; ++p)
-              tma_load_2d(base + L::kQ0 + qs * L::kTileBytes + p * L::kQPanel, &tmap_q, 64 * p,
-                          static_cast<int>(static_cast<long long>(head) * args.sq + q_start), &sh.q_full[qs]);
+              tma_load_2d(base + L::kQ0 + p * L::kPanel, &maps.q, 64 * p,
+                          static_cast<int>(static_cast<long long>(head) * args.sq + q_start), &sh.q_full);
           }
           __syncwarp();
-          ++qunits;
+          ++qloads;
         }
-        const unsigned bits = (box_valid >= 8) ? 0xffu : ((1u << box_valid) - 1u);
+        const unsigned bits = lane < ngroups ? ((gvalid >= 8) ? 0xffu : ((1u << gvalid) - 1u)) : 0u;
         uint32_t word[4] = {0, 0, 0, 0};
 #pragma unroll
-        for (int b = 0; b < kBoxes; ++b) word[b >> 2] |= __shfl_sync(0xffffffffu, bits, b) << (8 * (b & 3));
+        for (int b = 0; b < kGroups; ++b) word[b >> 2] |= __shfl_sync(0xffffffffu, bits, b) << (8 * (b & 3));
         push_info(word, static_cast<int>(v), (utiles == 0 ? kFirst : 0u) | (last ? kLast : 0u));
-        const int st = tile % kStages;
-        const uint32_t ph = ((tile / kStages) - 1) & 1;
-        if (ok && tile >= kStages) ok = mbar_wait_warp(&sh.k_empty[st], ph, abort_flag, args.status);
-        if (lane == 0 && ok) mbar_arrive_expect_tx(&sh.k_full[st], L::kTileBytes);
-        __syncwarp();
-        if (ok && lane < kBoxes) {
-#pragma unroll
-          for (int p = 0; p < D / 64; ++p)
-            tma_load_2d(base + L::kK0 + st * L::kTileBytes + lane * L::kBoxBytes + p * 1024, &tmap_k, 64 * p, box_row,
-                        &sh.k_full[st]);
-        }
-        if (ok && tile >= kStages) ok = mbar_wait_warp(&sh.v_empty[st], ph, abort_flag, args.status);
-        if (lane == 0 && ok) mbar_arrive_expect_tx(&sh.v_full[st], L::kTileBytes);
-        __syncwarp();
-        if (ok && lane < kBoxes) {
-#pragma unroll
-          for (int p = 0; p < D / 64; ++p)
-            tma_load_2d(base + L::kV0 + st * L::kTileBytes + lane * L::kBoxBytes + p * 1024, &tmap_v, 64 * p, box_row,
-                        &sh.v_full[st]);
-        }
         ++tile;
         ++utiles;
-        nbox = 0;
+        ngroups = 0;
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
         if (lane == 0) ATTN_TRACE(1, 0x100u + tile);
       };
-      auto add_box = [&](int row, int valid) {
-        if (nbox == kBoxes) emit_tile(false);
-        if (lane == nbox) {
-          box_row = row;
-          box_valid = valid;
+      auto add_group = [&](int row, int valid) {
+        if (ngroups == kGroups) emit_tile(false);
+        if (lane == ngroups) {
+          grow = row;
+          gvalid = valid;
         }
-        ++nbox;
+        ++ngroups;
       };
       auto flush_run = [&]() {
-        for (int r = run_s; r < run_e && ok; r += kBox) add_box(static_cast<int>(krow0 + r), min(kBox, run_e - r));
+        for (int r = run_s; r < run_e && ok; r += kGroup) add_group(static_cast<int>(krow0 + r), min(kGroup, run_e - r));
       };
       for (int c0 = 0; c0 < args.gk && ok; c0 += 32) {
         const int c = c0 + lane;
@@ -409,7 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
       }
       if (have_run && ok) flush_run();
       if (!ok) break;
-      if (utiles == 0 && nbox == 0) {
+      if (utiles == 0 && ngroups == 0) {
         const uint32_t zero[4] = {0, 0, 0, 0};
         push_info(zero, static_cast<int>(v), kEmpty);  // no key at all: rows are zero
       } else {
@@ -425,25 +447,25 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
       constexpr uint32_t idesc_qk = instr_desc(128, kBN, AB, false, false);
       constexpr uint32_t idesc_pv = instr_desc(128, D, AB, false, true);
       bool ok = true;
-      int entry = 0, t = 0, qunits = 0, ounits = 0;
+      int entry = 0, t = 0, qloads = 0, ounits = 0;
       int cur = -1;           // tile whose P.V is pending
       uint32_t cur_flags = 0;
       int cur_oslot = 0;
       auto issue_pv = [&]() {
-        const int b = cur & 1, st = cur % kStages;
+        const int b = cur & 1, item = 2 * cur + 1, sl = item % kSlots;
         ok = mbar_wait(&sh.p_full[b], (cur >> 1) & 1, abort_flag, args.status);
-        if (ok) ok = mbar_wait(&sh.v_full[st], (cur / kStages) & 1, abort_flag, args.status);
+        if (ok) ok = mbar_wait(&sh.slot_full[sl], (item / kSlots) & 1, abort_flag, args.status);
         if (!ok) return;
         tc_fence_after();
-        const uint32_t va = smem_u32(base + L::kV0 + st * L::kTileBytes);
+        const uint32_t va = smem_u32(base + L::kSlot0 + sl * L::kTileBytes);
         const uint32_t o_addr = tmem + 256 + cur_oslot * 128;
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint64_t bdesc = smem_desc(va + kk * 2 * L::kBoxBytes, 1024, L::kBoxBytes);
+          const uint64_t bdesc = smem_desc(va + kk * 2 * 1024, L::kPanel, 1024);
           umma_ts(o_addr, tmem + b * 128 + kk * 8, bdesc, idesc_pv, ((cur_flags & kFirst) && kk == 0) ? 0u : 1u);
         }
         umma_commit(&sh.s_free[b]);
-        umma_commit(&sh.v_empty[st]);
+        umma_commit(&sh.slot_empty[sl]);
         if (cur_flags & kLast) umma_commit(&sh.o_full[cur_oslot]);
         ATTN_TRACE(2, 0x200u + cur);
       };
@@ -457,27 +479,26 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
         if (fl & kEnd) break;
         if (fl & kEmpty) continue;
         // ---- S[t%2] = Q K^T for the next tile
-        const int b = t & 1, st = t % kStages;
-        ok = mbar_wait(&sh.k_full[st], (t / kStages) & 1, abort_flag, args.status);
-        if (ok && t >= 2) ok = mbar_wait(&sh.s_free[b], ((t >> 1) - 1) & 1, abort_flag, args.status);
-        const int qs = (fl & kFirst) ? (qunits & 1) : ((qunits - 1) & 1);
-        if (ok && (fl & kFirst)) {
-          ok = mbar_wait(&sh.q_full[qs], (qunits >> 1) & 1, abort_flag, args.status);
-          ++qunits;
+        const int b = t & 1, item = 2 * t, sl = item % kSlots;
+        if (fl & kFirst) {
+          ok = mbar_wait(&sh.q_full, qloads & 1, abort_flag, args.status);
+          ++qloads;
         }
+        if (ok) ok = mbar_wait(&sh.slot_full[sl], (item / kSlots) & 1, abort_flag, args.status);
+        if (ok && t >= 2) ok = mbar_wait(&sh.s_free[b], ((t >> 1) - 1) & 1, abort_flag, args.status);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t qa = smem_u32(base + L::kQ0 + qs * L::kTileBytes);
-        const uint32_t ka = smem_u32(base + L::kK0 + st * L::kTileBytes);
+        const uint32_t qa = smem_u32(base + L::kQ0);
+        const uint32_t ka = smem_u32(base + L::kSlot0 + sl * L::kTileBytes);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t adesc = smem_desc(qa + (kk >> 2) * L::kQPanel + (kk & 3) * 32, 16, 1024);
-          const uint64_t bdesc = smem_desc(ka + (kk >> 2) * 1024 + (kk & 3) * 32, 16, L::kBoxBytes);
-          umma_ss(tmem + b * 128, adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
+          const uint32_t off = (kk >> 2) * L::kPanel + (kk & 3) * 32;
+          umma_ss(tmem + b * 128, smem_desc(qa + off, 16, 1024), smem_desc(ka + off, 16, 1024), idesc_qk,
+                  kk > 0 ? 1u : 0u);
         }
         umma_commit(&sh.s_full[b]);
-        umma_commit(&sh.k_empty[st]);
-        if (fl & kLast) umma_commit(&sh.q_empty[qs]);
+        umma_commit(&sh.slot_empty[sl]);
+        if (fl & kLast) umma_commit(&sh.q_empty);
         ATTN_TRACE(2, 0x100u + t);
         // ---- O += P V for the previous tile
         if (cur >= 0) {
@@ -678,17 +699,19 @@ int num_sms() {
 
 template <int D, int AB>
 int launch_main(const void* q, const void* k, const void* v, const AttnArgs& a, cudaStream_t stream) {
-  CUtensorMap tq, tk, tv;
-  if (!make_rows_map(&tq, q, static_cast<long long>(a.bh) * a.sq, D, kBM, AB) ||
-      !make_rows_map(&tk, k, static_cast<long long>(a.bh) * a.sk, D, kBox, AB) ||
-      !make_rows_map(&tv, v, static_cast<long long>(a.bh) * a.sk, D, kBox, AB))
-    return kErrTensorMap;
+  AttnMaps maps;
+  if (!make_rows_map(&maps.q, q, static_cast<long long>(a.bh) * a.sq, D, kBM, AB)) return kErrTensorMap;
+  for (int h = 0; h < kHeights; ++h) {
+    if (!make_rows_map(&maps.k[h], k, static_cast<long long>(a.bh) * a.sk, D, kGroup << h, AB) ||
+        !make_rows_map(&maps.v[h], v, static_cast<long long>(a.bh) * a.sk, D, kGroup << h, AB))
+      return kErrTensorMap;
+  }
   const int smem = Layout<D>::kSmem;
   cudaError_t e = cudaFuncSetAttribute(sparse_attention_tc<D, AB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return static_cast<int>(e);
   const long long total = static_cast<long long>(a.bh) * a.max_units;
   const int grid = static_cast<int>(total < num_sms() ? total : num_sms());
-  sparse_attention_tc<D, AB><<<grid, kThreads, smem, stream>>>(tq, tk, tv, a);
+  sparse_attention_tc<D, AB><<<grid, kThreads, smem, stream>>>(maps, a);
   return launch_status();
 }
 
