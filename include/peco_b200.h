@@ -64,7 +64,9 @@ const char* peco_cluster_error_message(int code);
 /* Cluster-masked softmax(QK^T/sqrt(D))V over group-packed Q [BH,SQ,D] and
  * K/V [BH,SK,D]; map [BH,CQ,CK] bytes, sizes int32 [BH,CQ]/[BH,CK]; rows with
  * no allowed key -> 0.  dtype 0 = fp16, 1 = bf16; D in {64,128}.  Workspace:
- * int32 BH*(CK+2+3*(ceil(SQ/16)+CQ)) (the reference's size).
+ * int32 BH*(CK+2+3*(ceil(SQ/16)+CQ)) (the reference's size), accepted for
+ * ABI compatibility: the plan and key blocks (peco_attention_plan,
+ * peco_pack_key_blocks) live in stream-ordered scratch of the call.
  * Replaces peco/kernels/sparse_attention.cu:210-230 (bound at peco/attention_cuda.py:57,130-137). */
 int peco_sparse_attention(const void* q, const void* k, const void* v, const uint8_t* selected,
                           const int* q_sizes, const int* k_sizes, void* output, int* workspace, int bh, int sq,
@@ -121,28 +123,51 @@ int peco_base_offset(int mode, const void* x, const int32_t* labels, const float
                      uint8_t* codes, float* offset_min, float* scale, int bh, int tokens, int dims, int clusters,
                      int bits, int dtype, void* stream);
 
+/* Attention plan (workspace: int32 bh * peco_attention_workspace_stride),
+ * from the group map [BH,GQ,GK] and sizes [BH,GQ]/[BH,GK] (extents clamped
+ * like peco/kernels/sparse_attention.cu:25-31): the work units (<= 128 query
+ * rows of one query group), the key-row -> key-block map and, per unit, the
+ * selected key clusters.  Key blocks hold K or V as 8-row blocks of 8*D
+ * 16-bit elements in the tensor core's shared-memory image (D/64 panels of
+ * 8 rows x 128 bytes, 16-byte chunk c of row i at chunk c^i); each key
+ * cluster starts a new block.  When k_blocks/v_blocks ([BH,
+ * peco_key_block_rows(sk, gk), D]) are given, the padding rows of every
+ * cluster's last block are zeroed.  Splits the planning half of
+ * peco/kernels/sparse_attention.cu:17-52 out of the attention launch. */
+int peco_attention_plan(const uint8_t* map, const int* q_sizes, const int* k_sizes, void* k_blocks,
+                        void* v_blocks, int* workspace, int bh, int sq, int sk, int d, int gq, int gk,
+                        void* stream);
+
+long long peco_attention_workspace_stride(int sq, int sk, int gq, int gk);
+long long peco_key_block_rows(int sk, int gk);
+
+/* Row-major K/V [BH,SK,D] -> key blocks through a plan.  Used by the drop-in
+ * peco_sparse_attention (which plans and packs internally). */
+int peco_pack_key_blocks(const void* k, const void* v, void* k_blocks, void* v_blocks, const int* workspace,
+                         int bh, int sq, int sk, int d, int gq, int gk, void* stream);
+
 /* One pass over bf16 Q/K/V [BH,S,D] (video tokens first): packed row j of
  * each head takes source video row indices[j] -- Base-Offset fake quantized
  * for Q and K when bits > 0, copied for V (which uses K's indices) -- and
- * text rows j >= video are copied in place.  Replaces
- * peco/processor.py:141-149 (fake quant, three gathers and the concats). */
+ * text rows j >= video are copied in place.  With ``plan`` (a workspace
+ * written by peco_attention_plan with sq = sk = seq), K and V rows go to
+ * key blocks (k_packed/v_packed [BH, peco_key_block_rows(seq, gk), D])
+ * instead of row-major [BH,S,D].  Replaces peco/processor.py:141-149 (fake
+ * quant, three gathers and the concats). */
 int peco_quantize_gather(const void* q, const void* k, const void* v, void* q_packed, void* k_packed,
                          void* v_packed, const int32_t* q_indices, const int32_t* k_indices,
                          const int32_t* q_labels, const int32_t* k_labels, const float* q_centroids,
                          const float* k_centroids, int q_clusters, int k_clusters, int bh, int seq, int video,
-                         int dims, int bits, void* stream);
+                         int dims, int bits, const int* plan, int gq, int gk, void* stream);
 
-/* Sparse attention over packed bf16 Q/K/V whose output rows are scattered
- * through the inverse permutation: packed row j < video goes to row
- * q_indices[j] of ``output``, text rows stay in place.  Workspace: int32
- * bh * peco_attention_workspace_stride(sq, gq, gk).
+/* Sparse attention of packed bf16 Q [BH,SQ,D] over key blocks, following a
+ * plan from peco_attention_plan; output rows are scattered through the
+ * inverse permutation: packed row j < video goes to row q_indices[j] of
+ * ``output`` (q_indices null: no scatter), text rows stay in place.
  * Fuses peco/kernels/sparse_attention.cu with peco/clustering.py:127-136. */
-int peco_sparse_attention_restore(const void* q, const void* k, const void* v, const uint8_t* map,
-                                  const int* q_sizes, const int* k_sizes, void* output, int* workspace, int bh,
-                                  int sq, int sk, int d, int gq, int gk, const int32_t* q_indices, int video,
-                                  void* stream);
-
-long long peco_attention_workspace_stride(int sq, int gq, int gk);
+int peco_sparse_attention_restore(const void* q, const void* k_blocks, const void* v_blocks,
+                                  const int* workspace, void* output, int bh, int sq, int sk, int d, int gq,
+                                  int gk, const int32_t* q_indices, int video, void* stream);
 
 /* ---- diagnostics --------------------------------------------------------- */
 

@@ -32,9 +32,12 @@ _SIGNATURES = {
     "peco_select_cluster_connections": [P] * 5 + [I] * 4 + [F, I, P],
     "peco_select_text_partition": [P] * 7 + [I] * 4 + [F, I, I, I, P],
     "peco_base_offset": [I] + [P] * 7 + [I] * 6 + [P],
-    "peco_quantize_gather": [P] * 12 + [I] * 7 + [P],
-    "peco_sparse_attention_restore": [P] * 8 + [I] * 6 + [P, I, P],
-    "peco_attention_workspace_stride": [I, I, I],
+    "peco_quantize_gather": [P] * 12 + [I] * 7 + [P, I, I, P],
+    "peco_attention_plan": [P] * 6 + [I] * 6 + [P],
+    "peco_pack_key_blocks": [P] * 5 + [I] * 6 + [P],
+    "peco_sparse_attention_restore": [P] * 5 + [I] * 6 + [P, I, P],
+    "peco_attention_workspace_stride": [I, I, I, I],
+    "peco_key_block_rows": [I, I],
     "peco_device_status": [P, I, P],
     "peco_error_string": [I],
     "peco_cluster_error_message": [I],
@@ -45,6 +48,7 @@ _SIGNATURES = {
 _RESTYPES = {
     "peco_launch_count": ctypes.c_ulonglong,
     "peco_attention_workspace_stride": LL,
+    "peco_key_block_rows": LL,
     "peco_error_string": ctypes.c_char_p,
     "peco_cluster_error_message": ctypes.c_char_p,
     "peco_attention_error_string": ctypes.c_char_p,

@@ -83,3 +83,28 @@ def sparse_attention(q, k, v, dynamic_map, q_sizes, k_sizes, *, validate_sizes: 
             msg = lib.peco_attention_error_string(int(status)).decode("utf-8", errors="replace")
             raise RuntimeError(f"PECO CUDA sparse attention launch failed: {msg} ({status})")
         return output
+
+
+def plan_key_blocks(dynamic_map, q_sizes, k_sizes, sq, k, v):
+    """Plan a fused attention call and pack row-major K/V [B,H,SK,D] into key
+    blocks: returns (workspace, k_blocks, v_blocks) for
+    ``peco_sparse_attention_restore``.  The same steps the drop-in
+    ``sparse_attention`` takes internally, exposed for callers that keep the
+    plan (and tests of the fused entry points)."""
+    batch, heads, sk, dim = k.shape
+    bh = batch * heads
+    gq, gk = q_sizes.shape[-1], k_sizes.shape[-1]
+    lib = _native.load()
+    with torch.cuda.device(k.device):
+        ws = torch.empty(bh * int(lib.peco_attention_workspace_stride(sq, sk, gq, gk)), dtype=torch.int32,
+                         device=k.device)
+        kb = torch.empty((bh, int(lib.peco_key_block_rows(sk, gk)), dim), dtype=k.dtype, device=k.device)
+        vb = torch.empty_like(kb)
+        stream = _native.stream_of(k.device, dynamic_map, q_sizes, k_sizes, k, v, ws, kb, vb)
+        _native.check(lib.peco_attention_plan(_native.ptr(dynamic_map), _native.ptr(q_sizes), _native.ptr(k_sizes),
+                                              _native.ptr(kb), _native.ptr(vb), _native.ptr(ws), bh, sq, sk, dim, gq,
+                                              gk, stream), "peco_attention_plan")
+        _native.check(lib.peco_pack_key_blocks(_native.ptr(k), _native.ptr(v), _native.ptr(kb), _native.ptr(vb),
+                                               _native.ptr(ws), bh, sq, sk, dim, gq, gk, stream),
+                      "peco_pack_key_blocks")
+    return ws, kb, vb

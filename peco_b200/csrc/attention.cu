@@ -4,34 +4,37 @@
 // O = softmax(Q K^T / sqrt(D), masked by map[group(i), group(j)]) V, rows
 // with no allowed key -> 0.
 //
-// Work unit: up to 128 query rows of ONE query group (all rows of a unit
-// share one key set, so masking is per key column only).  For each unit the
-// selected key groups become contiguous runs of the group-packed K/V; every
-// run is padded to whole 8-row groups, 16 groups make a 128-key tile, and
-// consecutive groups of a run are fetched by one TMA box of 8, 16, 32, 64 or
-// 128 rows (rows past a run's end are masked).  Per tile t:
-//   S[t%2]  = Q K^T          tcgen05.mma, A = Q (smem), B = K tile (smem)
-//   P       = exp2(S*c - m)  4 softmax warps, thread = query row; online max
-//                            with lazy rescale of O (only when the max grows
-//                            by > 8 in log2 units); P overwrites S[t%2] in
-//                            TMEM as 16-bit pairs
-//   O[u%2] += P V            tcgen05.mma, A = P (TMEM), B = V tile (smem, MN-major)
+// Three kernels:
+//  * planner (one CTA per head): clamped cluster prefixes, the work units
+//    (up to 128 query rows of ONE query group, so masking is per key column
+//    only), the key-row -> key-block map, zeroed padding rows of the key
+//    blocks, and per unit the list of selected key clusters as block ranges;
+//  * pack (drop-in path only): row-major K/V -> key blocks (internal.h).  The
+//    fused path writes key blocks straight from its quantise/gather kernel;
+//  * main kernel (persistent, one CTA per SM).  Per unit, the selected key
+//    blocks are concatenated and cut into 128-key tiles (16 blocks); a run of
+//    consecutive blocks is ONE bulk copy.  Per tile t:
+//      S[t%2]  = Q K^T         tcgen05.mma, A = Q (smem), B = K blocks (smem)
+//      P       = exp2(S*c - m) 8 softmax warps: a query row is shared by two
+//                              warps, each owning 64 key columns with its own
+//                              running max (lazy rescale: only when it grows by
+//                              > 8 in log2 units) and sum; P overwrites its half
+//                              of S[t%2] in TMEM as 16-bit pairs
+//      O_h    += P_h V_h       tcgen05.mma, A = P half h (TMEM), B = the V blocks
+//                              of that half (smem, MN-major); O_0 and O_1 are
+//                              separate accumulators
+//    The epilogue merges the halves, O = (O_0 2^(m_0-M) + O_1 2^(m_1-M)) / L,
+//    and can scatter rows through an inverse permutation (fusing
+//    peco/clustering.py:127-136 into the output store).
 // The MMA issuer runs one tile ahead (QK of tile t+1 before PV of tile t), so
 // the tensor core computes the next scores while the softmax warps work on the
-// current ones.  K and V tiles stream through a 6-slot ring (three tiles in
-// flight), and O is double-buffered so a unit's epilogue overlaps the next
-// unit's MMAs.
+// current ones.  K and V stream through a 6-slot ring (three tiles in flight).
 //
-// CTAs are persistent (one per SM) and take units heaviest-first: the
-// planner lists every head's text groups (which attend to every key) before
-// its video clusters, and CTAs claim (unit, head) pairs in unit-major order
-// from a work counter in the workspace.
-//
-// Warp roles: warp 0 = TMA producer and scheduler, warp 1 = MMA issuer (one
-// thread) and TMEM owner, warps 2-5 = softmax + epilogue.  The epilogue can
-// scatter rows through an inverse permutation (fusing peco/clustering.py:
-// 127-136 into the output store).  Every wait is bounded (common.cuh); on
-// expiry the CTA records kDevTimeout in the device status word and unwinds.
+// Warp roles: warp 0 = producer (unit claims, bulk copies, tile masks), warp
+// 1 = MMA issuer (one thread) and TMEM owner, warps 2-9 = softmax + epilogue.
+// CTAs claim units from a work counter, every head's text groups first.
+// Every wait is bounded (common.cuh); on expiry the CTA records kDevTimeout in
+// the device status word and unwinds.
 #include "common.cuh"
 #include "../../include/peco_b200.h"
 #include "internal.h"
@@ -39,61 +42,35 @@
 namespace peco {
 namespace {
 
-constexpr int kBM = 128;       // query rows per unit
-constexpr int kBN = 128;       // keys per tile
-constexpr int kGroup = 8;      // rows per key group (the padding granule)
-constexpr int kGroups = kBN / kGroup;
-constexpr int kSlots = 6;      // K/V ring: slot of K(t) = 2t mod 6, V(t) = 2t+1 mod 6
-constexpr int kRing = 8;       // tile-info ring depth
-constexpr int kThreads = 192;  // 6 warps
-constexpr int kHeights = 5;    // TMA box heights 8 << h rows, h = 0..4
-constexpr uint32_t kTmemCols = 512;  // S0 | S1 | O0 | O1, 128 columns each
+constexpr int kBM = kUnitRows;   // query rows per unit
+constexpr int kBN = 128;         // keys per tile
+constexpr int kTileBlocks = kBN / kKeyBlockRows;
+constexpr int kSlots = 6;        // K/V ring: slot of K(t) = 2t mod 6, V(t) = 2t+1 mod 6
+constexpr int kRing = 8;         // tile-info ring depth
+constexpr int kSoftmaxWarps = 8;
+constexpr int kThreads = 32 * (2 + kSoftmaxWarps);
+constexpr uint32_t kTmemCols = 512;  // S0 | S1 | O_0 | O_1, 128 columns each
 
 // tile-info flags
 constexpr uint32_t kFirst = 1u, kLast = 2u, kEmpty = 4u, kEnd = 8u;
 
-#ifdef PECO_ATTN_TRACE
-// Debug builds record per-CTA progress: trace[cta*8 + slot] = value.
-#define ATTN_TRACE(slot, value)                                                                   \
-  do {                                                                                            \
-    if (args.trace) {                                                                             \
-      volatile unsigned* t_ = args.trace + static_cast<long long>(blockIdx.x) * 8;                \
-      t_[slot] = (value);                                                                         \
-      __threadfence_system();                                                                     \
-    }                                                                                             \
-  } while (0)
-#else
-#define ATTN_TRACE(slot, value) \
-  do {                          \
-  } while (0)
-#endif
-
 struct AttnArgs {
-#ifdef PECO_ATTN_TRACE
-  unsigned* trace;
-#endif
-  const uint8_t* map;      // [BH, GQ, GK]
-  int* ws;                 // planner output, ws_stride ints per head
-  void* out;               // [BH, out_rows, D]
-  const int32_t* perm;     // optional [BH, video] inverse permutation for packed rows < video
-  int bh, sq, sk, gq, gk, ws_stride, max_units;
-  int out_rows;            // rows per head of the output tensor
-  int video;               // packed rows below this index go through perm
-  int dynamic_sched;       // claim units from the work counter (else a static stride)
-  float scale_log2;        // log2(e) / sqrt(D)
+  const int* ws;              // plan workspace
+  const unsigned char* kb;    // key blocks
+  const unsigned char* vb;    // value blocks
+  void* out;                  // [BH, out_rows, D]
+  const int32_t* perm;        // optional [BH, video] inverse permutation for packed rows < video
+  PlanGeom g;
+  int bh;
+  int out_rows;               // rows per head of the output tensor
+  int video;                  // packed rows below this index go through perm
+  float scale_log2;           // log2(e) / sqrt(D)
   unsigned* status;
 };
 
-// TMA descriptors: Q (128-row boxes) and K/V with box heights 8 << h.
-struct AttnMaps {
-  CUtensorMap q;
-  CUtensorMap k[kHeights];
-  CUtensorMap v[kHeights];
-};
-
 struct TileInfo {
-  uint32_t mask[4];        // key rows of the tile that are valid
-  int unit;                // virtual unit index (local * BH + head)
+  uint32_t mask[4];           // key columns of the tile that are valid
+  int unit;                   // virtual unit index (local * BH + head)
   uint32_t flags;
 };
 
@@ -101,19 +78,22 @@ struct __align__(8) Shared {
   uint64_t q_full, q_empty;
   uint64_t slot_full[kSlots], slot_empty[kSlots];
   uint64_t s_full[2], s_free[2], p_full[2];
-  uint64_t o_full[2], o_free[2];
+  uint64_t o_full;
+  uint64_t xch_full[4], xch_back[4];   // epilogue hand-off between the two warps of a row quarter
   uint64_t info_full[kRing], info_empty[kRing];
   TileInfo info[kRing];
+  float2 xch[kBM];
   uint32_t tmem_base;
   int abort_flag;
 };
 
-// Operand tiles (Q, K, V) share one layout: two 64-column panels of 128 rows
-// x 128 bytes (16 KB each, 128-byte swizzle), 8-row groups 1 KB apart.
+// Q: D/64 panels of 128 rows x 128 bytes (128-byte swizzle, 8-row groups 1 KB
+// apart).  K/V slots: 16 key blocks of 8 * D * 2 bytes.
 template <int D>
 struct Layout {
   static constexpr int kTileBytes = kBN * D * 2;
-  static constexpr int kPanel = kBN * 128;
+  static constexpr int kBlockBytes = kKeyBlockRows * D * 2;
+  static constexpr int kQPanel = kBM * 128;
   static constexpr int kQ0 = 0;
   static constexpr int kSlot0 = kTileBytes;
   static constexpr int kShared = kSlot0 + kSlots * kTileBytes;
@@ -121,17 +101,12 @@ struct Layout {
 };
 
 __device__ __forceinline__ int* work_counter(const AttnArgs& a) {
-  return a.ws + static_cast<long long>(a.bh - 1) * a.ws_stride + (a.ws_stride - 1);
+  return const_cast<int*>(a.ws) + static_cast<long long>(a.bh - 1) * a.g.stride + (a.g.stride - 1);
 }
 
 // ---------------------------------------------------------------------------
-// planner: clamped group prefixes and the unit list of every head
+// planner
 // ---------------------------------------------------------------------------
-// ws per head: [0] = unit count, [1 .. gk+1] = key group starts, then
-// 3 ints per unit (q_start, q_count, q_group).  Group extents are clamped the
-// way the reference's work map clamps them (sparse_attention.cu:25-31):
-// start_g = min(S, sum_{g'<g} max(0, size_g')).  Units of later groups come
-// first, so the text groups (which attend to every key) start early.
 __device__ long long block_exclusive_scan(long long v, long long* tmp) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   long long incl = v;
@@ -157,79 +132,197 @@ __device__ long long block_exclusive_scan(long long v, long long* tmp) {
   return tmp[warp] + incl - v;
 }
 
-// dynamic smem: 2 * gq ints (clamped start and size of every query group)
-__global__ void __launch_bounds__(1024) attn_plan_kernel(const int* __restrict__ q_sizes, const int* __restrict__ k_sizes,
-                                                         int* __restrict__ ws, int gq, int gk, int sq, int sk,
-                                                         int ws_stride, int zero_counter) {
+// Group extents are clamped the way the reference's work map clamps them
+// (sparse_attention.cu:25-31): start_g = min(S, sum_{g'<g} max(0, size_g')).
+// Units of later query groups come first, so the text groups (which attend to
+// every key) start early.  Dynamic smem: 2 (gk + 1) + 2 gq + max_units ints.
+__global__ void __launch_bounds__(1024) attn_plan_kernel(const uint8_t* __restrict__ map,
+                                                         const int* __restrict__ q_sizes,
+                                                         const int* __restrict__ k_sizes, int* __restrict__ ws,
+                                                         const PlanGeom g, unsigned char* k_blocks,
+                                                         unsigned char* v_blocks, int block_bytes) {
   extern __shared__ int plan_sm[];
-  int* gstart = plan_sm;
-  int* gcount = plan_sm + gq;
+  int* skp = plan_sm;
+  int* sgp = skp + g.gk + 1;
+  int* gstart = sgp + g.gk + 1;
+  int* gcount = gstart + g.gq;
+  int* ugroup = gcount + g.gq;
   __shared__ long long tmp[32];
-  __shared__ long long carry;
+  __shared__ long long carry[2];
+  __shared__ int n_units;
   const int head = blockIdx.x;
-  int* w = ws + static_cast<long long>(head) * ws_stride;
-  int* kp = w + 1;
-  int* units = w + 2 + gk;
-  const int* qs = q_sizes + static_cast<long long>(head) * gq;
-  const int* ks = k_sizes + static_cast<long long>(head) * gk;
-  const int last = blockDim.x - 1;
-  if (threadIdx.x == 0) {
-    carry = 0;
-    kp[0] = 0;
-    // work counter of the persistent attention kernel (last int of the last head)
-    if (zero_counter && head == gridDim.x - 1) w[ws_stride - 1] = 0;
+  const int tid = threadIdx.x, last = blockDim.x - 1;
+  const int lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  int* w = ws + static_cast<long long>(head) * g.stride;
+  const int* qs = q_sizes + static_cast<long long>(head) * g.gq;
+  const int* ks = k_sizes + static_cast<long long>(head) * g.gk;
+  if (tid == 0) {
+    carry[0] = carry[1] = 0;
+    skp[0] = 0;
+    sgp[0] = 0;
+    if (head == gridDim.x - 1) w[g.stride - 1] = 0;  // work counter
   }
   __syncthreads();
-  for (int c0 = 0; c0 < gk; c0 += blockDim.x) {
-    const int c = c0 + threadIdx.x;
-    const long long v = c < gk ? max(0, ks[c]) : 0;
-    const long long pre = carry + block_exclusive_scan(v, tmp);
-    if (c < gk) kp[c + 1] = static_cast<int>(min(static_cast<long long>(sk), pre + v));
-    __syncthreads();
-    if (threadIdx.x == last) carry = pre + v;
-    __syncthreads();
-  }
-  if (threadIdx.x == 0) carry = 0;
-  __syncthreads();
-  for (int g0 = 0; g0 < gq; g0 += blockDim.x) {
-    const int g = g0 + threadIdx.x;
-    const long long v = g < gq ? max(0, qs[g]) : 0;
-    const long long pre = carry + block_exclusive_scan(v, tmp);
-    if (g < gq) {
-      const long long s0 = min(static_cast<long long>(sq), pre), s1 = min(static_cast<long long>(sq), pre + v);
-      gstart[g] = static_cast<int>(s0);
-      gcount[g] = static_cast<int>(s1 - s0);
+  // key clusters: clamped row prefix and block prefix
+  for (int c0 = 0; c0 < g.gk; c0 += blockDim.x) {
+    const int c = c0 + tid;
+    const long long v = c < g.gk ? max(0, ks[c]) : 0;
+    const long long pre = carry[0] + block_exclusive_scan(v, tmp);
+    const long long s0 = min(static_cast<long long>(g.sk), pre), s1 = min(static_cast<long long>(g.sk), pre + v);
+    const long long nb = (s1 - s0 + kKeyBlockRows - 1) / kKeyBlockRows;
+    const long long bpre = carry[1] + block_exclusive_scan(nb, tmp);
+    if (c < g.gk) {
+      skp[c + 1] = static_cast<int>(s1);
+      sgp[c + 1] = static_cast<int>(bpre + nb);
     }
     __syncthreads();
-    if (threadIdx.x == last) carry = pre + v;
+    if (tid == last) {
+      carry[0] = pre + v;
+      carry[1] = bpre + nb;
+    }
     __syncthreads();
   }
-  if (threadIdx.x == 0) carry = 0;
+  for (int c = tid; c <= g.gk; c += blockDim.x) {
+    w[g.off_kp + c] = skp[c];
+    w[g.off_gp + c] = sgp[c];
+  }
+  // query groups -> units
+  if (tid == 0) carry[0] = 0;
   __syncthreads();
-  for (int o0 = 0; o0 < gq; o0 += blockDim.x) {
-    const int o = o0 + threadIdx.x;
-    const int g = gq - 1 - o;
-    const int n = o < gq ? gcount[g] : 0;
+  for (int g0 = 0; g0 < g.gq; g0 += blockDim.x) {
+    const int q = g0 + tid;
+    const long long v = q < g.gq ? max(0, qs[q]) : 0;
+    const long long pre = carry[0] + block_exclusive_scan(v, tmp);
+    if (q < g.gq) {
+      const long long s0 = min(static_cast<long long>(g.sq), pre), s1 = min(static_cast<long long>(g.sq), pre + v);
+      gstart[q] = static_cast<int>(s0);
+      gcount[q] = static_cast<int>(s1 - s0);
+    }
+    __syncthreads();
+    if (tid == last) carry[0] = pre + v;
+    __syncthreads();
+  }
+  if (tid == 0) carry[0] = 0;
+  __syncthreads();
+  int* units = w + g.off_units;
+  for (int o0 = 0; o0 < g.gq; o0 += blockDim.x) {
+    const int o = o0 + tid;
+    const int q = g.gq - 1 - o;
+    const int n = o < g.gq ? gcount[q] : 0;
     const long long nu = (n + kBM - 1) / kBM;
-    const long long u0 = carry + block_exclusive_scan(nu, tmp);
+    const long long u0 = carry[0] + block_exclusive_scan(nu, tmp);
     for (int i = 0; i < nu; ++i) {
-      int* rec = units + 3 * (u0 + i);
-      rec[0] = gstart[g] + i * kBM;
+      int* rec = units + 4 * (u0 + i);
+      rec[0] = gstart[q] + i * kBM;
       rec[1] = min(kBM, n - i * kBM);
-      rec[2] = g;
+      ugroup[u0 + i] = q;
     }
     __syncthreads();
-    if (threadIdx.x == last) carry = u0 + nu;
+    if (tid == last) carry[0] = u0 + nu;
     __syncthreads();
   }
-  if (threadIdx.x == 0) w[0] = static_cast<int>(carry);
+  if (tid == 0) {
+    n_units = static_cast<int>(carry[0]);
+    w[0] = n_units;
+  }
+  // key row -> row of the key-block image
+  int* rows = w + g.off_rows;
+  for (int j = tid; j < g.sk; j += blockDim.x) {
+    int lo = 0, hi = g.gk;  // largest c in [0, gk] with skp[c] <= j
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (skp[mid] <= j) lo = mid;
+      else hi = mid - 1;
+    }
+    rows[j] = lo < g.gk ? kKeyBlockRows * sgp[lo] + (j - skp[lo]) : -1;
+  }
+  // zero the padding rows of every cluster's last block
+  if (k_blocks) {
+    const int panels = block_bytes / 1024;
+    for (int idx = tid; idx < g.gk * kKeyBlockRows; idx += blockDim.x) {
+      const int c = idx / kKeyBlockRows, i = idx % kKeyBlockRows;
+      const int r = (skp[c + 1] - skp[c]) % kKeyBlockRows;
+      if (r == 0 || i < r) continue;
+      const long long off = (static_cast<long long>(head) * g.blocks + sgp[c + 1] - 1) * block_bytes + i * 128;
+      for (int p = 0; p < panels; ++p) {
+        uint4* kd = reinterpret_cast<uint4*>(k_blocks + off + p * 1024);
+        uint4* vd = reinterpret_cast<uint4*>(v_blocks + off + p * 1024);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          kd[e] = make_uint4(0, 0, 0, 0);
+          vd[e] = make_uint4(0, 0, 0, 0);
+        }
+      }
+    }
+  }
+  __syncthreads();
+  // per unit: the selected key clusters as entries over the unit's block list
+  int2* ent_all = reinterpret_cast<int2*>(w + g.off_ent);
+  for (int u = warp; u < n_units; u += nwarps) {
+    const int q = ugroup[u];
+    const uint8_t* mrow = map + (static_cast<long long>(head) * g.gq + q) * g.gk;
+    int2* ent = ent_all + static_cast<long long>(u) * g.gk;
+    int nent = 0, blocks = 0;
+    for (int c0 = 0; c0 < g.gk; c0 += 32) {
+      const int c = c0 + lane;
+      int n = 0, nb = 0;
+      if (c < g.gk) {
+        n = skp[c + 1] - skp[c];
+        if (n > 0 && mrow[c]) nb = sgp[c + 1] - sgp[c];
+      }
+      const unsigned bal = __ballot_sync(0xffffffffu, nb > 0);
+      int incl = nb;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+      }
+      if (nb > 0) {
+        const int pe = blocks + incl;
+        const int idx = nent + __popc(bal & ((1u << lane) - 1u));
+        ent[idx] = make_int2(sgp[c] - (pe - nb), (pe << 4) | (n - kKeyBlockRows * (nb - 1)));
+      }
+      nent += __popc(bal);
+      blocks += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) {
+      units[4 * u + 2] = nent;
+      units[4 * u + 3] = blocks;
+    }
+  }
+}
+
+// row-major K/V [BH, SK, D] -> key blocks (rows without a block are skipped)
+template <int D>
+__global__ void pack_key_blocks_kernel(const uint4* __restrict__ k, const uint4* __restrict__ v,
+                                       unsigned char* __restrict__ kb, unsigned char* __restrict__ vb,
+                                       const int* __restrict__ ws, const PlanGeom g, int bh, unsigned* status) {
+  constexpr int kChunks = D / 8;
+  const long long total = static_cast<long long>(bh) * g.sk * kChunks;
+  for (long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int chunk = static_cast<int>(idx % kChunks);
+    const long long row = idx / kChunks;
+    const int head = static_cast<int>(row / g.sk);
+    const int j = static_cast<int>(row - static_cast<long long>(head) * g.sk);
+    const int dst = ws[static_cast<long long>(head) * g.stride + g.off_rows + j];
+    if (dst < 0) continue;
+    if (dst >= g.blocks * kKeyBlockRows) {
+      if (chunk == 0) record_status(status, kDevBadIndex);
+      continue;
+    }
+    const long long off = (static_cast<long long>(head) * g.blocks + dst / kKeyBlockRows) * (kKeyBlockRows * D * 2) +
+                          key_block_offset(dst % kKeyBlockRows, chunk * 8);
+    *reinterpret_cast<uint4*>(kb + off) = k[idx];
+    *reinterpret_cast<uint4*>(vb + off) = v[idx];
+  }
 }
 
 // ---------------------------------------------------------------------------
 // main kernel (persistent)
 // ---------------------------------------------------------------------------
 template <int D, int AB>  // AB: 0 = fp16, 1 = bf16
-__global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_constant__ AttnMaps maps,
+__global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_constant__ CUtensorMap qmap,
                                                                   const AttnArgs args) {
   using L = Layout<D>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -237,7 +330,8 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
   Shared& sh = *reinterpret_cast<Shared*>(base + L::kShared);
   volatile int* abort_flag = &sh.abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long long total_units = static_cast<long long>(args.bh) * args.max_units;
+  const PlanGeom& g = args.g;
+  const long long total_units = static_cast<long long>(args.bh) * g.max_units;
 
   if (threadIdx.x == 0) {
     mbar_init(&sh.q_full, 1);
@@ -249,23 +343,25 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sh.s_full[i], 1);
       mbar_init(&sh.s_free[i], 1);
-      mbar_init(&sh.p_full[i], 4);
-      mbar_init(&sh.o_full[i], 1);
-      mbar_init(&sh.o_free[i], 4);
+      mbar_init(&sh.p_full[i], kSoftmaxWarps);
+    }
+    mbar_init(&sh.o_full, 1);
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&sh.xch_full[i], 1);
+      mbar_init(&sh.xch_back[i], 1);
     }
     for (int i = 0; i < kRing; ++i) {
       mbar_init(&sh.info_full[i], 1);
-      mbar_init(&sh.info_empty[i], 5);  // MMA thread + 4 softmax warps
+      mbar_init(&sh.info_empty[i], 1 + kSoftmaxWarps);
     }
     sh.abort_flag = 0;
     fence_barrier_init();
   }
-  // K/V rows of padding groups are never loaded: zero the ring once so the
+  // blocks past a tile's end are never loaded: zero the ring once so the
   // tensor core only ever sees finite values there
   for (int i = threadIdx.x; i < kSlots * L::kTileBytes / 16; i += blockDim.x)
     reinterpret_cast<uint4*>(base + L::kSlot0)[i] = make_uint4(0, 0, 0, 0);
   fence_async_smem();
-  if (threadIdx.x == 0) ATTN_TRACE(0, 1);
   if (warp == 1) {
     tmem_alloc(&sh.tmem_base, kTmemCols);
     tmem_relinquish();
@@ -276,18 +372,11 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
 
   if (warp == 0) {
     // ------------------------------------------------------- producer
-    if (lane == 0) {
-      prefetch_tensormap(&maps.q);
-      for (int h = 0; h < kHeights; ++h) {
-        prefetch_tensormap(&maps.k[h]);
-        prefetch_tensormap(&maps.v[h]);
-      }
-    }
+    if (lane == 0) prefetch_tensormap(&qmap);
     bool ok = true;
     int tile = 0;      // tiles issued by this CTA
     int entry = 0;     // info entries pushed
     int qloads = 0;    // Q tiles loaded
-    int claims = 0;
     auto push_info = [&](const uint32_t (&mask)[4], int unit, uint32_t flags) {
       const int slot = entry % kRing;
       if (ok && entry >= kRing) ok = mbar_wait_warp(&sh.info_empty[slot], ((entry / kRing) - 1) & 1, abort_flag, args.status);
@@ -304,139 +393,127 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
       __syncwarp();
       ++entry;
     };
-    // Fill ring item ``item`` (K or V of a tile) with the pending groups: lane
-    // g < ngroups holds the global row of group g; runs of groups with
-    // consecutive rows become power-of-two boxes issued by their first lane.
-    auto fill_slot = [&](int item, const CUtensorMap* hmaps, int grow, int ngroups) {
-      const int sl = item % kSlots, fill = item / kSlots;
-      if (ok && fill > 0) ok = mbar_wait_warp(&sh.slot_empty[sl], (fill - 1) & 1, abort_flag, args.status);
-      if (!ok) return;
-      if (lane == 0) mbar_arrive_expect_tx(&sh.slot_full[sl], static_cast<uint32_t>(ngroups) * kGroup * D * 2);
-      __syncwarp();
-      const int prev = __shfl_up_sync(0xffffffffu, grow, 1);
-      const bool cont = lane > 0 && lane < ngroups && grow == prev + kGroup;
-      const unsigned cmask = __ballot_sync(0xffffffffu, cont);
-      if (lane < ngroups && !cont) {
-        // this lane starts a segment: count its groups, then issue its boxes
-        int n = 1;
-        while (lane + n < ngroups && ((cmask >> (lane + n)) & 1u)) ++n;
-        int g = lane, row = grow;
-        for (int h = kHeights - 1; h >= 0; --h) {
-          const int cnt = 1 << h;
-          while (n >= cnt) {
-            unsigned char* dst = base + L::kSlot0 + sl * L::kTileBytes + g * (kGroup * 128);
-#pragma unroll
-            for (int p = 0; p < D / 64; ++p) tma_load_2d(dst + p * L::kPanel, &hmaps[h], 64 * p, row, &sh.slot_full[sl]);
-            g += cnt;
-            row += cnt * kGroup;
-            n -= cnt;
-          }
-        }
-      }
-      __syncwarp();
-    };
     for (;;) {
       // ---- claim a unit
-      long long v = 0;
-      if (args.dynamic_sched) {
-        int got = 0;
-        if (lane == 0) got = atomicAdd(work_counter(args), 1);
-        v = __shfl_sync(0xffffffffu, got, 0);
-      } else {
-        v = static_cast<long long>(blockIdx.x) + static_cast<long long>(claims) * gridDim.x;
-        ++claims;
-      }
+      int got = 0;
+      if (lane == 0) got = atomicAdd(work_counter(args), 1);
+      const long long v = __shfl_sync(0xffffffffu, got, 0);
       if (v >= total_units || !ok) break;
       const int head = static_cast<int>(v % args.bh);
       const int local = static_cast<int>(v / args.bh);
-      const int* w = args.ws + static_cast<long long>(head) * args.ws_stride;
-      if (local >= w[0]) continue;
-      const int* kp = w + 1;
-      const int* rec = w + 2 + args.gk + 3 * local;
-      const int q_start = rec[0], qg = rec[2];
-      const uint8_t* map_row = args.map + (static_cast<long long>(head) * args.gq + qg) * args.gk;
-      const long long krow0 = static_cast<long long>(head) * args.sk;
-
-      // ---- stream the unit's key runs as 8-row groups grouped into tiles
-      int grow = 0, gvalid = 0;  // lane g holds group g of the pending tile
-      int ngroups = 0;
-      int utiles = 0;
-      int run_s = 0, run_e = 0;
-      bool have_run = false;
-      auto emit_tile = [&](bool last) {
-        fill_slot(2 * tile, maps.k, grow, ngroups);
-        fill_slot(2 * tile + 1, maps.v, grow, ngroups);
-        if (utiles == 0) {
-          // first tile of a non-empty unit: its Q tile, once the previous
-          // unit's last QK has released the buffer (its K/V are already in flight)
+      const int* w = args.ws + static_cast<long long>(head) * g.stride;
+      if (local >= w[0] || local >= g.max_units) continue;
+      const int4 rec = *reinterpret_cast<const int4*>(w + g.off_units + 4 * local);
+      const int q_start = rec.x;
+      int nent = rec.z, nblk = rec.w;
+      if (nent < 0 || nent > g.gk || nblk < 0) {  // not a plan of this geometry
+        if (lane == 0) record_status(args.status, kDevBadIndex);
+        nent = nblk = 0;
+      }
+      if (nblk == 0) {
+        const uint32_t zero[4] = {0, 0, 0, 0};
+        push_info(zero, static_cast<int>(v), kEmpty);  // no key at all: rows are zero
+        if (!ok) break;
+        continue;
+      }
+      const int2* ents = reinterpret_cast<const int2*>(w + g.off_ent) + static_cast<long long>(local) * g.gk;
+      const long long block0 = static_cast<long long>(head) * g.blocks;
+      // window of 32 entries, one per lane: block offset, end position, rows in last block
+      int w0 = 0, wz = 0, wend = 0x7fffffff, wlast = 0;
+      auto load_window = [&](int from) {
+        w0 = from;
+        wz = 0;
+        wend = 0x7fffffff;
+        wlast = 0;
+        if (from + lane < nent) {
+          const int2 e = ents[from + lane];
+          wz = e.x;
+          wend = e.y >> 4;
+          wlast = e.y & 15;
+        }
+      };
+      load_window(0);
+      const int ntiles = (nblk + kTileBlocks - 1) / kTileBlocks;
+      for (int t = 0; t < ntiles && ok; ++t) {
+        const int p0 = t * kTileBlocks;
+        const int before = __popc(__ballot_sync(0xffffffffu, wend <= p0));
+        if (before > 32 - kTileBlocks && w0 + 32 < nent) load_window(w0 + before);
+        // lane < ngroups: block of tile position lane (binary search over the window)
+        const int pos = p0 + lane;
+        int k = 0;
+#pragma unroll
+        for (int step = 16; step >= 1; step >>= 1) {
+          const int e = __shfl_sync(0xffffffffu, wend, k + step - 1);
+          if (e <= pos) k += step;
+        }
+        const int kz = __shfl_sync(0xffffffffu, wz, k);
+        const int kend = __shfl_sync(0xffffffffu, wend, k);
+        const int klast = __shfl_sync(0xffffffffu, wlast, k);
+        const int ngroups = min(kTileBlocks, nblk - p0);
+        int blk = 0, valid = 0;
+        if (lane < ngroups) {
+          blk = kz + pos;
+          valid = pos == kend - 1 ? klast : kKeyBlockRows;
+        }
+        // ---- K and V of the tile: one bulk copy per run of consecutive blocks
+        const int kitem = 2 * tile, vitem = kitem + 1;
+        const int ks = kitem % kSlots, vs = vitem % kSlots;
+        if (ok && kitem >= kSlots) ok = mbar_wait_warp(&sh.slot_empty[ks], ((kitem / kSlots) - 1) & 1, abort_flag, args.status);
+        if (ok && vitem >= kSlots) ok = mbar_wait_warp(&sh.slot_empty[vs], ((vitem / kSlots) - 1) & 1, abort_flag, args.status);
+        if (!ok) break;
+        if (lane == 0) {
+          const uint32_t bytes = static_cast<uint32_t>(ngroups) * L::kBlockBytes;
+          mbar_arrive_expect_tx(&sh.slot_full[ks], bytes);
+          mbar_arrive_expect_tx(&sh.slot_full[vs], bytes);
+        }
+        __syncwarp();
+        const int prev = __shfl_up_sync(0xffffffffu, blk, 1);
+        const bool cont = lane > 0 && lane < ngroups && blk == prev + 1;
+        const unsigned cmask = __ballot_sync(0xffffffffu, cont);
+        int n = 0;  // blocks of the run this lane starts (0 if none)
+        // the run ends at the first non-continuation lane above this one
+        // (lanes >= ngroups never continue, and ngroups <= 16 keeps the shift < 32)
+        if (lane < ngroups && !cont) n = __ffs(~cmask & (0xffffffffu << (lane + 1))) - 1 - lane;
+        // lanes 0-15 copy K, lanes 16-31 copy V of the run that lane - 16 starts
+        const int src = lane & (kTileBlocks - 1);
+        const int rn = __shfl_sync(0xffffffffu, n, src);
+        const int rb = __shfl_sync(0xffffffffu, blk, src);
+        if (rn > 0 && (rb < 0 || rb + rn > g.blocks)) {
+          // a block outside this head: skip the copy (the tile's wait then
+          // expires and the call reports the error)
+          record_status(args.status, kDevBadIndex);
+        } else if (rn > 0) {
+          const bool is_v = lane >= kTileBlocks;
+          const int sl = is_v ? vs : ks;
+          const unsigned char* gsrc = (is_v ? args.vb : args.kb) + (block0 + rb) * L::kBlockBytes;
+          bulk_load(base + L::kSlot0 + sl * L::kTileBytes + src * L::kBlockBytes, gsrc,
+                    static_cast<uint32_t>(rn) * L::kBlockBytes, &sh.slot_full[sl]);
+        }
+        __syncwarp();
+        if (t == 0) {
+          // first tile of the unit: its Q tile, once the previous unit's last
+          // QK has released the buffer (its K/V are already in flight)
           if (ok && qloads > 0) ok = mbar_wait_warp(&sh.q_empty, (qloads - 1) & 1, abort_flag, args.status);
           if (lane == 0 && ok) {
             mbar_arrive_expect_tx(&sh.q_full, L::kTileBytes);
 #pragma unroll
             for (int p = 0; p < D / 64; ++p)
-              tma_load_2d(base + L::kQ0 + p * L::kPanel, &maps.q, 64 * p,
-                          static_cast<int>(static_cast<long long>(head) * args.sq + q_start), &sh.q_full);
+              tma_load_2d(base + L::kQ0 + p * L::kQPanel, &qmap, 64 * p,
+                          static_cast<int>(static_cast<long long>(head) * g.sq + q_start), &sh.q_full);
           }
           __syncwarp();
           ++qloads;
         }
-        const unsigned bits = lane < ngroups ? ((gvalid >= 8) ? 0xffu : ((1u << gvalid) - 1u)) : 0u;
+        const unsigned bits = lane < ngroups ? ((1u << valid) - 1u) : 0u;
         uint32_t word[4] = {0, 0, 0, 0};
 #pragma unroll
-        for (int b = 0; b < kGroups; ++b) word[b >> 2] |= __shfl_sync(0xffffffffu, bits, b) << (8 * (b & 3));
-        push_info(word, static_cast<int>(v), (utiles == 0 ? kFirst : 0u) | (last ? kLast : 0u));
+        for (int b = 0; b < kTileBlocks; ++b) word[b >> 2] |= __shfl_sync(0xffffffffu, bits, b) << (8 * (b & 3));
+        push_info(word, static_cast<int>(v), (t == 0 ? kFirst : 0u) | (t == ntiles - 1 ? kLast : 0u));
         ++tile;
-        ++utiles;
-        ngroups = 0;
-        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-        if (lane == 0) ATTN_TRACE(1, 0x100u + tile);
-      };
-      auto add_group = [&](int row, int valid) {
-        if (ngroups == kGroups) emit_tile(false);
-        if (lane == ngroups) {
-          grow = row;
-          gvalid = valid;
-        }
-        ++ngroups;
-      };
-      auto flush_run = [&]() {
-        for (int r = run_s; r < run_e && ok; r += kGroup) add_group(static_cast<int>(krow0 + r), min(kGroup, run_e - r));
-      };
-      for (int c0 = 0; c0 < args.gk && ok; c0 += 32) {
-        const int c = c0 + lane;
-        int s = 0, e = 0;
-        bool sel = false;
-        if (c < args.gk) {
-          s = kp[c];
-          e = kp[c + 1];
-          sel = map_row[c] != 0 && e > s;
-        }
-        unsigned m = __ballot_sync(0xffffffffu, sel);
-        while (m && ok) {
-          const int b = __ffs(m) - 1;
-          m &= m - 1;
-          const int gs = __shfl_sync(0xffffffffu, s, b);
-          const int ge = __shfl_sync(0xffffffffu, e, b);
-          if (have_run && gs == run_e) {
-            run_e = ge;
-          } else {
-            if (have_run) flush_run();
-            run_s = gs;
-            run_e = ge;
-            have_run = true;
-          }
-        }
         if (*abort_flag) ok = false;
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       }
-      if (have_run && ok) flush_run();
       if (!ok) break;
-      if (utiles == 0 && ngroups == 0) {
-        const uint32_t zero[4] = {0, 0, 0, 0};
-        push_info(zero, static_cast<int>(v), kEmpty);  // no key at all: rows are zero
-      } else {
-        emit_tile(true);
-      }
     }
     const uint32_t zero[4] = {0, 0, 0, 0};
     push_info(zero, -1, kEnd);
@@ -447,10 +524,9 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
       constexpr uint32_t idesc_qk = instr_desc(128, kBN, AB, false, false);
       constexpr uint32_t idesc_pv = instr_desc(128, D, AB, false, true);
       bool ok = true;
-      int entry = 0, t = 0, qloads = 0, ounits = 0;
-      int cur = -1;           // tile whose P.V is pending
+      int entry = 0, t = 0, qloads = 0;
+      int cur = -1;  // tile whose P.V is pending
       uint32_t cur_flags = 0;
-      int cur_oslot = 0;
       auto issue_pv = [&]() {
         const int b = cur & 1, item = 2 * cur + 1, sl = item % kSlots;
         ok = mbar_wait(&sh.p_full[b], (cur >> 1) & 1, abort_flag, args.status);
@@ -458,16 +534,19 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
         if (!ok) return;
         tc_fence_after();
         const uint32_t va = smem_u32(base + L::kSlot0 + sl * L::kTileBytes);
-        const uint32_t o_addr = tmem + 256 + cur_oslot * 128;
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint64_t bdesc = smem_desc(va + kk * 2 * 1024, L::kPanel, 1024);
-          umma_ts(o_addr, tmem + b * 128 + kk * 8, bdesc, idesc_pv, ((cur_flags & kFirst) && kk == 0) ? 0u : 1u);
+        for (int h = 0; h < 2; ++h) {
+#pragma unroll
+          for (int kk = 0; kk < kBN / 32; ++kk) {
+            // 16 keys = two blocks; MN-major V: 64-dim panels 1 KB apart, 8-key groups one block apart
+            const uint64_t bdesc = smem_desc(va + (8 * h + 2 * kk) * L::kBlockBytes, 1024, L::kBlockBytes);
+            umma_ts(tmem + 256 + 128 * h, tmem + b * 128 + 64 * h + kk * 8, bdesc, idesc_pv,
+                    ((cur_flags & kFirst) && kk == 0) ? 0u : 1u);
+          }
         }
         umma_commit(&sh.s_free[b]);
         umma_commit(&sh.slot_empty[sl]);
-        if (cur_flags & kLast) umma_commit(&sh.o_full[cur_oslot]);
-        ATTN_TRACE(2, 0x200u + cur);
+        if (cur_flags & kLast) umma_commit(&sh.o_full);
       };
       for (;;) {
         const int slot = entry % kRing;
@@ -492,14 +571,13 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
         const uint32_t ka = smem_u32(base + L::kSlot0 + sl * L::kTileBytes);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * L::kPanel + (kk & 3) * 32;
-          umma_ss(tmem + b * 128, smem_desc(qa + off, 16, 1024), smem_desc(ka + off, 16, 1024), idesc_qk,
-                  kk > 0 ? 1u : 0u);
+          const uint32_t col = (kk & 3) * 32;
+          umma_ss(tmem + b * 128, smem_desc(qa + (kk >> 2) * L::kQPanel + col, 16, 1024),
+                  smem_desc(ka + (kk >> 2) * 1024 + col, 16, L::kBlockBytes), idesc_qk, kk > 0 ? 1u : 0u);
         }
         umma_commit(&sh.s_full[b]);
         umma_commit(&sh.slot_empty[sl]);
         if (fl & kLast) umma_commit(&sh.q_empty);
-        ATTN_TRACE(2, 0x100u + t);
         // ---- O += P V for the previous tile
         if (cur >= 0) {
           issue_pv();
@@ -507,12 +585,6 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
         }
         cur = t;
         cur_flags = fl;
-        if (fl & kFirst) {
-          cur_oslot = ounits & 1;
-          if (ounits >= 2) ok = mbar_wait(&sh.o_free[cur_oslot], ((ounits >> 1) - 1) & 1, abort_flag, args.status);
-          ++ounits;
-          if (!ok) break;
-        }
         ++t;
       }
       if (ok && cur >= 0) issue_pv();
@@ -524,49 +596,27 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
     // ----------------------------------------------- softmax + epilogue
     using T = typename std::conditional<AB == 1, __nv_bfloat16, __half>::type;
     const int quarter = warp & 3;                  // TMEM lane quarter of this warp
+    const int half = (warp - 2) >> 2;              // key columns [64 half, 64 half + 64)
     const int r = quarter * 32 + lane;             // query row within the unit
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t o_own = tmem + 256 + 128 * half;
     float m = -INFINITY, l = 0.0f;
     bool ok = true;
-    int entry = 0, t = 0, ounits = 0, oslot = 0;
-    // write this thread's row of unit v: O/l, or zero when ``zero``
-    auto write_row = [&](int v, bool have_o, float inv) {
+    int entry = 0, t = 0, units_done = 0;
+    // output row of unit v for this thread (nullptr: not a real row)
+    auto out_row = [&](int v) -> T* {
       const int head = v % args.bh, local = v / args.bh;
-      const int* rec = args.ws + static_cast<long long>(head) * args.ws_stride + 2 + args.gk + 3 * local;
+      const int* rec = args.ws + static_cast<long long>(head) * g.stride + g.off_units + 4 * local;
       const int q_start = rec[0], q_count = rec[1];
-      T* dst = nullptr;
-      if (r < q_count) {
-        const int prow = q_start + r;
-        long long orow = prow;
-        if (args.perm && prow < args.video) orow = args.perm[static_cast<long long>(head) * args.video + prow];
-        if (orow < 0 || orow >= args.out_rows) record_status(args.status, kDevBadIndex);
-        else dst = static_cast<T*>(args.out) + (static_cast<long long>(head) * args.out_rows + orow) * D;
+      if (r >= q_count) return nullptr;
+      const int prow = q_start + r;
+      long long orow = prow;
+      if (args.perm && prow < args.video) orow = args.perm[static_cast<long long>(head) * args.video + prow];
+      if (orow < 0 || orow >= args.out_rows) {
+        record_status(args.status, kDevBadIndex);
+        return nullptr;
       }
-      __syncwarp();
-      if (have_o) {
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t vv[32];
-          tmem_ld32_sync(tmem + 256 + oslot * 128 + lane_off + c * 32, vv);
-          if (dst) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-              uint4 pk;
-              uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float a = __uint_as_float(vv[j + 2 * e]) * inv, bb = __uint_as_float(vv[j + 2 * e + 1]) * inv;
-                pw[e] = AB ? pack_bf16x2(a, bb) : pack_f16x2(a, bb);
-              }
-              reinterpret_cast<uint4*>(dst)[(c * 32 + j) / 8] = pk;
-            }
-          }
-        }
-      } else if (dst) {
-#pragma unroll
-        for (int c = 0; c < D / 8; ++c) reinterpret_cast<uint4*>(dst)[c] = make_uint4(0, 0, 0, 0);
-      }
-      __syncwarp();
+      return static_cast<T*>(args.out) + (static_cast<long long>(head) * args.out_rows + orow) * D + (D / 2) * half;
     };
     for (;;) {
       const int slot = entry % kRing;
@@ -578,34 +628,50 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
       ++entry;
       if (ti.flags & kEnd) break;
       if (ti.flags & kEmpty) {
-        write_row(ti.unit, false, 0.0f);
+        T* dst = out_row(ti.unit);
+        if (dst) {
+#pragma unroll
+          for (int c = 0; c < D / 16; ++c) reinterpret_cast<uint4*>(dst)[c] = make_uint4(0, 0, 0, 0);
+        }
+        __syncwarp();
         continue;
       }
       if (ti.flags & kFirst) {
         m = -INFINITY;
         l = 0.0f;
-        oslot = ounits & 1;
-        ++ounits;
       }
       const int b = t & 1;
       ok = mbar_wait_warp(&sh.s_full[b], (t >> 1) & 1, abort_flag, args.status);
       if (!ok) break;
       tc_fence_after();
-      float s[kBN];
+      constexpr int kCols = kBN / 2;
+      float s[kCols];
 #pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) {
+      for (int c = 0; c < kCols / 32; ++c) {
         uint32_t vv[32];
-        tmem_ld32_sync(tmem + b * 128 + lane_off + c * 32, vv);
+        tmem_ld32_sync(tmem + b * 128 + 64 * half + lane_off + c * 32, vv);
 #pragma unroll
         for (int j = 0; j < 32; ++j) s[c * 32 + j] = __uint_as_float(vv[j]);
       }
-      float mx = -INFINITY;
+      // raw scores of masked keys become -inf; the row max runs in kChains
+      // independent chains (scale > 0, so it commutes with the max)
+      constexpr int kChains = 8;
+      float mxc[kChains];
 #pragma unroll
-      for (int j = 0; j < kBN; ++j) {
-        const bool valid = (ti.mask[j >> 5] >> (j & 31)) & 1u;
-        s[j] = valid ? s[j] * args.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, s[j]);
+      for (int i = 0; i < kChains; ++i) mxc[i] = -INFINITY;
+      const uint32_t mw[2] = {half ? ti.mask[2] : ti.mask[0], half ? ti.mask[3] : ti.mask[1]};
+#pragma unroll
+      for (int j = 0; j < kCols; ++j) {
+        const bool valid = (mw[j >> 5] >> (j & 31)) & 1u;
+        s[j] = valid ? s[j] : -INFINITY;
+        mxc[j % kChains] = fmaxf(mxc[j % kChains], s[j]);
       }
+#pragma unroll
+      for (int i = kChains / 2; i > 0; i >>= 1) {
+#pragma unroll
+        for (int k2 = 0; k2 < i; ++k2) mxc[k2] = fmaxf(mxc[k2], mxc[k2 + i]);
+      }
+      const float mx = mxc[0] * args.scale_log2;
       // grow the running max lazily (only by > 8 in log2 units); rescaling O
       // is warp-collective (tcgen05.ld/st are .sync.aligned) and needs the
       // previous tile's P.V to be complete
@@ -615,72 +681,124 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
         ok = mbar_wait_warp(&sh.s_free[(t - 1) & 1], ((t - 1) >> 1) & 1, abort_flag, args.status);
         if (!ok) break;
         tc_fence_after();
-        const float f = rescale_me ? exp2f(m - mx) : 1.0f;
+        const float f = rescale_me ? exp2_approx(m - mx) : 1.0f;
         l *= f;
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
           uint32_t vv[32];
-          tmem_ld32_sync(tmem + 256 + oslot * 128 + lane_off + c * 32, vv);
+          tmem_ld32_sync(o_own + lane_off + c * 32, vv);
           uint32_t lo[16], hi[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             lo[j] = __float_as_uint(__uint_as_float(vv[j]) * f);
             hi[j] = __float_as_uint(__uint_as_float(vv[16 + j]) * f);
           }
-          tmem_st16(tmem + 256 + oslot * 128 + lane_off + c * 32, lo);
-          tmem_st16(tmem + 256 + oslot * 128 + lane_off + c * 32 + 16, hi);
+          tmem_st16(o_own + lane_off + c * 32, lo);
+          tmem_st16(o_own + lane_off + c * 32 + 16, hi);
         }
       }
       if (grow) m = mx;
-      const float mref = (m == -INFINITY) ? 0.0f : m;
-      float sum = 0.0f;
-      uint32_t packed[kBN / 2];
+      // p = 2^(s*c - m): one FFMA and one ex2 per score (masked: 2^-inf = 0)
+      const float neg_m = (m == -INFINITY) ? 0.0f : -m;
+      float sumc[kChains];
 #pragma unroll
-      for (int j = 0; j < kBN; j += 2) {
-        const float p0 = exp2f(s[j] - mref);
-        const float p1 = exp2f(s[j + 1] - mref);
-        sum += p0 + p1;
+      for (int i = 0; i < kChains; ++i) sumc[i] = 0.0f;
+      uint32_t packed[kCols / 2];
+#pragma unroll
+      for (int j = 0; j < kCols; j += 2) {
+        const float p0 = exp2_approx(fmaf(s[j], args.scale_log2, neg_m));
+        const float p1 = exp2_approx(fmaf(s[j + 1], args.scale_log2, neg_m));
+        sumc[(j / 2) % kChains] += p0;
+        sumc[(j / 2 + kChains / 2) % kChains] += p1;
         packed[j >> 1] = AB ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
       }
-      l += sum;
 #pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) {
+      for (int i = kChains / 2; i > 0; i >>= 1) {
+#pragma unroll
+        for (int k2 = 0; k2 < i; ++k2) sumc[k2] += sumc[k2 + i];
+      }
+      l += sumc[0];
+#pragma unroll
+      for (int c = 0; c < kCols / 32; ++c) {
         uint32_t part[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) part[j] = packed[c * 16 + j];
-        tmem_st16(tmem + b * 128 + lane_off + c * 16, part);
+        tmem_st16(tmem + b * 128 + 64 * half + lane_off + c * 16, part);
       }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sh.p_full[b]);
-      if (lane == 0) ATTN_TRACE(3 + quarter, 0x300u + t);
       ++t;
       if (ti.flags & kLast) {
-        // epilogue of the unit: O[oslot] is final once its last P.V completes
-        ok = mbar_wait_warp(&sh.o_full[oslot], ((ounits - 1) >> 1) & 1, abort_flag, args.status);
+        // epilogue of the unit: O_0 and O_1 are final once its last P.V completes
+        ok = mbar_wait_warp(&sh.o_full, units_done & 1, abort_flag, args.status);
         if (!ok) break;
         tc_fence_after();
-        write_row(ti.unit, true, l > 0.0f ? 1.0f / l : 0.0f);
+        // merge factors: half 1 hands (m, l) to half 0, which returns the
+        // scale of each accumulator with 1/L folded in
+        float a0, a1;
+        if (half == 1) {
+          sh.xch[r] = make_float2(m, l);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sh.xch_full[quarter]);
+          ok = mbar_wait_warp(&sh.xch_back[quarter], units_done & 1, abort_flag, args.status);
+          if (!ok) break;
+          const float2 f = sh.xch[r];
+          a0 = f.x;
+          a1 = f.y;
+        } else {
+          ok = mbar_wait_warp(&sh.xch_full[quarter], units_done & 1, abort_flag, args.status);
+          if (!ok) break;
+          const float2 o = sh.xch[r];
+          const float mm = fmaxf(m, o.x);
+          const float e0 = m == -INFINITY ? 0.0f : exp2_approx(m - mm);
+          const float e1 = o.x == -INFINITY ? 0.0f : exp2_approx(o.x - mm);
+          const float tot = l * e0 + o.y * e1;
+          const float inv = tot > 0.0f ? 1.0f / tot : 0.0f;
+          a0 = e0 * inv;
+          a1 = e1 * inv;
+          sh.xch[r] = make_float2(a0, a1);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sh.xch_back[quarter]);
+        }
+        ++units_done;
+        T* dst = out_row(ti.unit);
+        __syncwarp();
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c) {
+          // this warp writes output dims [D/2 half, D/2 (half + 1))
+          uint32_t v0[32], v1[32];
+          tmem_ld32_sync(tmem + 256 + lane_off + (D / 2) * half + c * 32, v0);
+          tmem_ld32_sync(tmem + 384 + lane_off + (D / 2) * half + c * 32, v1);
+          if (dst) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+              uint4 pk;
+              uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float x0 = __uint_as_float(v0[j + 2 * e]) * a0 + __uint_as_float(v1[j + 2 * e]) * a1;
+                const float x1 = __uint_as_float(v0[j + 2 * e + 1]) * a0 + __uint_as_float(v1[j + 2 * e + 1]) * a1;
+                pw[e] = AB ? pack_bf16x2(x0, x1) : pack_f16x2(x0, x1);
+              }
+              reinterpret_cast<uint4*>(dst)[(c * 32 + j) / 8] = pk;
+            }
+          }
+        }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sh.o_free[oslot]);
       }
     }
     __syncwarp();
   }
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0) ATTN_TRACE(0, 3);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
 }
-
-#ifdef PECO_ATTN_TRACE
-unsigned* g_attn_trace = nullptr;
-#endif
 
 bool make_rows_map(CUtensorMap* m, const void* base, long long rows, int dims, int box_rows, int dtype) {
   const uint64_t gdims[2] = {static_cast<uint64_t>(dims), static_cast<uint64_t>(rows)};
@@ -698,105 +816,160 @@ int num_sms() {
 }
 
 template <int D, int AB>
-int launch_main(const void* q, const void* k, const void* v, const AttnArgs& a, cudaStream_t stream) {
-  AttnMaps maps;
-  if (!make_rows_map(&maps.q, q, static_cast<long long>(a.bh) * a.sq, D, kBM, AB)) return kErrTensorMap;
-  for (int h = 0; h < kHeights; ++h) {
-    if (!make_rows_map(&maps.k[h], k, static_cast<long long>(a.bh) * a.sk, D, kGroup << h, AB) ||
-        !make_rows_map(&maps.v[h], v, static_cast<long long>(a.bh) * a.sk, D, kGroup << h, AB))
-      return kErrTensorMap;
-  }
+int launch_main(const void* q, const AttnArgs& a, cudaStream_t stream) {
+  CUtensorMap qmap;
+  if (!make_rows_map(&qmap, q, static_cast<long long>(a.bh) * a.g.sq, D, kBM, AB)) return kErrTensorMap;
   const int smem = Layout<D>::kSmem;
   cudaError_t e = cudaFuncSetAttribute(sparse_attention_tc<D, AB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return static_cast<int>(e);
-  const long long total = static_cast<long long>(a.bh) * a.max_units;
+  const long long total = static_cast<long long>(a.bh) * a.g.max_units;
   const int grid = static_cast<int>(total < num_sms() ? total : num_sms());
-  sparse_attention_tc<D, AB><<<grid, kThreads, smem, stream>>>(maps, a);
+  sparse_attention_tc<D, AB><<<grid, kThreads, smem, stream>>>(qmap, a);
   return launch_status();
+}
+
+int check_shape(int bh, int sq, int sk, int d, int gq, int gk) {
+  if (bh < 1 || bh > 65535 || sq < 0 || sk < 0 || gq < 1 || gk < 1) return kErrInvalidValue;
+  if (d != 64 && d != 128) return kErrUnsupported;
+  const PlanGeom g = plan_geom(sq, sk, gq, gk);
+  // int32 positions (entries pack end << 4), unit indices and per-head offsets
+  if (g.blocks * kKeyBlockRows > (1LL << 26) || static_cast<long long>(bh) * g.max_units > 2147483647LL ||
+      g.stride > 2147483647LL)
+    return kErrUnsupported;
+  return kOk;
 }
 
 }  // namespace
 
-int launch_sparse_attention(const void* q, const void* k, const void* v, const uint8_t* map, const int* q_sizes,
-                            const int* k_sizes, void* out, int* ws, int ws_stride, int bh, int sq, int sk, int d,
-                            int gq, int gk, int dtype, const int32_t* perm, int video, cudaStream_t stream) {
-  if (bh < 1 || bh > 65535 || sq < 0 || sk < 0 || gq < 1 || gk < 1 || (dtype != 0 && dtype != 1))
-    return kErrInvalidValue;
-  if (d != 64 && d != 128) return kErrUnsupported;
-  if (sq == 0) return kOk;
-  const long long max_units = (static_cast<long long>(sq) + kBM - 1) / kBM + gq;
-  const long long need = 2 + gk + 3 * max_units;
-  if (need > ws_stride) return kErrWorkspace;
-  if (static_cast<long long>(bh) * max_units > 2147483647LL) return kErrUnsupported;
-  const size_t plan_smem = 2 * sizeof(int) * static_cast<size_t>(gq);
-  if (plan_smem > 200 * 1024) return kErrUnsupported;
-  if (plan_smem > 48 * 1024)
-    cudaFuncSetAttribute(attn_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(plan_smem));
-  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
-       reinterpret_cast<uintptr_t>(out)) & 15)
-    return kErrInvalidValue;
-  // the work counter takes the last int of the last head's region when the
-  // workspace has room for it; otherwise CTAs take units with a fixed stride
-  const int dynamic = ws_stride >= need + 1 ? 1 : 0;
-  attn_plan_kernel<<<bh, 1024, plan_smem, stream>>>(q_sizes, k_sizes, ws, gq, gk, sq, sk, ws_stride, dynamic);
-  int rc = launch_status();
+int launch_attention_plan(const uint8_t* map, const int* q_sizes, const int* k_sizes, void* k_blocks,
+                          void* v_blocks, int* ws, int bh, int sq, int sk, int d, int gq, int gk,
+                          cudaStream_t stream) {
+  int rc = check_shape(bh, sq, sk, d, gq, gk);
   if (rc) return rc;
-  AttnArgs a;
-#ifdef PECO_ATTN_TRACE
-  a.trace = g_attn_trace;
-#endif
-  a.map = map;
-  a.ws = ws;
-  a.out = out;
-  a.perm = perm;
-  a.bh = bh;
-  a.sq = sq;
-  a.sk = sk;
-  a.gq = gq;
-  a.gk = gk;
-  a.ws_stride = ws_stride;
-  a.max_units = static_cast<int>(max_units);
-  a.out_rows = sq;
-  a.video = perm ? video : 0;
-  a.dynamic_sched = dynamic;
-  a.scale_log2 = static_cast<float>(1.4426950408889634 / sqrt(static_cast<double>(d)));
-  a.status = device_status_ptr();
-  if (d == 128) return dtype ? launch_main<128, 1>(q, k, v, a, stream) : launch_main<128, 0>(q, k, v, a, stream);
-  return dtype ? launch_main<64, 1>(q, k, v, a, stream) : launch_main<64, 0>(q, k, v, a, stream);
+  if ((k_blocks == nullptr) != (v_blocks == nullptr)) return kErrInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(ws) | reinterpret_cast<uintptr_t>(k_blocks) | reinterpret_cast<uintptr_t>(v_blocks)) & 15)
+    return kErrInvalidValue;
+  const PlanGeom g = plan_geom(sq, sk, gq, gk);
+  const size_t smem = sizeof(int) * (2 * static_cast<size_t>(gk + 1) + 2 * static_cast<size_t>(gq) + g.max_units);
+  if (smem > 200 * 1024) return kErrUnsupported;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(attn_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
+  attn_plan_kernel<<<bh, 1024, smem, stream>>>(map, q_sizes, k_sizes, ws, g, static_cast<unsigned char*>(k_blocks),
+                                               static_cast<unsigned char*>(v_blocks), kKeyBlockRows * d * 2);
+  return launch_status();
 }
 
-// Workspace ints per head needed by launch_sparse_attention (the last one
-// of the last head holds the work counter).
-long long attention_ws_stride(int sq, int gq, int gk) {
-  const long long max_units = (static_cast<long long>(sq) + kBM - 1) / kBM + gq;
-  return 3 + gk + 3 * max_units;
+int launch_pack_key_blocks(const void* k, const void* v, void* k_blocks, void* v_blocks, const int* ws, int bh,
+                           int sq, int sk, int d, int gq, int gk, cudaStream_t stream) {
+  int rc = check_shape(bh, sq, sk, d, gq, gk);
+  if (rc) return rc;
+  if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(k_blocks) |
+       reinterpret_cast<uintptr_t>(v_blocks)) & 15)
+    return kErrInvalidValue;
+  const PlanGeom g = plan_geom(sq, sk, gq, gk);
+  const long long chunks = static_cast<long long>(bh) * sk * (d / 8);
+  if (chunks == 0) return kOk;
+  long long blocks = (chunks + 255) / 256;
+  if (blocks > kNumSMs * 16) blocks = kNumSMs * 16;
+  if (d == 128)
+    pack_key_blocks_kernel<128><<<static_cast<int>(blocks), 256, 0, stream>>>(
+        static_cast<const uint4*>(k), static_cast<const uint4*>(v), static_cast<unsigned char*>(k_blocks),
+        static_cast<unsigned char*>(v_blocks), ws, g, bh, device_status_ptr());
+  else
+    pack_key_blocks_kernel<64><<<static_cast<int>(blocks), 256, 0, stream>>>(
+        static_cast<const uint4*>(k), static_cast<const uint4*>(v), static_cast<unsigned char*>(k_blocks),
+        static_cast<unsigned char*>(v_blocks), ws, g, bh, device_status_ptr());
+  return launch_status();
+}
+
+int launch_attention_main(const void* q, const void* k_blocks, const void* v_blocks, const int* ws, void* out,
+                          int bh, int sq, int sk, int d, int gq, int gk, int dtype, const int32_t* perm, int video,
+                          cudaStream_t stream) {
+  int rc = check_shape(bh, sq, sk, d, gq, gk);
+  if (rc) return rc;
+  if (dtype != 0 && dtype != 1) return kErrInvalidValue;
+  if (sq == 0) return kOk;
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k_blocks) | reinterpret_cast<uintptr_t>(v_blocks) |
+       reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(ws)) & 15)
+    return kErrInvalidValue;
+  AttnArgs a;
+  a.ws = ws;
+  a.kb = static_cast<const unsigned char*>(k_blocks);
+  a.vb = static_cast<const unsigned char*>(v_blocks);
+  a.out = out;
+  a.perm = perm;
+  a.g = plan_geom(sq, sk, gq, gk);
+  a.bh = bh;
+  a.out_rows = sq;
+  a.video = perm ? video : 0;
+  a.scale_log2 = static_cast<float>(1.4426950408889634 / sqrt(static_cast<double>(d)));
+  a.status = device_status_ptr();
+  if (d == 128) return dtype ? launch_main<128, 1>(q, a, stream) : launch_main<128, 0>(q, a, stream);
+  return dtype ? launch_main<64, 1>(q, a, stream) : launch_main<64, 0>(q, a, stream);
 }
 
 }  // namespace peco
 
-// Drop-in for peco/kernels/sparse_attention.cu:210-230.  Workspace: int32
-// BH * (CK + 2 + 3 * (ceil(SQ/16) + CQ)), the reference's size.
+using namespace peco;
+
+// Drop-in for peco/kernels/sparse_attention.cu:210-230.  The caller's
+// workspace (the reference's size) is accepted for ABI compatibility; the
+// plan and the key blocks live in stream-ordered scratch of this call.
 extern "C" int peco_sparse_attention(const void* q, const void* k, const void* v, const uint8_t* selected,
                                      const int* q_sizes, const int* k_sizes, void* output, int* workspace, int bh,
-                                     int sq, int sk, int d, int cq, int ck, int dtype, void* stream) {
-  const long long cap = (static_cast<long long>(sq) + 15) / 16 + cq;
-  const long long stride = ck + 2 + 3 * cap;
-  if (stride > 2147483647LL) return peco::kErrInvalidValue;
-  return peco::launch_sparse_attention(q, k, v, selected, q_sizes, k_sizes, output, workspace,
-                                       static_cast<int>(stride), bh, sq, sk, d, cq, ck, dtype, nullptr, 0,
-                                       static_cast<cudaStream_t>(stream));
+                                     int sq, int sk, int d, int cq, int ck, int dtype, void* stream_ptr) {
+  (void)workspace;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  int rc = check_shape(bh, sq, sk, d, cq, ck);
+  if (rc) return rc;
+  if (dtype != 0 && dtype != 1) return kErrInvalidValue;
+  if (sq == 0) return kOk;
+  const PlanGeom g = plan_geom(sq, sk, cq, ck);
+  const size_t ws_bytes = (static_cast<size_t>(bh) * g.stride * sizeof(int) + 255) & ~size_t(255);
+  const size_t kb_bytes = static_cast<size_t>(bh) * g.blocks * kKeyBlockRows * d * 2;
+  void* scratch = nullptr;
+  cudaError_t e = cudaMallocAsync(&scratch, ws_bytes + 2 * kb_bytes, stream);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  int* ws = static_cast<int*>(scratch);
+  unsigned char* kb = static_cast<unsigned char*>(scratch) + ws_bytes;
+  unsigned char* vb = kb + kb_bytes;
+  rc = launch_attention_plan(selected, q_sizes, k_sizes, kb, vb, ws, bh, sq, sk, d, cq, ck, stream);
+  if (!rc) rc = launch_pack_key_blocks(k, v, kb, vb, ws, bh, sq, sk, d, cq, ck, stream);
+  if (!rc) rc = launch_attention_main(q, kb, vb, ws, output, bh, sq, sk, d, cq, ck, dtype, nullptr, 0, stream);
+  e = cudaFreeAsync(scratch, stream);
+  return rc ? rc : static_cast<int>(e);
 }
 
-extern "C" long long peco_attention_workspace_stride(int sq, int gq, int gk) {
-  return peco::attention_ws_stride(sq, gq, gk);
+extern "C" long long peco_attention_workspace_stride(int sq, int sk, int gq, int gk) {
+  if (sq < 0 || sk < 0 || gq < 1 || gk < 1) return -1;
+  return plan_geom(sq, sk, gq, gk).stride;
 }
 
-extern "C" int peco_sparse_attention_restore(const void* q, const void* k, const void* v, const uint8_t* map,
-                                             const int* q_sizes, const int* k_sizes, void* output, int* workspace,
-                                             int bh, int sq, int sk, int d, int gq, int gk, const int32_t* q_indices,
-                                             int video, void* stream) {
-  const long long stride = peco::attention_ws_stride(sq, gq, gk);
-  if (stride > 2147483647LL || video < 0 || video > sq) return peco::kErrInvalidValue;
-  return peco::launch_sparse_attention(q, k, v, map, q_sizes, k_sizes, output, workspace, static_cast<int>(stride), bh,
-                                       sq, sk, d, gq, gk, 1, q_indices, video, static_cast<cudaStream_t>(stream));
+extern "C" long long peco_key_block_rows(int sk, int gk) {
+  if (sk < 0 || gk < 1) return -1;
+  return plan_geom(0, sk, 1, gk).blocks * kKeyBlockRows;
+}
+
+extern "C" int peco_attention_plan(const uint8_t* map, const int* q_sizes, const int* k_sizes, void* k_blocks,
+                                   void* v_blocks, int* workspace, int bh, int sq, int sk, int d, int gq, int gk,
+                                   void* stream) {
+  return launch_attention_plan(map, q_sizes, k_sizes, k_blocks, v_blocks, workspace, bh, sq, sk, d, gq, gk,
+                               static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int peco_pack_key_blocks(const void* k, const void* v, void* k_blocks, void* v_blocks,
+                                    const int* workspace, int bh, int sq, int sk, int d, int gq, int gk,
+                                    void* stream) {
+  return launch_pack_key_blocks(k, v, k_blocks, v_blocks, workspace, bh, sq, sk, d, gq, gk,
+                                static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int peco_sparse_attention_restore(const void* q, const void* k_blocks, const void* v_blocks,
+                                             const int* workspace, void* output, int bh, int sq, int sk, int d,
+                                             int gq, int gk, const int32_t* q_indices, int video, void* stream) {
+  if (video < 0 || video > sq) return kErrInvalidValue;
+  return launch_attention_main(q, k_blocks, v_blocks, workspace, output, bh, sq, sk, d, gq, gk, 1, q_indices, video,
+                               static_cast<cudaStream_t>(stream));
 }

@@ -32,15 +32,71 @@ int launch_select(const float* qc, const float* kc, const int32_t* qs, const int
                   int cq, int ck, int dims, float top_p, int minimum, int extend, int valid_text, int text_length,
                   int32_t* q_ext, int32_t* k_ext, cudaStream_t stream);
 
+// ---------------------------------------------------------------------------
+// Attention plan and key blocks
+// ---------------------------------------------------------------------------
+// Keys and values reach the attention kernel as 8-row KEY BLOCKS: every key
+// cluster starts a new block (its last block is zero-padded), and a block
+// holds the byte image the tensor core reads from shared memory -- D/64
+// panels of 8 rows x 128 bytes, the 16-byte chunk c of row i stored at chunk
+// position c ^ i (128-byte swizzle).  One contiguous run of blocks is then one
+// bulk copy.  Head h owns blocks [h * blocks, (h + 1) * blocks).
+constexpr int kKeyBlockRows = 8;
+constexpr int kUnitRows = 128;  // query rows per attention work unit
+
+// Per-head plan workspace (int32), written by the planner kernel:
+//   [0] unit count, [1..3] reserved
+//   kp    [gk+1]            clamped row start of every key cluster
+//   gp    [gk+1]            first key block of every key cluster
+//   units [max_units][4]    q_start, q_count, entry count, block count
+//   rows  [sk]              key row -> row in the key-block image (-1: unused)
+//   ent   [max_units][gk]   int2 entries, one per selected key cluster:
+//                           (first block - first position, end position << 4 | rows in last block)
+// The last int of the last head's region is the work counter of the
+// persistent attention kernel.
+struct PlanGeom {
+  int sq, sk, gq, gk;
+  long long max_units, blocks;
+  long long off_kp, off_gp, off_units, off_rows, off_ent, stride;
+};
+
+__host__ __device__ inline PlanGeom plan_geom(int sq, int sk, int gq, int gk) {
+  PlanGeom g;
+  g.sq = sq;
+  g.sk = sk;
+  g.gq = gq;
+  g.gk = gk;
+  g.max_units = (static_cast<long long>(sq) + kUnitRows - 1) / kUnitRows + gq;
+  g.blocks = (static_cast<long long>(sk) + kKeyBlockRows - 1) / kKeyBlockRows + gk;
+  g.off_kp = 4;
+  g.off_gp = g.off_kp + gk + 1;
+  g.off_units = (g.off_gp + gk + 1 + 3) & ~3LL;
+  g.off_rows = g.off_units + 4 * g.max_units;
+  g.off_ent = (g.off_rows + sk + 3) & ~3LL;
+  g.stride = (g.off_ent + 2 * g.max_units * gk + 1 + 3) & ~3LL;
+  return g;
+}
+
+// byte offset of element (row i, dim d) inside one key block (2-byte elements)
+__host__ __device__ inline int key_block_offset(int i, int d) {
+  return (d >> 6) * 1024 + i * 128 + ((((d & 63) >> 3) ^ i) << 4) + (d & 7) * 2;
+}
+
 int launch_quant_gather(const void* q, const void* k, const void* v, void* qp, void* kp, void* vp,
                         const int32_t* q_perm, const int32_t* k_perm, const int32_t* q_labels,
                         const int32_t* k_labels, const float* q_cen, const float* k_cen, int cq, int ck, int bh,
-                        int seq, int video, int dims, int bits, cudaStream_t stream);
+                        int seq, int video, int dims, int bits, const int* plan, int gq, int gk,
+                        cudaStream_t stream);
 
-int launch_sparse_attention(const void* q, const void* k, const void* v, const uint8_t* map, const int* q_sizes,
-                            const int* k_sizes, void* out, int* ws, int ws_stride, int bh, int sq, int sk, int d,
-                            int gq, int gk, int dtype, const int32_t* perm, int video, cudaStream_t stream);
+int launch_attention_plan(const uint8_t* map, const int* q_sizes, const int* k_sizes, void* k_blocks,
+                          void* v_blocks, int* ws, int bh, int sq, int sk, int d, int gq, int gk,
+                          cudaStream_t stream);
 
-long long attention_ws_stride(int sq, int gq, int gk);
+int launch_pack_key_blocks(const void* k, const void* v, void* k_blocks, void* v_blocks, const int* ws, int bh,
+                           int sq, int sk, int d, int gq, int gk, cudaStream_t stream);
+
+int launch_attention_main(const void* q, const void* k_blocks, const void* v_blocks, const int* ws, void* out,
+                          int bh, int sq, int sk, int d, int gq, int gk, int dtype, const int32_t* perm, int video,
+                          cudaStream_t stream);
 
 }  // namespace peco

@@ -339,6 +339,9 @@ struct GatherJob {
 };
 struct GatherJobs {
   GatherJob job[3];
+  // optional attention plan: K and V (jobs 1 and 2) then go to key blocks
+  const int* plan;
+  long long plan_stride, off_rows, blocks;
 };
 
 template <int D>
@@ -354,6 +357,17 @@ __global__ void quant_gather_kernel(GatherJobs jobs, int bh, int seq, int video,
     const long long head = row / seq;
     const int j = static_cast<int>(row - head * seq);
     __nv_bfloat16* dst = J.dst + row * D + sub * 8;
+    if (jobs.plan && blockIdx.y > 0) {
+      const int kr = jobs.plan[head * jobs.plan_stride + jobs.off_rows + j];
+      if (kr < 0) continue;  // key row outside every key cluster: never attended
+      if (kr >= jobs.blocks * kKeyBlockRows) {
+        if (sub == 0) record_status(status, kDevBadIndex);
+        continue;
+      }
+      dst = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<unsigned char*>(J.dst) +
+                                             (head * jobs.blocks + kr / kKeyBlockRows) * (kKeyBlockRows * D * 2) +
+                                             key_block_offset(kr % kKeyBlockRows, sub * 8));
+    }
     if (j >= video) {
       *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(J.src + row * D + sub * 8);
       continue;
@@ -411,8 +425,19 @@ int launch_stable_sort(const int32_t* labels, long long label_stride, int rows, 
 int launch_quant_gather(const void* q, const void* k, const void* v, void* qp, void* kp, void* vp,
                         const int32_t* q_perm, const int32_t* k_perm, const int32_t* q_labels,
                         const int32_t* k_labels, const float* q_cen, const float* k_cen, int cq, int ck, int bh,
-                        int seq, int video, int dims, int bits, cudaStream_t stream) {
+                        int seq, int video, int dims, int bits, const int* plan, int gq, int gk,
+                        cudaStream_t stream) {
   GatherJobs jobs;
+  jobs.plan = plan;
+  jobs.plan_stride = jobs.off_rows = jobs.blocks = 0;
+  if (plan) {
+    if (gq < 1 || gk < 1 || (reinterpret_cast<uintptr_t>(kp) | reinterpret_cast<uintptr_t>(vp)) & 15)
+      return kErrInvalidValue;
+    const PlanGeom g = plan_geom(seq, seq, gq, gk);
+    jobs.plan_stride = g.stride;
+    jobs.off_rows = g.off_rows;
+    jobs.blocks = g.blocks;
+  }
   jobs.job[0] = {static_cast<const __nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(qp), q_perm,
                  bits ? q_labels : nullptr, q_cen, cq};
   jobs.job[1] = {static_cast<const __nv_bfloat16*>(k), static_cast<__nv_bfloat16*>(kp), k_perm,
@@ -526,9 +551,10 @@ extern "C" int peco_quantize_gather(const void* q, const void* k, const void* v,
                                     void* v_packed, const int32_t* q_indices, const int32_t* k_indices,
                                     const int32_t* q_labels, const int32_t* k_labels, const float* q_centroids,
                                     const float* k_centroids, int q_clusters, int k_clusters, int bh, int seq,
-                                    int video, int dims, int bits, void* stream) {
+                                    int video, int dims, int bits, const int* plan, int gq, int gk,
+                                    void* stream) {
   if (bh < 1 || seq < 1 || video < 0 || video > seq || (bits != 0 && bits != 4 && bits != 8)) return kErrInvalidValue;
   return launch_quant_gather(q, k, v, q_packed, k_packed, v_packed, q_indices, k_indices, q_labels, k_labels,
-                             q_centroids, k_centroids, q_clusters, k_clusters, bh, seq, video, dims, bits,
-                             static_cast<cudaStream_t>(stream));
+                             q_centroids, k_centroids, q_clusters, k_clusters, bh, seq, video, dims, bits, plan, gq,
+                             gk, static_cast<cudaStream_t>(stream));
 }

@@ -4,15 +4,18 @@
 ``extend_text_partition`` and ``PecoAttention`` keep the reference's names,
 fields, validation and state semantics (centroids cached per layer across
 denoising steps, reset by ``reset``).  ``PecoAttention.attention`` runs the
-whole sparse call through four library entry points on the caller's stream:
+whole sparse call through five library entry points on the caller's stream:
 
 1. ``peco_kmeans_fit``      -- Q and K Lloyd iterations together, straight from
                                the bf16 video prefix (no fp32 copy);
 2. ``peco_select_text_partition`` -- cluster-pair selection written directly
                                into the text-extended map and sizes;
-3. ``peco_quantize_gather`` -- Base-Offset fake quant + cluster reorder of Q/K,
-                               reorder of V, text rows copied, one pass;
-4. ``peco_sparse_attention_restore`` -- tcgen05 sparse attention whose epilogue
+3. ``peco_attention_plan``  -- work units, per-unit key-cluster lists and the
+                               key-block layout of the packed K/V;
+4. ``peco_quantize_gather`` -- Base-Offset fake quant + cluster reorder of Q/K,
+                               reorder of V, text rows copied, one pass; K and
+                               V land directly in key blocks;
+5. ``peco_sparse_attention_restore`` -- tcgen05 sparse attention whose epilogue
                                writes rows back in the original token order.
 
 No host synchronisation happens inside a call.
@@ -173,7 +176,8 @@ class PecoAttention:
             raise ValueError("more clusters than video tokens")
         ev = None
         if self.stage_events is not None:
-            ev = {n: torch.cuda.Event(enable_timing=True) for n in ("start", "kmeans", "select", "gather", "attention")}
+            ev = {n: torch.cuda.Event(enable_timing=True)
+                  for n in ("start", "kmeans", "select", "plan", "gather", "attention")}
             self.stage_events.append(ev)
             ev["start"].record()
         qb, kb = self._update_cluster_state(q[:, :, :video], k[:, :, :video])
@@ -196,24 +200,34 @@ class PecoAttention:
                 ev["select"].record()
             if getattr(self, "keep_partition", False):
                 self.last_partition = (emap, qs_ext, ks_ext)
-            qp, kp, vp = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-            stream = _native.stream_of(dev, q, k, v, qp, kp, vp)
+            # plan first: it zeroes the padding rows of the key blocks and maps
+            # every packed key row to its block row for the gather
+            stride = int(lib.peco_attention_workspace_stride(s, s, gq, gk))
+            ws = torch.empty(h * stride, dtype=torch.int32, device=dev)
+            kblocks = torch.empty((h, int(lib.peco_key_block_rows(s, gk)), d), dtype=k.dtype, device=dev)
+            vblocks = torch.empty_like(kblocks)
+            stream = _native.stream_of(dev, ws, kblocks, vblocks)
+            st = lib.peco_attention_plan(_native.ptr(emap), _native.ptr(qs_ext), _native.ptr(ks_ext),
+                                         _native.ptr(kblocks), _native.ptr(vblocks), _native.ptr(ws), h, s, s, d,
+                                         gq, gk, stream)
+            _native.check(st, "peco_attention_plan")
+            if ev:
+                ev["plan"].record()
+            qp = torch.empty_like(q)
+            stream = _native.stream_of(dev, q, k, v, qp)
             st = lib.peco_quantize_gather(
-                _native.ptr(q), _native.ptr(k), _native.ptr(v), _native.ptr(qp), _native.ptr(kp), _native.ptr(vp),
-                _native.ptr(qb.perm), _native.ptr(kb.perm), _native.ptr(qb.labels), _native.ptr(kb.labels),
-                _native.ptr(self.q_centroids), _native.ptr(self.k_centroids), cq, ck, h, s, video, d,
-                int(self.config.base_offset_bits), stream)
+                _native.ptr(q), _native.ptr(k), _native.ptr(v), _native.ptr(qp), _native.ptr(kblocks),
+                _native.ptr(vblocks), _native.ptr(qb.perm), _native.ptr(kb.perm), _native.ptr(qb.labels),
+                _native.ptr(kb.labels), _native.ptr(self.q_centroids), _native.ptr(self.k_centroids), cq, ck, h, s,
+                video, d, int(self.config.base_offset_bits), _native.ptr(ws), gq, gk, stream)
             _native.check(st, "peco_quantize_gather")
             if ev:
                 ev["gather"].record()
             out = torch.empty_like(q)
-            stride = int(lib.peco_attention_workspace_stride(s, gq, gk))
-            ws = torch.empty(h * stride, dtype=torch.int32, device=dev)
-            stream = _native.stream_of(dev, qp, kp, vp, out, ws, qb.perm)
+            stream = _native.stream_of(dev, out, qb.perm)
             st = lib.peco_sparse_attention_restore(
-                _native.ptr(qp), _native.ptr(kp), _native.ptr(vp), _native.ptr(emap), _native.ptr(qs_ext),
-                _native.ptr(ks_ext), _native.ptr(out), _native.ptr(ws), h, s, s, d, gq, gk, _native.ptr(qb.perm),
-                video, stream)
+                _native.ptr(qp), _native.ptr(kblocks), _native.ptr(vblocks), _native.ptr(ws), _native.ptr(out), h, s,
+                s, d, gq, gk, _native.ptr(qb.perm), video, stream)
             _native.check(st, "peco_sparse_attention_restore")
             if ev:
                 ev["attention"].record()

@@ -141,12 +141,56 @@ def test_quantize_gather_bit_exact(bits):
     lib = _native.load()
     dev = Q.device
     args = [Q, K, V, *outs, qi.to(DEV), ki.to(DEV), ql.to(DEV), kl.to(DEV), qc.to(DEV), kc.to(DEV)]
-    st = lib.peco_quantize_gather(*[_native.ptr(t) for t in args], 16, 32, h, s, nv, d, bits,
+    st = lib.peco_quantize_gather(*[_native.ptr(t) for t in args], 16, 32, h, s, nv, d, bits, None, 0, 0,
                                   _native.stream_of(dev, *args))
     _native.check(st, "peco_quantize_gather")
     assert torch.equal(outs[0].cpu(), ref_q)
     assert torch.equal(outs[1].cpu(), ref_k)
     assert torch.equal(outs[2].cpu(), ref_v)
+
+
+def test_quantize_gather_writes_key_blocks():
+    """With a plan, K/V land in key blocks: identical to packing the
+    row-major result of the same pass."""
+    from peco_b200 import _native, attention_cuda
+    w = synthetic.workload("hv480", heads=2, grid=(2, 12, 18), text_length=32, valid_text=24, q_clusters=16,
+                           k_clusters=32)
+    q, k, v = synthetic.make_inputs(w, seed=12)
+    h, s, d, nv = w.heads, w.seq, w.dims, w.video_tokens
+    g = torch.Generator().manual_seed(3)
+    ql = torch.randint(16, (h, nv), generator=g, dtype=torch.int32)
+    kl = torch.randint(32, (h, nv), generator=g, dtype=torch.int32)
+    qc = torch.randn((h, 16, d), generator=g)
+    kc = torch.randn((h, 32, d), generator=g)
+    qi, ki = O.sort_indices(ql), O.sort_indices(kl)
+    qs = torch.cat((torch.bincount(ql[0], minlength=16).view(1, 1, 16).expand(1, h, 16),
+                    torch.tensor([24, 8]).view(1, 1, 2).expand(1, h, 2)), -1).int().contiguous()
+    ks = torch.cat((torch.stack([torch.bincount(kl[i], minlength=32) for i in range(h)]).view(1, h, 32),
+                    torch.tensor([24, 8]).view(1, 1, 2).expand(1, h, 2)), -1).int().contiguous()
+    dmap = torch.rand((1, h, 18, 34), generator=g) < 0.5
+    Q, K, V = (t.to(DEV).contiguous() for t in (q, k, v))
+    lib = _native.load()
+    dev = Q.device
+    rows = [torch.empty_like(Q) for _ in range(3)]
+    common = [qi.to(DEV), ki.to(DEV), ql.to(DEV), kl.to(DEV), qc.to(DEV), kc.to(DEV)]
+    st = lib.peco_quantize_gather(*[_native.ptr(t) for t in [Q, K, V, *rows, *common]], 16, 32, h, s, nv, d, 4,
+                                  None, 0, 0, _native.stream_of(dev, Q, K, V, *rows, *common))
+    _native.check(st, "peco_quantize_gather")
+    meta = [t.to(DEV).contiguous() for t in (dmap, qs, ks)]
+    ws, kb_ref, vb_ref = attention_cuda.plan_key_blocks(*meta, s, rows[1], rows[2])
+    qp = torch.empty_like(Q)
+    kb, vb = torch.empty_like(kb_ref), torch.empty_like(vb_ref)
+    st = lib.peco_attention_plan(*[_native.ptr(t) for t in (*meta, kb, vb, ws)], h, s, s, d, 18, 34,
+                                 _native.stream_of(dev, *meta, kb, vb, ws))
+    _native.check(st, "peco_attention_plan")
+    st = lib.peco_quantize_gather(*[_native.ptr(t) for t in [Q, K, V, qp, kb, vb, *common]], 16, 32, h, s, nv, d, 4,
+                                  _native.ptr(ws), 18, 34, _native.stream_of(dev, Q, K, V, qp, kb, vb, ws, *common))
+    _native.check(st, "peco_quantize_gather")
+    assert torch.equal(qp, rows[0])
+    for hh in range(h):  # blocks past the ones a head uses are never written
+        used = 8 * int(((ks[0, hh].long() + 7) // 8).sum())
+        assert torch.equal(kb[hh, :used].view(torch.int16), kb_ref[hh, :used].view(torch.int16))
+        assert torch.equal(vb[hh, :used].view(torch.int16), vb_ref[hh, :used].view(torch.int16))
 
 
 def _select_ties_explain(qc, kc, qs, ks, p, ratio, got, ref):

@@ -109,6 +109,48 @@ def test_dense_map_equals_full_attention():
     assert_close_attention(got, ref)
 
 
+def key_block_image(x, sizes, sk):
+    """Restatement of the key-block layout: row-major x [H,SK,D] (16-bit) ->
+    [H, blocks * 8, D] in block image order, and the blocks each head uses.
+    Cluster c (extent clamped to SK) starts block gp[c]; block b holds D/64
+    panels of 8 rows x 128 bytes and the 16-byte chunk c of row i sits at
+    chunk c ^ i; padding rows are zero (blocks past the used ones are left
+    unwritten by the kernels)."""
+    h, _, d = x.shape
+    gk = sizes.shape[-1]
+    blocks = (sk + 7) // 8 + gk
+    i = torch.arange(8).view(8, 1)
+    dd = torch.arange(d).view(1, d)
+    off = ((dd // 64) * 1024 + i * 128 + (((dd % 64) // 8) ^ i) * 16 + (dd % 8) * 2) // 2  # [8, D] element slots
+    img = torch.zeros((h, blocks, 8 * d), dtype=x.dtype)
+    used = []
+    for hh in range(h):
+        ends = torch.cumsum(sizes[hh].clamp_min(0).long(), 0).clamp_max(sk)
+        starts = torch.cat((torch.zeros(1, dtype=torch.long), ends[:-1]))
+        nb = (ends - starts + 7) // 8
+        gp = torch.cat((torch.zeros(1, dtype=torch.long), torch.cumsum(nb, 0)[:-1]))
+        for c in range(gk):
+            for r in range(int(ends[c] - starts[c])):
+                b, ii = divmod(int(gp[c]) * 8 + r, 8)
+                img[hh, b, off[ii]] = x[hh, int(starts[c]) + r]
+        used.append(int(nb.sum()))
+    return img.view(h, blocks * 8, d), used
+
+
+def test_key_blocks_match_layout_restatement():
+    """Plan + pack of row-major K/V reproduce the key-block image bit for bit."""
+    from peco_b200 import attention_cuda
+    for d, seed in ((128, 5), (64, 6)):
+        q, k, v, dmap, qs, ks = random_problem(2, 300, 290, d, 5, 9, torch.bfloat16, seed=seed)
+        ks[0, 1, 3] += 40  # sizes that overrun SK are clamped like the reference's work map
+        args = [t.to(DEV).contiguous() for t in (dmap, qs, ks, k, v)]
+        ws, kb, vb = attention_cuda.plan_key_blocks(args[0], args[1], args[2], 300, args[3], args[4])
+        for got, x in ((kb, k), (vb, v)):
+            ref, used = key_block_image(x[0], ks[0], 290)
+            for hh, n in enumerate(used):
+                assert torch.equal(got[hh, :8 * n].cpu().view(torch.int16), ref[hh, :8 * n].view(torch.int16))
+
+
 def _pipeline_inputs(w, seed, heads):
     """Packed Q/K/V, text-extended map and sizes of a real PECO call (oracle)."""
     q, k, v = synthetic.make_inputs(w, seed=seed, heads=heads)
@@ -153,11 +195,12 @@ def test_restore_epilogue_scatters_rows():
     out = torch.empty_like(args[0])
     lib = _native.load()
     gq, gk = em.shape[-2], em.shape[-1]
-    ws = torch.empty(h * lib.peco_attention_workspace_stride(s, gq, gk), dtype=torch.int32, device=DEV)
+    ws, kb, vb = attention_cuda.plan_key_blocks(args[3], args[4], args[5], s, args[1], args[2])
     perm = qi.to(DEV).contiguous()
-    keep = [*args, out, ws, perm]
-    st = lib.peco_sparse_attention_restore(*[_native.ptr(t) for t in args], _native.ptr(out), _native.ptr(ws), h, s,
-                                           s, d, gq, gk, _native.ptr(perm), nv, _native.stream_of(args[0].device, *keep))
+    keep = [args[0], kb, vb, ws, out, perm]
+    st = lib.peco_sparse_attention_restore(_native.ptr(args[0]), _native.ptr(kb), _native.ptr(vb), _native.ptr(ws),
+                                           _native.ptr(out), h, s, s, d, gq, gk, _native.ptr(perm), nv,
+                                           _native.stream_of(args[0].device, *keep))
     _native.check(st, "peco_sparse_attention_restore")
     text_idx = torch.arange(nv, s, dtype=torch.int32)
     idx = torch.cat((qi, text_idx.expand(h, -1)), -1)
