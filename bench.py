@@ -52,6 +52,8 @@ def parse_args():
     ap.add_argument("--config", default="hv480")
     ap.add_argument("--e2e-steps", type=int, default=100)
     ap.add_argument("--cpu-sample-heads", type=int, default=2)
+    ap.add_argument("--baselines", choices=("all", "none"), default="all",
+                    help="'none' skips the CPU and reference-GPU legs reported beside the line (for profiler runs)")
     return ap.parse_args()
 
 
@@ -425,7 +427,7 @@ def main():
     world, rank, local = dist_init(args.gpus)
     try:
         result, (inputs_w) = run_ours(args, world, rank, local)
-        if rank == 0 and world == 1:
+        if rank == 0 and world == 1 and args.baselines == "all":
             q_c, k_c, v_c, w = inputs_w
             ms, cores, sample = cpu_baseline(w, (q_c, k_c, v_c), args.cpu_sample_heads)
             result["cpu_baseline"] = {"value": round(ms, 1), "unit": "ms", "cores": cores, "kind": "port",

@@ -38,6 +38,7 @@ _SIGNATURES = {
     "peco_sparse_attention_restore": [P] * 5 + [I] * 6 + [P, I, P],
     "peco_attention_workspace_stride": [I, I, I, I],
     "peco_key_block_rows": [I, I],
+    "peco_kmeans_work_floats": [I, I],
     "peco_device_status": [P, I, P],
     "peco_error_string": [I],
     "peco_cluster_error_message": [I],
@@ -49,6 +50,7 @@ _RESTYPES = {
     "peco_launch_count": ctypes.c_ulonglong,
     "peco_attention_workspace_stride": LL,
     "peco_key_block_rows": LL,
+    "peco_kmeans_work_floats": LL,
     "peco_error_string": ctypes.c_char_p,
     "peco_cluster_error_message": ctypes.c_char_p,
     "peco_attention_error_string": ctypes.c_char_p,

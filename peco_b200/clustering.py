@@ -55,7 +55,9 @@ class KmeansBuffers:
         f32, i32 = torch.float32, torch.int32
         self.labels = torch.empty((bh, tokens), dtype=i32, device=device)
         self.centers = torch.empty((bh, clusters, dims), dtype=f32, device=device)
-        self.work = torch.empty((bh, clusters, dims), dtype=f32, device=device)
+        # ping-pong centres + the centres' bf16 tensor-core image
+        self.work = torch.empty((bh, int(_native.load().peco_kmeans_work_floats(clusters, dims))), dtype=f32,
+                                device=device)
         self.norms = torch.empty((bh, clusters), dtype=f32, device=device)
         self.counts = torch.empty((bh, clusters), dtype=i32, device=device)
         self.offsets = torch.empty((bh, clusters + 1), dtype=i32, device=device)

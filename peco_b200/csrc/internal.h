@@ -21,6 +21,7 @@ struct KmeansProblem {
   int32_t* counts;        // [B, C] sizes of the last partition
   int32_t* offsets;       // [B, C+1] cluster starts in the packed order
   int32_t* perm;          // [B, tokens] stable argsort of the last labels
+  unsigned char* image;   // [B, image bytes per head] bf16 hi/lo image of the centres being assigned against
 };
 
 int kmeans_fit_bf16(int njobs, const KmeansProblem* probs, int bh, int dims, int iters, cudaStream_t stream);

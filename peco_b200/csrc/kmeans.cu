@@ -10,12 +10,19 @@
 // the same accumulator).  The computed distance is then within
 //   E = 2^-12 ||x|| max||c|| + 2^-20 (max||c||^2 + 2 ||x|| max||c||)
 // of the fp32 distance (split residual, fp32 accumulation and the final
-// subtraction, with a 4x margin).  The epilogue keeps every centroid within
-// 2E of the best one: a single survivor is the fp32 argmin outright; several
-// survivors (near-ties) are recomputed exactly in fp32 on the CUDA cores and
-// the lowest index wins ties.  Labels therefore equal the fp32 argmin except
-// where two fp32 distances tie to rounding level.  fp32 inputs (the drop-in
-// entry point) also split x into bf16 hi + lo (three MMA terms).
+// subtraction, with a 4x margin).  The epilogue finds the minimum, then every
+// centroid within 2E of it: a single survivor is the fp32 argmin outright;
+// several survivors (near-ties) are recomputed exactly in fp32 on the CUDA
+// cores and the lowest index wins ties.  Labels therefore equal the fp32
+// argmin except where two fp32 distances tie to rounding level.  fp32 inputs
+// (the drop-in entry point) are split into bf16 hi + lo rows first (three MMA
+// terms).
+//
+// The bf16 hi/lo centroid split is computed once per iteration -- by the
+// update kernel, which produces the centroids -- and stored as the byte image
+// the tensor core reads from shared memory, so an assignment CTA fetches it
+// with bulk copies.  Token tiles arrive by TMA.  CTAs take equal-cost ranges
+// of the (problem, head, tile) list.
 //
 // Update (peco/kernels/kmeans.cu:179-196, peco/clustering.py:74-80): tokens
 // are stably sorted by label (counting sort), then one warp per cluster sums
@@ -30,333 +37,434 @@
 namespace peco {
 namespace {
 
-#ifdef PECO_KMEANS_STATS
-__device__ unsigned long long g_kstats[8];
-#endif
-
 constexpr int kTileM = 128;
-constexpr int kProdWarps = 4, kEpiWarps = 4;
-constexpr int kAssignThreads = 32 * (kProdWarps + 1 + kEpiWarps);
 constexpr int kMaxCand = 8;
-constexpr float kBoundScale = 2.44140625e-4f;   // 2^-12
+// warp 0: TMA / bulk-copy producer (and the centroid norms of each head);
+// warp 1: MMA issuer and TMEM owner; warps 2-9: epilogue, two warps per TMEM
+// lane quarter, each scanning half of the centroid columns
+constexpr int kEpiWarps = 8;
+constexpr int kMmaWarp = 1, kEpiWarp0 = 2;
+constexpr int kAssignThreads = 32 * (kEpiWarp0 + kEpiWarps);
+constexpr float kBoundScale = 2.44140625e-4f;      // 2^-12
 constexpr float kBoundTiny = 9.5367431640625e-7f;  // 2^-20
+constexpr int kCopyPiece = 32768;                  // bytes per bulk copy
+
+__host__ __device__ constexpr int round16(int v) { return (v + 15) & ~15; }
+
+// Centroid chunking: nc centroids per chunk (multiple of 16, <= 256).  The
+// image of one (head, chunk) is b_bytes = 2 nc D 2 bytes: the hi term, then
+// the lo term, each D/64 panels of nc rows x 128 bytes with the 128-byte
+// swizzle (16-byte chunk q of row j at q ^ (j % 8)); rows past C are zero.
+struct CenterGeom {
+  int nc, nchunks, b_bytes, panel_bytes, term_bytes;
+};
+__host__ __device__ inline CenterGeom center_geom(int C, int D) {
+  CenterGeom g;
+  g.nc = round16(C < 256 ? C : 256);
+  g.nchunks = (C + g.nc - 1) / g.nc;
+  g.panel_bytes = g.nc * 128;
+  g.term_bytes = g.nc * D * 2;
+  g.b_bytes = 2 * g.term_bytes;
+  return g;
+}
+
+// Byte offset of element d of centroid row j inside one chunk image term.
+__device__ __forceinline__ int image_offset(const CenterGeom& g, int j, int d) {
+  return (d >> 6) * g.panel_bytes + j * 128 + (((((d & 63) >> 3)) ^ (j & 7)) << 4) + (d & 7) * 2;
+}
+
+// Write E consecutive elements of centroid c (dims d0..d0+E-1, d0 % E == 0,
+// E in {1, 2, 4}) as bf16 hi + lo into the image of one head.
+template <int E>
+__device__ __forceinline__ void write_image(unsigned char* img_head, const CenterGeom& g, int c, int d0,
+                                            const float (&v)[E]) {
+  unsigned char* chunk = img_head + static_cast<long long>(c / g.nc) * g.b_bytes;
+  const int off = image_offset(g, c % g.nc, d0);
+  __nv_bfloat16 hi[E], lo[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    hi[e] = __float2bfloat16_rn(v[e]);
+    lo[e] = __float2bfloat16_rn(v[e] - __bfloat162float(hi[e]));
+  }
+  if constexpr (E == 4) {
+    *reinterpret_cast<uint2*>(chunk + off) = *reinterpret_cast<const uint2*>(hi);
+    *reinterpret_cast<uint2*>(chunk + g.term_bytes + off) = *reinterpret_cast<const uint2*>(lo);
+  } else if constexpr (E == 2) {
+    *reinterpret_cast<uint32_t*>(chunk + off) = *reinterpret_cast<const uint32_t*>(hi);
+    *reinterpret_cast<uint32_t*>(chunk + g.term_bytes + off) = *reinterpret_cast<const uint32_t*>(lo);
+  } else {
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      *reinterpret_cast<__nv_bfloat16*>(chunk + image_offset(g, c % g.nc, d0 + e)) = hi[e];
+      *reinterpret_cast<__nv_bfloat16*>(chunk + g.term_bytes + image_offset(g, c % g.nc, d0 + e)) = lo[e];
+    }
+  }
+}
+
+// Norms and image of a set of centroids: one warp per padded centroid row
+// (rows past C get a zero image).  centers [B, C, D]; norms [B, C];
+// image [B, nchunks * b_bytes].
+template <int D>
+__global__ void center_prep_kernel(const float* __restrict__ centers, float* __restrict__ norms,
+                                   unsigned char* __restrict__ image, int bh, int C) {
+  constexpr int E = D / 32;
+  const CenterGeom g = center_geom(C, D);
+  const int padded = g.nchunks * g.nc;
+  const long long w = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= static_cast<long long>(bh) * padded) return;
+  const int head = static_cast<int>(w / padded), c = static_cast<int>(w % padded);
+  float v[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) v[e] = c < C ? centers[(static_cast<long long>(head) * C + c) * D + lane * E + e] : 0.0f;
+  if (image) write_image<E>(image + static_cast<long long>(head) * g.nchunks * g.b_bytes, g, c, lane * E, v);
+  if (c < C && norms) {
+    float s = 0.0f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) s = fmaf(v[e], v[e], s);
+    s = warp_sum(s);
+    if (lane == 0) norms[static_cast<long long>(head) * C + c] = s;
+  }
+}
+
+// fp32 rows -> bf16 hi and lo rows (hi = rn(x), lo = rn(x - hi))
+__global__ void split_rows_kernel(const float4* __restrict__ x, uint2* __restrict__ hi, uint2* __restrict__ lo,
+                                  long long n4) {
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const float4 f = x[i];
+    const float v[4] = {f.x, f.y, f.z, f.w};
+    __nv_bfloat16 h[4], l[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      h[e] = __float2bfloat16_rn(v[e]);
+      l[e] = __float2bfloat16_rn(v[e] - __bfloat162float(h[e]));
+    }
+    hi[i] = *reinterpret_cast<const uint2*>(h);
+    lo[i] = *reinterpret_cast<const uint2*>(l);
+  }
+}
 
 struct AssignJob {
-  const void* x;            // token rows, bf16 or fp32, row length D
-  long long head_rows;      // rows between consecutive heads in x
-  int tokens;               // tokens per head
-  int clusters;             // centroids per head
-  const float* centers;     // [B, C, D]
-  const float* norms;       // [B, C] squared centroid norms
-  int32_t* labels;          // [B, tokens]
+  int tokens, clusters;
+  long long head_rows;          // rows between consecutive heads in the token maps
+  const float* x32;             // fp32 rows for the exact recompute (split mode), else null
+  const float* centers;         // [B, C, D] fp32 (exact recompute of near-ties)
+  const float* norms;           // [B, C]
+  const unsigned char* image;   // [B, nchunks * b_bytes]
+  int32_t* labels;              // [B, tokens]
 };
 
 struct AssignJobs {
   AssignJob job[2];
+  int njobs, bh;
+  long long items[2];   // (head, tile) items per problem
+  long long cost[2];    // cost of one item (centroid columns)
+  int ncta;
+};
+
+struct AssignMaps {
+  CUtensorMap xhi[2], xlo[2];   // bf16 token rows (lo: split mode only), box 64 x 128
 };
 
 struct __align__(8) AssignBars {
-  uint64_t a_full[2], a_empty[2], b_full[2], b_empty[2], acc_full[2], acc_empty[2];
+  uint64_t g_full, g_free;
+  uint64_t a_full[2], a_empty[2];
+  uint64_t b_full[2], b_empty[2];
+  uint64_t acc_full[2], acc_empty[2];
+  uint64_t xch_full[2];        // half 1 -> half 0 hand-off, per accumulator slot
+  float4 xch[2][kTileM];       // (best, runner-up, index bits, partial |x|^2)
   uint32_t tmem_base;
   int abort_flag;
-  float cmax;
 };
 
-__host__ __device__ constexpr int round16(int v) { return (v + 15) & ~15; }
-
-struct AssignGeom {
-  int nc;        // centroids per chunk (multiple of 16, <= 256)
-  int nchunks;
-  int a_bytes;   // one A slot: x as bf16 (hi [+ lo] for fp32 inputs)
-  int b_bytes;   // one B slot: a centroid chunk as bf16 hi + lo
-  int nbslots;   // B ring: 1 when the single chunk stays resident, else 2 (1 if smem is short)
-  int naslots;   // A ring: 2 (1 if smem is short)
-  int tmem_cols;
-  int norms_off; // byte offset of the staged centroid norms
-  int smem;      // dynamic smem bytes
+// Shared-memory carve-up common to every problem of a launch.
+struct AssignSmem {
+  int resident;     // 1: each head's single chunk stays in smem; 0: chunks stream through 2 slots
+  int nbslots, naslots;
+  int b_bytes, a_bytes, a_off, cn_off, cn_cap, smem;
 };
-
-__host__ __device__ inline AssignGeom assign_geom(int C, int D, bool xf32) {
-  AssignGeom g;
-  g.nc = round16(C < 256 ? C : 256);
-  g.nchunks = (C + g.nc - 1) / g.nc;
-  g.a_bytes = kTileM * D * 2 * (xf32 ? 2 : 1);
-  g.b_bytes = 2 * g.nc * D * 2;
-  g.nbslots = g.nchunks == 1 ? 1 : 2;
-  g.naslots = 2;
-  const int norm_bytes = ((C * 4) + 1023) & ~1023;
-  while (1024 + g.nbslots * g.b_bytes + g.naslots * g.a_bytes + norm_bytes > 225 * 1024 &&
-         (g.nbslots > 1 || g.naslots > 1)) {
-    if (g.nbslots > 1) g.nbslots = 1;
-    else g.naslots = 1;
+__host__ __device__ inline AssignSmem assign_smem(int C0, int C1, int njobs, int D, bool split) {
+  AssignSmem s;
+  int bmax = 0, cmax = 0;
+  bool all_single = true;
+  for (int j = 0; j < njobs; ++j) {
+    const CenterGeom g = center_geom(j ? C1 : C0, D);
+    bmax = bmax > g.b_bytes ? bmax : g.b_bytes;
+    const int cpad = (g.nchunks * g.nc + 31) & ~31;  // whole 32-column blocks
+    cmax = cmax > cpad ? cmax : cpad;
+    all_single = all_single && g.nchunks == 1;
   }
-  int cols = 2 * g.nc;
-  int p = 32;
-  while (p < cols) p <<= 1;
-  g.tmem_cols = p;
-  g.norms_off = g.nbslots * g.b_bytes + g.naslots * g.a_bytes;
-  g.smem = 1024 + g.norms_off + norm_bytes;
-  return g;
-}
-
-// swizzled 16-byte chunk store into a K-major panel tile (panel = 64 columns,
-// rows 128 bytes apart, ``panel_bytes`` between panels)
-__device__ __forceinline__ void store_row_chunk(unsigned char* tile, int row, int chunk, uint4 v, int panel_bytes) {
-  const int panel = chunk >> 3, c = chunk & 7;
-  *reinterpret_cast<uint4*>(tile + panel * panel_bytes + row * 128 + ((c ^ (row & 7)) << 4)) = v;
-}
-
-__device__ __forceinline__ uint4 load_row_chunk(const unsigned char* tile, int row, int chunk, int panel_bytes) {
-  const int panel = chunk >> 3, c = chunk & 7;
-  return *reinterpret_cast<const uint4*>(tile + panel * panel_bytes + row * 128 + ((c ^ (row & 7)) << 4));
-}
-
-// bf16 hi/lo split of 8 fp32 values: hi = rn(v), lo = rn(v - hi)
-__device__ __forceinline__ void split8(const float (&f)[8], uint4& hi, uint4& lo) {
-  uint32_t* hw = reinterpret_cast<uint32_t*>(&hi);
-  uint32_t* lw = reinterpret_cast<uint32_t*>(&lo);
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const float h0 = __bfloat162float(__float2bfloat16_rn(f[2 * e]));
-    const float h1 = __bfloat162float(__float2bfloat16_rn(f[2 * e + 1]));
-    hw[e] = pack_bf16x2(h0, h1);
-    lw[e] = pack_bf16x2(f[2 * e] - h0, f[2 * e + 1] - h1);
+  s.resident = all_single ? 1 : 0;
+  s.nbslots = all_single ? 1 : 2;
+  s.b_bytes = bmax;
+  s.a_bytes = kTileM * D * 2 * (split ? 2 : 1);
+  s.cn_cap = cmax;
+  s.naslots = 2;
+  for (;;) {
+    s.a_off = s.nbslots * s.b_bytes;
+    s.cn_off = s.a_off + s.naslots * s.a_bytes;
+      s.smem = 1024 + s.cn_off + ((cmax * 4 + 1023) & ~1023);
+    if (s.smem <= 227 * 1024) break;
+    if (s.nbslots > 1) s.nbslots = 1;       // streamed chunks: single-buffered
+    else if (s.naslots > 1) s.naslots = 1;  // then a single token tile
+    else break;
   }
+  return s;
 }
 
-template <int D, bool XF32>
-__global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const AssignJobs jobs, int tiles_per_cta,
-                                                                        unsigned* status) {
-  const AssignJob& J = jobs.job[blockIdx.z];
-  const int head = blockIdx.y;
-  const int C = J.clusters;
-  const int ntiles = (J.tokens + kTileM - 1) / kTileM;
-  const int t_begin = blockIdx.x * tiles_per_cta;
-  if (t_begin >= ntiles) return;
-  const int t_end = min(ntiles, t_begin + tiles_per_cta);
-  const int my_tiles = t_end - t_begin;
-  const AssignGeom G = assign_geom(C, D, XF32);
+// item f of the flattened list: problem j, head, tile (head-major per problem)
+struct Item {
+  int j, head, tile;
+};
+__device__ __forceinline__ Item decode_item(const AssignJobs& a, long long f) {
+  Item it;
+  it.j = f < a.items[0] ? 0 : 1;
+  const long long local = it.j ? f - a.items[0] : f;
+  const int nt = (a.job[it.j].tokens + kTileM - 1) / kTileM;
+  it.head = static_cast<int>(local / nt);
+  it.tile = static_cast<int>(local % nt);
+  return it;
+}
+// first item whose cumulative cost reaches x
+__device__ __forceinline__ long long item_at(const AssignJobs& a, long long x) {
+  const long long c0 = a.items[0] * a.cost[0];
+  if (x <= c0) return (x + a.cost[0] - 1) / a.cost[0];
+  const long long f = a.items[0] + (x - c0 + a.cost[1] - 1) / a.cost[1];
+  const long long total = a.items[0] + (a.njobs > 1 ? a.items[1] : 0);
+  return f < total ? f : total;
+}
+
+template <int D, bool SPLIT>
+__global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const __grid_constant__ AssignMaps maps,
+                                                                        const AssignJobs jobs, unsigned* status) {
+  const long long total_cost = jobs.items[0] * jobs.cost[0] + (jobs.njobs > 1 ? jobs.items[1] * jobs.cost[1] : 0);
+  const long long f_begin = item_at(jobs, total_cost * blockIdx.x / jobs.ncta);
+  const long long f_end = item_at(jobs, total_cost * (blockIdx.x + 1) / jobs.ncta);
+  if (f_begin >= f_end) return;
+  const AssignSmem S = assign_smem(jobs.job[0].clusters, jobs.njobs > 1 ? jobs.job[1].clusters : 1, jobs.njobs, D, SPLIT);
 
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  unsigned char* bslot[2] = {base, base + (G.nbslots > 1 ? G.b_bytes : 0)};
-  unsigned char* aslot0 = base + G.nbslots * G.b_bytes;
-  float* cn = reinterpret_cast<float*>(base + G.norms_off);  // squared centroid norms of this head
+  float* cn = reinterpret_cast<float*>(base + S.cn_off);  // centroid norms of the current head (+inf past C)
   __shared__ AssignBars sb;
-  __shared__ float xnorm[2][kTileM];
   volatile int* abort_flag = &sb.abort_flag;
-
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const float* cen = J.centers + static_cast<long long>(head) * C * D;
-  const float* norms = J.norms + static_cast<long long>(head) * C;
-  const int NA = G.naslots, NB = G.nbslots;
+  const int NA = S.naslots;
+
   if (threadIdx.x == 0) {
+    mbar_init(&sb.g_full, 32);
+    mbar_init(&sb.g_free, 1 + kEpiWarps);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&sb.a_full[i], 32 * kProdWarps);
+      mbar_init(&sb.a_full[i], 1);
       mbar_init(&sb.a_empty[i], kEpiWarps);
-      mbar_init(&sb.b_full[i], 32 * kProdWarps);
+      mbar_init(&sb.b_full[i], 1);
       mbar_init(&sb.b_empty[i], 1);
       mbar_init(&sb.acc_full[i], 1);
       mbar_init(&sb.acc_empty[i], kEpiWarps);
+      mbar_init(&sb.xch_full[i], kEpiWarps / 2);
     }
     sb.abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == kProdWarps) {
-    tmem_alloc(&sb.tmem_base, G.tmem_cols);
+  if (warp == kMmaWarp) {
+    tmem_alloc(&sb.tmem_base, 512);
     tmem_relinquish();
-  }
-  for (int c = threadIdx.x; c < C; c += blockDim.x) cn[c] = norms[c];
-  __syncthreads();
-  // max centroid norm of this head (bound scale)
-  if (warp == 0) {
-    float m = 0.0f;
-    for (int c = lane; c < C; c += 32) m = fmaxf(m, cn[c]);
-    m = warp_max(m);
-    if (lane == 0) sb.cmax = sqrtf(m);
   }
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sb.tmem_base;
-  const int a_panel = kTileM * 128;         // bytes per 64-column panel of an A tile
-  const int b_panel = G.nc * 128;           // bytes per 64-column panel of one B term
-  const int b_term = G.nc * D * 2;          // offset of the lo term in a B slot
+  const int a_panel = kTileM * 128;  // bytes per 64-column panel of an A tile
+  // group = (problem, head): the centroids in smem change with it
+  auto group_of = [&](const Item& it) { return it.j * jobs.bh + it.head; };
+  auto last_of_group = [&](long long f, const Item& it) {
+    if (f + 1 >= f_end) return true;
+    const Item nx = decode_item(jobs, f + 1);
+    return group_of(nx) != group_of(it);
+  };
 
-  if (warp < kProdWarps) {
-    // ------------------------------------------------------------ producers
-    const int tid = threadIdx.x;  // 0..127
-    bool ok = true;
-    auto load_b = [&](int chunk, unsigned char* dst) {
-      // centroid rows j = tid, tid + 128 of this chunk, fp32 -> bf16 hi + lo
-      for (int j = tid; j < G.nc; j += 32 * kProdWarps) {
-        const int c = chunk * G.nc + j;
-        const float4* src = reinterpret_cast<const float4*>(cen + static_cast<long long>(c) * D);
-#pragma unroll
-        for (int g = 0; g < D / 64; ++g) {
-          float4 buf[16];
-#pragma unroll
-          for (int u = 0; u < 16; ++u) buf[u] = c < C ? src[g * 16 + u] : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const float f[8] = {buf[2 * u].x, buf[2 * u].y, buf[2 * u].z, buf[2 * u].w,
-                                buf[2 * u + 1].x, buf[2 * u + 1].y, buf[2 * u + 1].z, buf[2 * u + 1].w};
-            uint4 hi, lo;
-            split8(f, hi, lo);
-            store_row_chunk(dst, j, g * 8 + u, hi, b_panel);
-            store_row_chunk(dst + b_term, j, g * 8 + u, lo, b_panel);
-          }
-        }
-      }
-      fence_async_smem();
-    };
-    if (G.nchunks == 1) {
-      load_b(0, bslot[0]);
-      mbar_arrive(&sb.b_full[0]);
+  if (warp == 0) {
+    // ------------------------------------------------ TMA / bulk producer
+    if (lane == 0) {
+      prefetch_tensormap(&maps.xhi[0]);
+      if (jobs.njobs > 1) prefetch_tensormap(&maps.xhi[1]);
     }
-    for (int i = 0; i < my_tiles && ok; ++i) {
-      const int tile = t_begin + i;
-      const int s = i % NA, use = i / NA;
-      if (use > 0) ok = mbar_wait_warp(&sb.a_empty[s], (use - 1) & 1, abort_flag, status);
-      if (!ok) break;
-      unsigned char* a_hi = aslot0 + s * G.a_bytes;
-      unsigned char* a_lo = a_hi + kTileM * D * 2;
-      const int row = tid;
-      const int tok = tile * kTileM + row;
-      float ss = 0.0f;
-      if (tok < J.tokens) {
-        const long long grow = static_cast<long long>(head) * J.head_rows + tok;
-        if (XF32) {
-          const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(J.x) + grow * D);
-#pragma unroll
-          for (int g = 0; g < D / 64; ++g) {
-            float4 buf[16];
-#pragma unroll
-            for (int u = 0; u < 16; ++u) buf[u] = src[g * 16 + u];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              const float f[8] = {buf[2 * u].x, buf[2 * u].y, buf[2 * u].z, buf[2 * u].w,
-                                  buf[2 * u + 1].x, buf[2 * u + 1].y, buf[2 * u + 1].z, buf[2 * u + 1].w};
-#pragma unroll
-              for (int e = 0; e < 8; ++e) ss = fmaf(f[e], f[e], ss);
-              uint4 hi, lo;
-              split8(f, hi, lo);
-              store_row_chunk(a_hi, row, g * 8 + u, hi, a_panel);
-              store_row_chunk(a_lo, row, g * 8 + u, lo, a_panel);
-            }
-          }
+    bool ok = true;
+    int group = -1, ngroups = 0, bchunk = 0;
+    long long i = 0;
+    for (long long f = f_begin; f < f_end && ok; ++f, ++i) {
+      const Item it = decode_item(jobs, f);
+      const AssignJob& J = jobs.job[it.j];
+      const CenterGeom cg = center_geom(J.clusters, D);
+      const unsigned char* img = J.image + static_cast<long long>(it.head) * cg.nchunks * cg.b_bytes;
+      if (group_of(it) != group) {
+        if (ngroups > 0) ok = mbar_wait_warp(&sb.g_free, (ngroups - 1) & 1, abort_flag, status);
+        if (!ok) break;
+        // centroid norms (+inf for padding columns) and, when resident, the image
+        const float* nr = J.norms + static_cast<long long>(it.head) * J.clusters;
+        for (int c = lane; c < ((cg.nchunks * cg.nc + 31) & ~31); c += 32) cn[c] = c < J.clusters ? nr[c] : INFINITY;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&sb.g_full, S.resident ? cg.b_bytes : 0);
+          if (S.resident)
+            for (int off = 0; off < cg.b_bytes; off += kCopyPiece)
+              bulk_load(base + off, img + off, min(kCopyPiece, cg.b_bytes - off), &sb.g_full);
         } else {
-          const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(J.x) + grow * D);
-          uint4 buf[D / 8];
-#pragma unroll
-          for (int ch = 0; ch < D / 8; ++ch) buf[ch] = src[ch];
-#pragma unroll
-          for (int ch = 0; ch < D / 8; ++ch) {
-            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&buf[ch]);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 f = __bfloat1622float2(h[e]);
-              ss = fmaf(f.x, f.x, ss);
-              ss = fmaf(f.y, f.y, ss);
-            }
-            store_row_chunk(a_hi, row, ch, buf[ch], a_panel);
-          }
+          mbar_arrive(&sb.g_full);
         }
-      } else {
-        for (int ch = 0; ch < D / 8; ++ch) {
-          store_row_chunk(a_hi, row, ch, make_uint4(0, 0, 0, 0), a_panel);
-          if (XF32) store_row_chunk(a_lo, row, ch, make_uint4(0, 0, 0, 0), a_panel);
+        group = group_of(it);
+        ++ngroups;
+      }
+      const int s = static_cast<int>(i % NA);
+      if (i >= NA) ok = mbar_wait_warp(&sb.a_empty[s], ((i / NA) - 1) & 1, abort_flag, status);
+      if (!ok) break;
+      if (lane == 0) {
+        unsigned char* a = base + S.a_off + s * S.a_bytes;
+        mbar_arrive_expect_tx(&sb.a_full[s], S.a_bytes);
+        const int row = static_cast<int>(static_cast<long long>(it.head) * J.head_rows + static_cast<long long>(it.tile) * kTileM);
+#pragma unroll
+        for (int p = 0; p < D / 64; ++p) {
+          tma_load_2d(a + p * a_panel, &maps.xhi[it.j], 64 * p, row, &sb.a_full[s]);
+          if (SPLIT) tma_load_2d(a + kTileM * D * 2 + p * a_panel, &maps.xlo[it.j], 64 * p, row, &sb.a_full[s]);
         }
       }
-      xnorm[s][row] = sqrtf(ss);
-      fence_async_smem();
-      mbar_arrive(&sb.a_full[s]);
-      if (G.nchunks > 1) {
-        for (int k = 0; k < G.nchunks && ok; ++k) {
-          const int g = i * G.nchunks + k;
-          const int bs = g % NB, bu = g / NB;
+      if (!S.resident) {
+        for (int k = 0; k < cg.nchunks && ok; ++k, ++bchunk) {
+          const int bs = bchunk % S.nbslots, bu = bchunk / S.nbslots;
           if (bu > 0) ok = mbar_wait_warp(&sb.b_empty[bs], (bu - 1) & 1, abort_flag, status);
           if (!ok) break;
-          load_b(k, bslot[bs]);
-          mbar_arrive(&sb.b_full[bs]);
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&sb.b_full[bs], cg.b_bytes);
+            for (int off = 0; off < cg.b_bytes; off += kCopyPiece)
+              bulk_load(base + bs * S.b_bytes + off, img + static_cast<long long>(k) * cg.b_bytes + off,
+                        min(kCopyPiece, cg.b_bytes - off), &sb.b_full[bs]);
+          }
         }
       }
+      __syncwarp();
     }
-  } else if (warp == kProdWarps) {
+    __syncwarp();
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------ MMA
     if (lane == 0) {
-      const uint32_t idesc = instr_desc(128, G.nc, 1, false, false);
       bool ok = true;
-      int last_g = -1;
-      if (G.nchunks == 1) ok = mbar_wait(&sb.b_full[0], 0, abort_flag, status);
-      for (int i = 0; i < my_tiles && ok; ++i) {
-        const int s = i % NA;
-        ok = mbar_wait(&sb.a_full[s], (i / NA) & 1, abort_flag, status);
+      int group = -1, ngroups = 0, bchunk = 0, gacc = 0;
+      long long i = 0;
+      for (long long f = f_begin; f < f_end && ok; ++f, ++i) {
+        const Item it = decode_item(jobs, f);
+        const CenterGeom cg = center_geom(jobs.job[it.j].clusters, D);
+        const uint32_t idesc = instr_desc(128, cg.nc, 1, false, false);
+        if (group_of(it) != group) {
+          ok = mbar_wait(&sb.g_full, ngroups & 1, abort_flag, status);
+          group = group_of(it);
+          ++ngroups;
+        }
+        const int s = static_cast<int>(i % NA);
+        if (ok) ok = mbar_wait(&sb.a_full[s], (i / NA) & 1, abort_flag, status);
         if (!ok) break;
-        const uint32_t a_hi = smem_u32(aslot0 + s * G.a_bytes);
+        const uint32_t a_hi = smem_u32(base + S.a_off + s * S.a_bytes);
         const uint32_t a_lo = a_hi + kTileM * D * 2;
-        for (int k = 0; k < G.nchunks && ok; ++k) {
-          const int g = i * G.nchunks + k;
-          const int as = g & 1, au = g >> 1;
-          if (au > 0) ok = mbar_wait(&sb.acc_empty[as], (au - 1) & 1, abort_flag, status);
+        for (int k = 0; k < cg.nchunks && ok; ++k, ++gacc) {
+          const int as = gacc & 1;
+          if (gacc >= 2) ok = mbar_wait(&sb.acc_empty[as], ((gacc >> 1) - 1) & 1, abort_flag, status);
           int bs = 0;
-          if (ok && G.nchunks > 1) {
-            bs = g % NB;
-            ok = mbar_wait(&sb.b_full[bs], (g / NB) & 1, abort_flag, status);
+          if (ok && !S.resident) {
+            bs = bchunk % S.nbslots;
+            ok = mbar_wait(&sb.b_full[bs], (bchunk / S.nbslots) & 1, abort_flag, status);
+            ++bchunk;
           }
           if (!ok) break;
           tc_fence_after();
-          const uint32_t b_hi = smem_u32(bslot[bs]);
-          const uint32_t b_lo = b_hi + b_term;
-          const uint32_t acc = tmem + as * G.nc;
+          const uint32_t b_hi = smem_u32(base + bs * S.b_bytes);
+          const uint32_t b_lo = b_hi + cg.term_bytes;
+          const uint32_t acc = tmem + as * 256;
           // terms, smallest first: x.c_lo, [x_lo.c_hi], x.c_hi
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t off_a = (kk >> 2) * a_panel + (kk & 3) * 32;
-            const uint32_t off_b = (kk >> 2) * b_panel + (kk & 3) * 32;
+            const uint32_t off_b = (kk >> 2) * cg.panel_bytes + (kk & 3) * 32;
             umma_ss(acc, smem_desc(a_hi + off_a, 16, 1024), smem_desc(b_lo + off_b, 16, 1024), idesc, kk > 0 ? 1u : 0u);
           }
-          if (XF32) {
+          if (SPLIT) {
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk) {
               const uint32_t off_a = (kk >> 2) * a_panel + (kk & 3) * 32;
-              const uint32_t off_b = (kk >> 2) * b_panel + (kk & 3) * 32;
+              const uint32_t off_b = (kk >> 2) * cg.panel_bytes + (kk & 3) * 32;
               umma_ss(acc, smem_desc(a_lo + off_a, 16, 1024), smem_desc(b_hi + off_b, 16, 1024), idesc, 1u);
             }
           }
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t off_a = (kk >> 2) * a_panel + (kk & 3) * 32;
-            const uint32_t off_b = (kk >> 2) * b_panel + (kk & 3) * 32;
+            const uint32_t off_b = (kk >> 2) * cg.panel_bytes + (kk & 3) * 32;
             umma_ss(acc, smem_desc(a_hi + off_a, 16, 1024), smem_desc(b_hi + off_b, 16, 1024), idesc, 1u);
           }
           umma_commit(&sb.acc_full[as]);
-          if (G.nchunks > 1) umma_commit(&sb.b_empty[bs]);
-          last_g = g;
+          if (!S.resident) umma_commit(&sb.b_empty[bs]);
         }
+        if (ok && last_of_group(f, it)) umma_commit(&sb.g_free);
       }
-      if (last_g >= 0) mbar_wait(&sb.acc_full[last_g & 1], (last_g >> 1) & 1, abort_flag, status);
+      // drain our MMAs before TMEM is released
+      if (gacc > 0) mbar_wait(&sb.acc_full[(gacc - 1) & 1], ((gacc - 1) >> 1) & 1, abort_flag, status);
     }
     __syncwarp();
   } else {
     // ------------------------------------------------------------- epilogue
     const int quarter = warp & 3;
+    const int half = (warp - kEpiWarp0) >> 2;  // which half of the columns (and of x's dims)
     const int r = quarter * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const float cmax = sb.cmax;
     bool ok = true;
-    for (int i = 0; i < my_tiles && ok; ++i) {
-      const int tile = t_begin + i;
-      const int s = i % NA;
+    int group = -1, ngroups = 0, gacc = 0;
+    float cmax = 0.0f;
+    long long i = 0;
+    for (long long f = f_begin; f < f_end && ok; ++f, ++i) {
+      const Item it = decode_item(jobs, f);
+      const AssignJob& J = jobs.job[it.j];
+      const int C = J.clusters;
+      const CenterGeom cg = center_geom(C, D);
+      if (group_of(it) != group) {
+        ok = mbar_wait_warp(&sb.g_full, ngroups & 1, abort_flag, status);
+        if (!ok) break;
+        float m = 0.0f;
+        for (int c = lane; c < C; c += 32) m = fmaxf(m, cn[c]);
+        cmax = sqrtf(warp_max(m));
+        group = group_of(it);
+        ++ngroups;
+      }
+      const int s = static_cast<int>(i % NA);
       ok = mbar_wait_warp(&sb.a_full[s], (i / NA) & 1, abort_flag, status);
       if (!ok) break;
-      const float xn = xnorm[s][r];
-      const float E2 = 2.0f * (kBoundScale * xn * cmax + kBoundTiny * (cmax * cmax + 2.0f * xn * cmax));
+      const unsigned char* a_hi = base + S.a_off + s * S.a_bytes;
+      // this half's share of |x|^2: dims [half D/2, (half + 1) D/2)
+      float ss = 0.0f;
+#pragma unroll
+      for (int h8 = 0; h8 < D / 16; ++h8) {
+        const int ch = half * (D / 16) + h8;
+        const int off = (ch >> 3) * a_panel + r * 128 + (((ch & 7) ^ (r & 7)) << 4);
+        const uint4 u = *reinterpret_cast<const uint4*>(a_hi + off);
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+        float2 lo2[4] = {};
+        if (SPLIT) {
+          const uint4 w = *reinterpret_cast<const uint4*>(a_hi + kTileM * D * 2 + off);
+          const __nv_bfloat162* l2 = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) lo2[e] = __bfloat1622float2(l2[e]);
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f2 = __bfloat1622float2(h2[e]);
+          const float x0 = f2.x + lo2[e].x, x1 = f2.y + lo2[e].y;
+          ss = fmaf(x0, x0, ss);
+          ss = fmaf(x1, x1, ss);
+        }
+      }
+      float E2 = 0.0f;  // half 0: bound once both norm halves are known
       float best = INFINITY;
       float cd[kMaxCand];
       int ci[kMaxCand];
       int ncand = 0;
       bool overflow = false;
-      // keep entries within ``t`` (order preserved: slot m <= q)
+      // keep entries within ``t`` (order preserved)
       auto prune = [&](float t) {
         int m = 0;
 #pragma unroll
@@ -372,52 +480,131 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
         }
         ncand = m;
       };
-      for (int k = 0; k < G.nchunks && ok; ++k) {
-        const int g = i * G.nchunks + k;
-        const int as = g & 1;
-        ok = mbar_wait_warp(&sb.acc_full[as], (g >> 1) & 1, abort_flag, status);
+      auto push = [&](float dj, int c) {
+        if (ncand < kMaxCand) {
+#pragma unroll
+          for (int q = 0; q < kMaxCand; ++q)
+            if (q == ncand) {
+              cd[q] = dj;
+              ci[q] = c;
+            }
+          ++ncand;
+        } else {
+          overflow = true;
+        }
+      };
+      for (int k = 0; k < cg.nchunks && ok; ++k, ++gacc) {
+        const int as = gacc & 1;
+        ok = mbar_wait_warp(&sb.acc_full[as], (gacc >> 1) & 1, abort_flag, status);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t acc = tmem + as * G.nc + lane_off;
-        for (int c0 = 0; c0 < G.nc; c0 += 32) {
+        const uint32_t acc = tmem + as * 256 + lane_off;
+        const float* cnk = cn + k * cg.nc;
+        const int nblk = cg.nc / 32 + ((cg.nc & 31) ? 1 : 0);
+        const int nb0 = (nblk + 1) >> 1;  // half 0 takes blocks [0, nb0), half 1 the rest
+        const int blo = half ? nb0 : 0, bhi = half ? nblk : nb0;
+        // One pass over this half's blocks: best distance d = |c|^2 - 2 x.c,
+        // its index and the runner-up, in four independent chains (column
+        // j mod 4); 64 columns per TMEM wait.  Block loops stay rolled: the
+        // unrolled body must fit the instruction cache.
+        float b1[4], b2[4];
+        int bi[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          b1[e] = INFINITY;
+          b2[e] = INFINITY;
+          bi[e] = 0x7fffffff;
+        }
+        auto scan_block = [&](const uint32_t* v, int b) {
+          const float4* c4 = reinterpret_cast<const float4*>(cnk + b * 32);
+          const int cbase = k * cg.nc + b * 32;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 nq = c4[q];
+            const float nv[4] = {nq.x, nq.y, nq.z, nq.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float d = fmaf(-2.0f, __uint_as_float(v[4 * q + e]), nv[e]);
+              const bool lt = d < b1[e];
+              b2[e] = fminf(b2[e], fmaxf(d, b1[e]));
+              bi[e] = lt ? cbase + 4 * q + e : bi[e];
+              b1[e] = fminf(b1[e], d);
+            }
+          }
+        };
+#pragma unroll 1
+        for (int b = blo; b + 1 < bhi; b += 2) {
+          uint32_t v[64];
+          tmem_ld64_sync(acc + b * 32, v);
+          scan_block(v, b);
+          scan_block(v + 32, b + 1);
+        }
+        if ((bhi - blo) & 1) {
           uint32_t v[32];
+          tmem_ld32_sync(acc + (bhi - 1) * 32, v);
+          scan_block(v, bhi - 1);
+        }
+        float m1 = b1[0], m2 = b2[0];
+        int i1 = bi[0];
+#pragma unroll
+        for (int e = 1; e < 4; ++e) {
+          m2 = fminf(fminf(m2, b2[e]), fmaxf(m1, b1[e]));
+          if (b1[e] < m1 || (b1[e] == m1 && bi[e] < i1)) i1 = bi[e];
+          m1 = fminf(m1, b1[e]);
+        }
+        if (half == 1) {
+          // hand this half's result to half 0 and move on
+          sb.xch[as][r] = make_float4(m1, m2, __int_as_float(i1), ss);
+          tc_fence_before();
           __syncwarp();
-          tmem_ld32_sync(acc + c0, v);
-          const int cb = k * G.nc + c0;
-          float d[32];
-          float mn = INFINITY;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int c = cb + j;
-            d[j] = (c < C) ? fmaf(-2.0f, __uint_as_float(v[j]), cn[c]) : INFINITY;
-            mn = fminf(mn, d[j]);
+          if (lane == 0) {
+            mbar_arrive(&sb.xch_full[as]);
+            mbar_arrive(&sb.acc_empty[as]);
           }
-          best = fminf(best, mn);
-          const float thr = best + E2;
-          // Candidates of this block as a bit mask; the (rare) pushes run in
-          // one compact loop instead of 32 unrolled copies.
-          unsigned m = 0;
-          if (mn <= thr) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) m |= (d[j] <= thr ? 1u : 0u) << j;
+          continue;
+        }
+        ok = mbar_wait_warp(&sb.xch_full[as], (gacc >> 1) & 1, abort_flag, status);
+        if (!ok) break;
+        {
+          const float4 o = sb.xch[as][r];
+          const int oi = __float_as_int(o.z);
+          m2 = fminf(fminf(m2, o.y), fmaxf(m1, o.x));
+          if (o.x < m1 || (o.x == m1 && oi < i1)) i1 = oi;
+          m1 = fminf(m1, o.x);
+          if (k == 0) {
+            const float xn = sqrtf(ss + o.w);
+            E2 = 2.0f * (kBoundScale * xn * cmax + kBoundTiny * (cmax * cmax + 2.0f * xn * cmax));
           }
-          while (m) {
-            const int j = __ffs(m) - 1;
-            m &= m - 1;
-            float dj = 0.0f;
+        }
+        best = fminf(best, m1);
+        const float thr = best + E2;
+        if (ncand > 0) prune(thr);
+        // candidates of this chunk: none (m1 > thr), exactly its best
+        // (runner-up > thr), or several -- then rescan it (rare)
+        const bool many = m1 <= thr && m2 <= thr;
+        if (m1 <= thr && !many) push(m1, i1);
+        if (__any_sync(0xffffffffu, many)) {
+#pragma unroll 1
+          for (int b = 0; b < nblk; ++b) {
+            uint32_t v[32];
+            tmem_ld32_sync(acc + b * 32, v);
+            const float4* c4 = reinterpret_cast<const float4*>(cnk + b * 32);
+            unsigned m = 0;
 #pragma unroll
-            for (int jj = 0; jj < 32; ++jj) dj = (jj == j) ? d[jj] : dj;
-            if (ncand == kMaxCand) prune(thr);
-            if (ncand < kMaxCand) {
-#pragma unroll
-              for (int q = 0; q < kMaxCand; ++q)
-                if (q == ncand) {
-                  cd[q] = dj;
-                  ci[q] = cb + j;
-                }
-              ++ncand;
-            } else {
-              overflow = true;
+            for (int q = 0; q < 8; ++q) {
+              const float4 nq = c4[q];
+              m |= (fmaf(-2.0f, __uint_as_float(v[4 * q + 0]), nq.x) <= thr ? 1u : 0u) << (4 * q + 0);
+              m |= (fmaf(-2.0f, __uint_as_float(v[4 * q + 1]), nq.y) <= thr ? 1u : 0u) << (4 * q + 1);
+              m |= (fmaf(-2.0f, __uint_as_float(v[4 * q + 2]), nq.z) <= thr ? 1u : 0u) << (4 * q + 2);
+              m |= (fmaf(-2.0f, __uint_as_float(v[4 * q + 3]), nq.w) <= thr ? 1u : 0u) << (4 * q + 3);
+            }
+            if (!many) m = 0;
+            // distances recorded as the chunk's best (a lower bound): a later
+            // prune keeps them and the exact recompute settles them
+            while (m) {
+              const int jb = __ffs(m) - 1;
+              m &= m - 1;
+              push(m1, k * cg.nc + b * 32 + jb);
             }
           }
         }
@@ -426,113 +613,98 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
         if (lane == 0) mbar_arrive(&sb.acc_empty[as]);
       }
       if (!ok) break;
-      const int tok = tile * kTileM + r;
-      const bool valid = tok < J.tokens;
-      prune(best + E2);
-      int label = ncand > 0 ? ci[0] : 0;
-      // Near-ties are recomputed in exact fp32, one token at a time by the
-      // whole warp: lane l owns D/32 consecutive dimensions, so each
-      // candidate centroid row is one coalesced load, and all candidates of
-      // the token are in flight together.
-      unsigned amb = __ballot_sync(0xffffffffu, valid && (overflow || ncand > 1));
-      constexpr int E = D / 32;
-      const unsigned char* a_hi = aslot0 + s * G.a_bytes;
-      while (amb) {
-        const int src = __ffs(amb) - 1;
-        amb &= amb - 1;
-        const int stok = __shfl_sync(0xffffffffu, tok, src);
-        const int n = __shfl_sync(0xffffffffu, overflow ? -1 : ncand, src);
-        const long long grow = static_cast<long long>(head) * J.head_rows + stok;
-        float xv[E];
-        if (XF32) {
-          const float* xr = static_cast<const float*>(J.x) + grow * D + lane * E;
+      if (half == 0) {
+        const int tok = it.tile * kTileM + r;
+        const bool valid = tok < J.tokens;
+        if (ncand > 1) prune(best + E2);
+        int label = ncand > 0 ? ci[0] : 0;
+        // Near-ties are recomputed in exact fp32, one token at a time by the
+        // whole warp: lane l owns D/32 consecutive dimensions, so each
+        // candidate centroid row is one coalesced load, and all candidates of
+        // the token are in flight together.
+        unsigned amb = __ballot_sync(0xffffffffu, valid && (overflow || ncand > 1));
+        constexpr int E = D / 32;
+        const float* cen = J.centers + static_cast<long long>(it.head) * C * D;
+        while (amb) {
+          const int src = __ffs(amb) - 1;
+          amb &= amb - 1;
+          const int stok = __shfl_sync(0xffffffffu, tok, src);
+          const int n = __shfl_sync(0xffffffffu, overflow ? -1 : ncand, src);
+          float xv[E];
+          if (SPLIT) {
+            const float* xr = J.x32 + (static_cast<long long>(it.head) * J.head_rows + stok) * D + lane * E;
 #pragma unroll
-          for (int e = 0; e < E; ++e) xv[e] = xr[e];
-        } else {
-          const int srow = quarter * 32 + src;
-          const uint4 u = load_row_chunk(a_hi, srow, (lane * E) >> 3, a_panel);
-          const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u) + ((lane * E) & 7);
+            for (int e = 0; e < E; ++e) xv[e] = xr[e];
+          } else {
+            const int srow = quarter * 32 + src;
+            const int d0 = lane * E;
+            const uint4 u = *reinterpret_cast<const uint4*>(a_hi + (d0 >> 6) * a_panel + srow * 128 +
+                                                            ((((d0 & 63) >> 3) ^ (srow & 7)) << 4));
+            const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u) + (d0 & 7);
 #pragma unroll
-          for (int e = 0; e < E; ++e) xv[e] = __bfloat162float(h[e]);
-        }
-        float bd = INFINITY;
-        int bl = 0x7fffffff;
-        auto score = [&](int id, float partial) {
-          const float dot = warp_sum(partial);
-          const float e = __fsub_rn(cn[id], 2.0f * dot);
-          if (e < bd || (e == bd && id < bl)) {
-            bd = e;
-            bl = id;
+            for (int e = 0; e < E; ++e) xv[e] = __bfloat162float(h[e]);
           }
-        };
-        if (n >= 0) {
-          float part[kMaxCand];
-          int ids[kMaxCand];
-#pragma unroll
-          for (int q = 0; q < kMaxCand; ++q) {
-            ids[q] = __shfl_sync(0xffffffffu, ci[q], src);
-            part[q] = 0.0f;
-            if (q < n) {
-              const float* cr = cen + static_cast<long long>(ids[q]) * D + lane * E;
-#pragma unroll
-              for (int e = 0; e < E; ++e) part[q] = fmaf(xv[e], cr[e], part[q]);
+          float bd = INFINITY;
+          int bl = 0x7fffffff;
+          auto score = [&](int id, float partial) {
+            const float dot = warp_sum(partial);
+            const float e = __fsub_rn(cn[id], 2.0f * dot);
+            if (e < bd || (e == bd && id < bl)) {
+              bd = e;
+              bl = id;
             }
-          }
+          };
+          if (n >= 0) {
+            float part[kMaxCand];
+            int ids[kMaxCand];
 #pragma unroll
-          for (int q = 0; q < kMaxCand; ++q)
-            if (q < n) score(ids[q], part[q]);
-        } else {
-          for (int c0 = 0; c0 < C; c0 += 4) {
-            float part[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
+            for (int q = 0; q < kMaxCand; ++q) {
+              ids[q] = __shfl_sync(0xffffffffu, ci[q], src);
               part[q] = 0.0f;
-              const int id = min(c0 + q, C - 1);
-              const float* cr = cen + static_cast<long long>(id) * D + lane * E;
+              if (q < n) {
+                const float* cr = cen + static_cast<long long>(ids[q]) * D + lane * E;
 #pragma unroll
-              for (int e = 0; e < E; ++e) part[q] = fmaf(xv[e], cr[e], part[q]);
+                for (int e = 0; e < E; ++e) part[q] = fmaf(xv[e], cr[e], part[q]);
+              }
             }
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-              if (c0 + q < C) score(c0 + q, part[q]);
+            for (int q = 0; q < kMaxCand; ++q)
+              if (q < n) score(ids[q], part[q]);
+          } else {
+#pragma unroll 1
+            for (int c0 = 0; c0 < C; c0 += 4) {
+              float part[4];
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                part[q] = 0.0f;
+                const int id = min(c0 + q, C - 1);
+                const float* cr = cen + static_cast<long long>(id) * D + lane * E;
+#pragma unroll
+                for (int e = 0; e < E; ++e) part[q] = fmaf(xv[e], cr[e], part[q]);
+              }
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+                if (c0 + q < C) score(c0 + q, part[q]);
+            }
           }
+          if (lane == src) label = bl;
         }
-        if (lane == src) label = bl;
-      }
-      if (valid) {
-        J.labels[static_cast<long long>(head) * J.tokens + tok] = label;
-#ifdef PECO_KMEANS_STATS
-        // debug builds: [0] tokens, [1] survivors after pruning, [2] overflows, [3] tokens needing a recompute
-        atomicAdd(&g_kstats[0], 1ull);
-        atomicAdd(&g_kstats[1], static_cast<unsigned long long>(ncand));
-        if (overflow) atomicAdd(&g_kstats[2], 1ull);
-        if (ncand > 1) atomicAdd(&g_kstats[3], 1ull);
-#endif
+        if (valid) J.labels[static_cast<long long>(it.head) * J.tokens + tok] = label;
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sb.a_empty[s]);
+      if (lane == 0) {
+        mbar_arrive(&sb.a_empty[s]);
+        if (last_of_group(f, it)) mbar_arrive(&sb.g_free);
+      }
     }
   }
   __syncwarp();
   tc_fence_before();
   __syncthreads();
-  if (warp == kProdWarps) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
-    tmem_dealloc(tmem, G.tmem_cols);
+    tmem_dealloc(tmem, 512);
   }
-}
-
-// ||c||^2 per centroid (fp32, one warp per centroid); writes norms [rows].
-__global__ void center_norms_kernel(const float* __restrict__ centers, float* __restrict__ norms, long long rows,
-                                    int dims) {
-  const long long w = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (w >= rows) return;
-  const float* c = centers + w * dims;
-  float s = 0.0f;
-  for (int d = lane; d < dims; d += 32) s = fmaf(c[d], c[d], s);
-  s = warp_sum(s);
-  if (lane == 0) norms[w] = s;
 }
 
 // Centroid update, one warp per cluster.  x rows of head b are
@@ -548,6 +720,7 @@ struct UpdateJob {
   float* means;             // [B, C, D]
   float* sums;              // optional [B, C, D]
   float* norms;             // optional [B, C]
+  unsigned char* image;     // optional [B, nchunks * b_bytes]: bf16 hi/lo image of the means
 };
 struct UpdateJobs {
   UpdateJob job[2];
@@ -570,15 +743,45 @@ __device__ __forceinline__ void load_lane_elems(const T* row, float (&v)[E]) {
   }
 }
 
+// A lane's E consecutive elements of a row, kept as raw words until summed.
+template <typename T, int E>
+struct LaneRaw {
+  static constexpr int kBytes = E * static_cast<int>(sizeof(T));
+  static constexpr int kWords = (kBytes + 3) / 4;
+  uint32_t w[kWords];
+  __device__ __forceinline__ void load(const T* row) {
+    if constexpr (kBytes == 16) {
+      const uint4 u = *reinterpret_cast<const uint4*>(row);
+      w[0] = u.x; w[1] = u.y; w[2] = u.z; w[3] = u.w;
+    } else if constexpr (kBytes == 8) {
+      const uint2 u = *reinterpret_cast<const uint2*>(row);
+      w[0] = u.x; w[1] = u.y;
+    } else if constexpr (kBytes == 4) {
+      w[0] = *reinterpret_cast<const uint32_t*>(row);
+    } else {
+      T* h = reinterpret_cast<T*>(w);
+#pragma unroll
+      for (int e = 0; e < E; ++e) h[e] = row[e];
+    }
+  }
+  __device__ __forceinline__ float get(int e) const { return to_f32<T>(reinterpret_cast<const T*>(w)[e]); }
+};
+
+// One warp per cluster; lane l owns elements [l*E, (l+1)*E).  The cluster's
+// token ids arrive 32 at a time in one coalesced load (the next batch is
+// prefetched), the rows of a batch are all in flight at once, and the sums
+// run strictly in ascending token order (bit-exact with a sequential
+// scatter-add).
 template <int D, typename T>
-__global__ void kmeans_update_kernel(const UpdateJobs jobs, int bh, unsigned* status) {
+__global__ void __launch_bounds__(256) kmeans_update_kernel(const UpdateJobs jobs, int bh, unsigned* status) {
   const UpdateJob& J = jobs.job[blockIdx.y];
   const long long w = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (w >= static_cast<long long>(bh) * J.clusters) return;
   const int head = static_cast<int>(w / J.clusters);
   const int c = static_cast<int>(w - static_cast<long long>(head) * J.clusters);
-  constexpr int E = D / 32;  // elements per lane
+  constexpr int E = D / 32;                            // elements per lane
+  constexpr int kRows = sizeof(T) == 2 ? 32 : 16;      // rows in flight
   const int start = J.offsets[static_cast<long long>(head) * (J.clusters + 1) + c];
   int end = J.offsets[static_cast<long long>(head) * (J.clusters + 1) + c + 1];
   const int32_t* perm = J.perm + static_cast<long long>(head) * J.tokens;
@@ -588,46 +791,52 @@ __global__ void kmeans_update_kernel(const UpdateJobs jobs, int bh, unsigned* st
   for (int e = 0; e < E; ++e) acc[e] = 0.0f;
   bool bad = start < 0 || end > J.tokens || start > end;
   if (bad) end = start;
-  // The cluster's token ids arrive 32 at a time in one coalesced load; rows
-  // are then fetched 8 at a time (all in flight) and added strictly in
-  // ascending token order.
-  for (int base = start; base < end; base += 32) {
-    int my_t = 0;
-    if (base + lane < end) {
-      my_t = perm[base + lane];
-      if (my_t < 0 || my_t >= J.tokens) {
+  auto token_id = [&](int pos) {
+    int t = 0;
+    if (pos < end) {
+      t = perm[pos];
+      if (t < 0 || t >= J.tokens) {
         bad = true;
-        my_t = 0;
+        t = 0;
       }
     }
+    return t;
+  };
+  int next_t = token_id(start + lane);
+  for (int base = start; base < end; base += 32) {
+    const int my_t = next_t;
+    next_t = token_id(base + 32 + lane);
     const int cnt = min(32, end - base);
-    for (int j = 0; j < cnt; j += 8) {
-      float v[8][E];
+    for (int j = 0; j < cnt; j += kRows) {
+      LaneRaw<T, E> v[kRows];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
+      for (int u = 0; u < kRows; ++u) {
         const int t = __shfl_sync(0xffffffffu, my_t, (j + u) & 31);
-        if (j + u < cnt) {
-          const T* row = xb + static_cast<long long>(t) * D;
-          load_lane_elems<T, E>(row, v[u]);
-        }
+        if (j + u < cnt) v[u].load(xb + static_cast<long long>(t) * D);
       }
 #pragma unroll
-      for (int u = 0; u < 8; ++u)
+      for (int u = 0; u < kRows; ++u)
         if (j + u < cnt)
 #pragma unroll
-          for (int e = 0; e < E; ++e) acc[e] = __fadd_rn(acc[e], v[u][e]);
+          for (int e = 0; e < E; ++e) acc[e] = __fadd_rn(acc[e], v[u].get(e));
     }
   }
   if (bad && lane == 0) record_status(status, kDevBadIndex);
   const int n = end - start;
   const long long o = (static_cast<long long>(head) * J.clusters + c) * D + lane * E;
   float nsq = 0.0f;
+  float mv[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) {
     const float m = n > 0 ? __fdiv_rn(acc[e], static_cast<float>(n)) : J.previous[o + e];
+    mv[e] = m;
     J.means[o + e] = m;
     if (J.sums) J.sums[o + e] = acc[e];
     nsq = fmaf(m, m, nsq);
+  }
+  if (J.image) {
+    const CenterGeom g = center_geom(J.clusters, D);
+    write_image<E>(J.image + static_cast<long long>(head) * g.nchunks * g.b_bytes, g, c, lane * E, mv);
   }
   if (J.norms) {
     nsq = warp_sum(nsq);
@@ -635,35 +844,72 @@ __global__ void kmeans_update_kernel(const UpdateJobs jobs, int bh, unsigned* st
   }
 }
 
-template <int D, bool XF32>
-int launch_assign_t(const AssignJobs& jobs, int njobs, int bh, cudaStream_t stream) {
-  int max_smem = 0, max_chunks = 0, max_tiles = 0;
-  for (int j = 0; j < njobs; ++j) {
-    const AssignGeom g = assign_geom(jobs.job[j].clusters, D, XF32);
-    max_smem = max(max_smem, g.smem);
-    max_chunks = max(max_chunks, g.nchunks);
-    max_tiles = max(max_tiles, (jobs.job[j].tokens + kTileM - 1) / kTileM);
+bool make_token_map(CUtensorMap* m, const void* base, long long rows, int dims) {
+  const uint64_t gdims[2] = {static_cast<uint64_t>(dims), static_cast<uint64_t>(rows)};
+  const uint64_t gstr[1] = {static_cast<uint64_t>(dims) * 2};
+  const uint32_t box[2] = {64, static_cast<uint32_t>(kTileM)};
+  return encode_tensor_map(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, gdims, gstr, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return kNumSMs;
+  return n > 0 ? n : kNumSMs;
+}
+
+// x_hi/x_lo: bf16 token rows of each problem ([rows, D], head b at row
+// b * head_rows; x_lo only in split mode), ``rows`` rows per map.
+template <int D, bool SPLIT>
+int launch_assign_t(AssignJobs jobs, const void* const (&x_hi)[2], const void* const (&x_lo)[2],
+                    const long long (&rows)[2], cudaStream_t stream) {
+  AssignMaps maps;
+  for (int j = 0; j < jobs.njobs; ++j) {
+    if (!make_token_map(&maps.xhi[j], x_hi[j], rows[j], D)) return kErrTensorMap;
+    if (SPLIT && !make_token_map(&maps.xlo[j], x_lo[j], rows[j], D)) return kErrTensorMap;
   }
-  if (max_smem > 227 * 1024) return kErrUnsupported;
-  // spread tiles so that ~2 waves of CTAs cover every (job, head)
-  long long ctas_wanted = 2LL * kNumSMs;
-  int per_head = static_cast<int>((ctas_wanted + static_cast<long long>(bh) * njobs - 1) / (static_cast<long long>(bh) * njobs));
-  per_head = max(1, min(per_head, max_tiles));
-  int tiles_per_cta = (max_tiles + per_head - 1) / per_head;
-  if (max_chunks == 1) tiles_per_cta = max(tiles_per_cta, 2);  // amortise the resident centroid load
-  const int grid_x = (max_tiles + tiles_per_cta - 1) / tiles_per_cta;
-  cudaError_t e = cudaFuncSetAttribute(kmeans_assign_kernel<D, XF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  if (jobs.njobs == 1) {
+    maps.xhi[1] = maps.xhi[0];
+    maps.xlo[1] = maps.xlo[0];
+  }
+  const AssignSmem S = assign_smem(jobs.job[0].clusters, jobs.njobs > 1 ? jobs.job[1].clusters : 1, jobs.njobs, D, SPLIT);
+  if (S.smem > 227 * 1024) return kErrUnsupported;
+  long long total_cost = 0;
+  for (int j = 0; j < 2; ++j) {
+    if (j < jobs.njobs) {
+      const CenterGeom g = center_geom(jobs.job[j].clusters, D);
+      jobs.items[j] = static_cast<long long>(jobs.bh) * ((jobs.job[j].tokens + kTileM - 1) / kTileM);
+      jobs.cost[j] = static_cast<long long>(g.nchunks) * g.nc;
+      total_cost += jobs.items[j] * jobs.cost[j];
+    } else {
+      jobs.items[j] = 0;
+      jobs.cost[j] = 1;
+    }
+  }
+  const long long items = jobs.items[0] + jobs.items[1];
+  jobs.ncta = static_cast<int>(items < sm_count() ? items : sm_count());
+  // one CTA per SM: its 512 TMEM columns are then always free
+  const int smem = S.smem > 116 * 1024 ? S.smem : 116 * 1024;
+  cudaError_t e = cudaFuncSetAttribute(kmeans_assign_kernel<D, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return static_cast<int>(e);
-  dim3 grid(grid_x, bh, njobs);
-  kmeans_assign_kernel<D, XF32><<<grid, kAssignThreads, max_smem, stream>>>(jobs, tiles_per_cta, device_status_ptr());
+  kmeans_assign_kernel<D, SPLIT><<<jobs.ncta, kAssignThreads, smem, stream>>>(maps, jobs, device_status_ptr());
   return launch_status();
 }
 
-int launch_norms(const float* centers, float* norms, long long rows, int dims, cudaStream_t stream) {
-  const long long threads = rows * 32;
+// norms and bf16 hi/lo image of [bh, C, D] centroids
+int launch_prep(const float* centers, float* norms, unsigned char* image, int bh, int C, int dims, cudaStream_t stream) {
+  const CenterGeom g = center_geom(C, dims);
+  const long long threads = static_cast<long long>(bh) * g.nchunks * g.nc * 32;
   const int blocks = static_cast<int>((threads + 255) / 256);
-  center_norms_kernel<<<blocks, 256, 0, stream>>>(centers, norms, rows, dims);
+  if (dims == 128) center_prep_kernel<128><<<blocks, 256, 0, stream>>>(centers, norms, image, bh, C);
+  else if (dims == 64) center_prep_kernel<64><<<blocks, 256, 0, stream>>>(centers, norms, image, bh, C);
+  else return kErrUnsupported;
   return launch_status();
+}
+
+long long image_bytes_per_head(int C, int dims) {
+  const CenterGeom g = center_geom(C, dims);
+  return static_cast<long long>(g.nchunks) * g.b_bytes;
 }
 
 template <typename T>
@@ -687,16 +933,24 @@ int kmeans_fit_bf16(int njobs, const KmeansProblem* probs, int bh, int dims, int
   if (dims != 64 && dims != 128) return kErrUnsupported;
   int rc = 0;
   int maxc = 0;
+  const void* xs[2] = {probs[0].x, njobs > 1 ? probs[1].x : probs[0].x};
+  const void* none[2] = {nullptr, nullptr};
+  long long rows[2] = {0, 0};
   for (int j = 0; j < njobs; ++j) {
     const KmeansProblem& p = probs[j];
-    if (p.clusters < 1 || p.tokens < 1 || p.clusters > p.tokens) return kErrInvalidValue;
+    if (p.clusters < 1 || p.tokens < 1 || p.clusters > p.tokens || p.head_rows < p.tokens) return kErrInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(p.x) | reinterpret_cast<uintptr_t>(p.image)) & 15) return kErrInvalidValue;
     maxc = max(maxc, p.clusters);
-    // norms of the initial centres
-    rc = launch_norms(p.centers_a, p.norms, static_cast<long long>(bh) * p.clusters, dims, stream);
+    // the token map covers every head's rows up to the last token
+    rows[j] = static_cast<long long>(bh - 1) * p.head_rows + p.tokens;
+    // norms and image of the initial centres
+    rc = launch_prep(p.centers_a, p.norms, p.image, bh, p.clusters, dims, stream);
     if (rc) return rc;
   }
   for (int it = 0; it < iters; ++it) {
     AssignJobs aj{};
+    aj.njobs = njobs;
+    aj.bh = bh;
     UpdateJobs uj{};
     for (int j = 0; j < njobs; ++j) {
       const KmeansProblem& p = probs[j];
@@ -704,10 +958,13 @@ int kmeans_fit_bf16(int njobs, const KmeansProblem* probs, int bh, int dims, int
       const bool even_left = ((iters - 1 - it) & 1) == 0;
       const float* cur = (it == 0) ? p.centers_a : (even_left ? p.centers_b : p.centers_out);
       float* nxt = even_left ? p.centers_out : p.centers_b;  // in-place is safe: each lane reads then writes
-      aj.job[j] = {p.x, p.head_rows, p.tokens, p.clusters, cur, p.norms, p.labels};
-      uj.job[j] = {p.x, p.head_rows, p.tokens, p.clusters, p.perm, p.offsets, cur, nxt, nullptr, p.norms};
+      aj.job[j] = {p.tokens, p.clusters, p.head_rows, nullptr, cur, p.norms, p.image, p.labels};
+      // the last update needs no image: nothing assigns against it
+      uj.job[j] = {p.x, p.head_rows, p.tokens, p.clusters, p.perm, p.offsets, cur, nxt, nullptr, p.norms,
+                   it + 1 < iters ? p.image : nullptr};
     }
-    rc = dims == 128 ? launch_assign_t<128, false>(aj, njobs, bh, stream) : launch_assign_t<64, false>(aj, njobs, bh, stream);
+    rc = dims == 128 ? launch_assign_t<128, false>(aj, xs, none, rows, stream)
+                     : launch_assign_t<64, false>(aj, xs, none, rows, stream);
     if (rc) return rc;
     for (int j = 0; j < njobs; ++j) {
       const KmeansProblem& p = probs[j];
@@ -720,12 +977,19 @@ int kmeans_fit_bf16(int njobs, const KmeansProblem* probs, int bh, int dims, int
   return 0;
 }
 
+long long kmeans_work_floats(int clusters, int dims) {
+  if (clusters < 1 || (dims != 64 && dims != 128)) return -1;
+  return static_cast<long long>(clusters) * dims + image_bytes_per_head(clusters, dims) / 4;
+}
+
 }  // namespace peco
 
 using namespace peco;
 
 // Drop-in for peco/kernels/kmeans.cu:139-175.  ``scratch`` is not needed by the
 // tensor-core path and is left untouched; ``center_norms`` receives ||c||^2.
+// fp32 tokens are split into bf16 hi + lo rows and the centroids into their
+// bf16 image in stream-ordered scratch of this call.
 extern "C" int peco_assign_tokens_to_centers(const float* x, const float* centers, int32_t* labels, float* scratch,
                                              float* center_norms, int batch, int tokens, int dims, int clusters,
                                              int chunk_size, void* stream_ptr) {
@@ -735,11 +999,38 @@ extern "C" int peco_assign_tokens_to_centers(const float* x, const float* center
   if (batch < 1 || tokens < 1 || clusters < 1 || dims < 1) return kErrInvalidValue;
   if (dims != 64 && dims != 128) return kErrUnsupported;
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(centers)) & 15) return kErrInvalidValue;
-  int rc = launch_norms(centers, center_norms, static_cast<long long>(batch) * clusters, dims, stream);
-  if (rc) return rc;
-  AssignJobs jobs{};
-  jobs.job[0] = {x, tokens, tokens, clusters, centers, center_norms, labels};
-  return dims == 128 ? launch_assign_t<128, true>(jobs, 1, batch, stream) : launch_assign_t<64, true>(jobs, 1, batch, stream);
+  const long long rows = static_cast<long long>(batch) * tokens;
+  const size_t half_bytes = static_cast<size_t>(rows) * dims * 2;
+  const size_t img_bytes = static_cast<size_t>(batch) * image_bytes_per_head(clusters, dims);
+  void* buf = nullptr;
+  cudaError_t e = cudaMallocAsync(&buf, 2 * half_bytes + img_bytes, stream);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  unsigned char* hi = static_cast<unsigned char*>(buf);
+  unsigned char* lo = hi + half_bytes;
+  unsigned char* img = lo + half_bytes;
+  int rc = launch_prep(centers, center_norms, img, batch, clusters, dims, stream);
+  if (!rc) {
+    const long long n4 = rows * dims / 4;
+    long long blocks = (n4 + 255) / 256;
+    if (blocks > kNumSMs * 16) blocks = kNumSMs * 16;
+    split_rows_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(reinterpret_cast<const float4*>(x),
+                                                                    reinterpret_cast<uint2*>(hi),
+                                                                    reinterpret_cast<uint2*>(lo), n4);
+    rc = launch_status();
+  }
+  if (!rc) {
+    AssignJobs jobs{};
+    jobs.njobs = 1;
+    jobs.bh = batch;
+    jobs.job[0] = {tokens, clusters, tokens, x, centers, center_norms, img, labels};
+    const void* xh[2] = {hi, hi};
+    const void* xl[2] = {lo, lo};
+    const long long nrows[2] = {rows, rows};
+    rc = dims == 128 ? launch_assign_t<128, true>(jobs, xh, xl, nrows, stream)
+                     : launch_assign_t<64, true>(jobs, xh, xl, nrows, stream);
+  }
+  cudaError_t f = cudaFreeAsync(buf, stream);
+  return rc ? rc : static_cast<int>(f);
 }
 
 // Drop-in for peco/kernels/kmeans.cu:179-196: writes sums, counts and means
@@ -760,7 +1051,7 @@ extern "C" int peco_recompute_cluster_centers(const float* x, const int32_t* lab
   int rc = launch_stable_sort(labels, tokens, batch, tokens, clusters, perm, counts, offsets, stream);
   if (!rc) {
     UpdateJobs uj{};
-    uj.job[0] = {x, tokens, tokens, clusters, perm, offsets, previous, means, sums, nullptr};
+    uj.job[0] = {x, tokens, tokens, clusters, perm, offsets, previous, means, sums, nullptr, nullptr};
     rc = launch_update_t<float>(uj, 1, batch, dims, clusters, stream);
   }
   cudaError_t f = cudaFreeAsync(scratch, stream);
@@ -774,9 +1065,17 @@ extern "C" int peco_kmeans_fit(const void* q_x, long long q_head_rows, int q_tok
                                int k_clusters, int32_t* k_labels, const float* k_init, float* k_centers, float* k_work,
                                float* k_norms, int32_t* k_counts, int32_t* k_offsets, int32_t* k_perm, int bh, int dims,
                                int iters, void* stream) {
+  // work per problem: [bh, C, D] ping-pong centres, then the bh centroid images
+  auto image_of = [&](float* work, int clusters) {
+    return work ? reinterpret_cast<unsigned char*>(work + static_cast<long long>(bh) * clusters * dims) : nullptr;
+  };
   KmeansProblem p[2];
-  p[0] = {q_x, q_head_rows, q_tokens, q_clusters, q_init, q_work, q_centers, q_norms, q_labels, q_counts, q_offsets, q_perm};
-  p[1] = {k_x, k_head_rows, k_tokens, k_clusters, k_init, k_work, k_centers, k_norms, k_labels, k_counts, k_offsets, k_perm};
+  p[0] = {q_x, q_head_rows, q_tokens, q_clusters, q_init, q_work, q_centers, q_norms, q_labels, q_counts, q_offsets, q_perm,
+          image_of(q_work, q_clusters)};
+  p[1] = {k_x, k_head_rows, k_tokens, k_clusters, k_init, k_work, k_centers, k_norms, k_labels, k_counts, k_offsets, k_perm,
+          image_of(k_work, k_clusters)};
   const int njobs = k_x ? 2 : 1;
   return kmeans_fit_bf16(njobs, p, bh, dims, iters, static_cast<cudaStream_t>(stream));
 }
+
+extern "C" long long peco_kmeans_work_floats(int clusters, int dims) { return peco::kmeans_work_floats(clusters, dims); }
