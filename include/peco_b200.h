@@ -6,9 +6,12 @@
  * synchronises, and returns 0 on success, a cudaError_t value for CUDA
  * failures, or one of the PECO_ERR_* codes below.  Buffers are allocated by
  * the caller (the reference's convention, peco/clustering_cuda.py:83-90 and
- * peco/attention_cuda.py:128); the only exception is the legacy
- * peco_recompute_cluster_centers, which takes its sort scratch from the
- * stream-ordered allocator.
+ * peco/attention_cuda.py:128); the exceptions are three drop-in symbols whose
+ * reference signatures pass no room for what the sm_100a kernels need:
+ * peco_assign_tokens_to_centers (bf16 split of fp32 tokens and centres),
+ * peco_recompute_cluster_centers (sort scratch) and peco_sparse_attention
+ * (attention plan and key blocks) take it from the stream-ordered allocator
+ * (cudaMallocAsync / cudaFreeAsync on the caller's stream).
  *
  * Device-side faults are never raised with traps: kernels skip out-of-range
  * indices and give up bounded waits, OR-ing a bit into a per-device status
