@@ -34,6 +34,7 @@ extern "C" {
 #define PECO_ERR_DRIVER 20003       /* driver entry point unavailable */
 #define PECO_ERR_TIMEOUT 20004      /* a device-side bounded wait expired */
 #define PECO_ERR_WORKSPACE 20005    /* workspace too small */
+#define PECO_ERR_CAPACITY 20006     /* problem larger than a no-alloc entry point's fixed scratch */
 
 #define PECO_STATUS_TIMEOUT 1u      /* status word bit: a bounded wait expired */
 #define PECO_STATUS_BAD_INDEX 2u    /* status word bit: an index failed its bounds check */
@@ -60,6 +61,23 @@ int peco_recompute_cluster_centers(const float* x, const int32_t* labels, const 
  * Replaces peco/kernels/kmeans.cu:200-217 (bound at peco/clustering_cuda.py:67,128-146). */
 int peco_reorder_token_features(const void* input, const int32_t* indices, void* output, int batch_heads,
                                 int tokens, int dims, int item_size, int inverse, void* stream);
+
+/* peco_recompute_cluster_centers without any allocation (no counterpart in
+ * the reference): identical results, with the sort scratch -- batch*tokens +
+ * batch*(clusters+1) ints -- in a fixed per-device array of
+ * peco_recompute_cluster_centers_static_capacity() ints (2^21, 8 MiB); larger
+ * problems return PECO_ERR_CAPACITY without launching.  For callers that must
+ * not allocate once running: a serving loop that pre-plans all its memory
+ * (an allocation can fail or stall under fragmentation there), or a process
+ * whose stream-ordered pool is unavailable or capped.  The first call on a
+ * device looks up the array's address (cudaGetSymbolAddress) and should come
+ * before any stream capture.  Nothing in the scratch must start at zero.
+ * Calls that overlap on one device share the scratch and race; serialise
+ * them. */
+int peco_recompute_cluster_centers_static(const float* x, const int32_t* labels, const float* previous,
+                                          float* sums, int32_t* counts, float* means, int batch, int tokens,
+                                          int dims, int clusters, void* stream);
+long long peco_recompute_cluster_centers_static_capacity(void);
 
 /* Error text for the clustering entry points (peco/kernels/kmeans.cu:220-223). */
 const char* peco_cluster_error_message(int code);

@@ -25,6 +25,8 @@ F = ctypes.c_float
 _SIGNATURES = {
     "peco_assign_tokens_to_centers": [P] * 5 + [I] * 5 + [P],
     "peco_recompute_cluster_centers": [P] * 6 + [I] * 4 + [P],
+    "peco_recompute_cluster_centers_static": [P] * 6 + [I] * 4 + [P],
+    "peco_recompute_cluster_centers_static_capacity": [],
     "peco_reorder_token_features": [P] * 3 + [I] * 5 + [P],
     "peco_sparse_attention": [P] * 8 + [I] * 7 + [P],
     "peco_sort_labels": [P] * 4 + [I] * 3 + [P],
@@ -51,6 +53,7 @@ _RESTYPES = {
     "peco_attention_workspace_stride": LL,
     "peco_key_block_rows": LL,
     "peco_kmeans_work_floats": LL,
+    "peco_recompute_cluster_centers_static_capacity": LL,
     "peco_error_string": ctypes.c_char_p,
     "peco_cluster_error_message": ctypes.c_char_p,
     "peco_attention_error_string": ctypes.c_char_p,

@@ -28,6 +28,7 @@ enum PecoStatus : int {
   kErrDriverEntry = 20003,         // driver entry point unavailable
   kErrWaitTimeout = 20004,         // a device-side bounded wait expired (see status word)
   kErrWorkspace = 20005,           // workspace too small
+  kErrCapacity = 20006,            // problem larger than the fixed scratch of a no-alloc entry point
 };
 
 // Device status word bits (OR-ed by kernels; read with peco_device_status()).

@@ -77,6 +77,7 @@ const char* error_string(int code) {
     case kErrDriverEntry: return "CUDA driver entry point unavailable";
     case kErrWaitTimeout: return "a device-side bounded wait expired";
     case kErrWorkspace: return "workspace buffer too small";
+    case kErrCapacity: return "problem larger than the fixed device scratch of this no-allocation entry point";
     default: return cudaGetErrorString(static_cast<cudaError_t>(code));
   }
 }

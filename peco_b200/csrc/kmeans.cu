@@ -30,9 +30,17 @@
 // reference's CPU scatter_add -- and divides by the count; empty clusters keep
 // their previous centre.  No atomics: the result is deterministic and, for
 // identical labels, bit-identical to the reference's CPU centroids.
+#include <mutex>
+
 #include "common.cuh"
 #include "../../include/peco_b200.h"
 #include "internal.h"
+
+// Fixed scratch of peco_recompute_cluster_centers_static: the stable sort's
+// permutation (batch * tokens ints) followed by the cluster offsets
+// (batch * (clusters + 1) ints).  One copy per device, 8 MiB.  Nothing in it
+// needs to start at zero: every call writes the part it reads.
+static __device__ __align__(256) int32_t g_update_scratch[1 << 21];
 
 namespace peco {
 namespace {
@@ -1058,6 +1066,60 @@ extern "C" int peco_recompute_cluster_centers(const float* x, const int32_t* lab
   if (!rc && f != cudaSuccess) rc = static_cast<int>(f);
   return rc;
 }
+
+// The same sort + update as peco_recompute_cluster_centers, with its scratch
+// in g_update_scratch instead of the stream-ordered pool, so the call makes no
+// allocation of any kind.  The scratch address is looked up once per device
+// (cudaGetSymbolAddress with that device current); the first call on a device
+// does that lookup.  Calls that overlap on one device (other streams, other
+// threads) share the scratch and race: the caller serialises them.
+namespace {
+constexpr long long kStaticUpdateInts = 1LL << 21;
+constexpr int kStaticMaxDevices = 64;
+int32_t* g_update_scratch_ptr[kStaticMaxDevices] = {};
+std::mutex g_update_scratch_mutex;
+
+int update_scratch(int32_t** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  if (dev < 0 || dev >= kStaticMaxDevices) return kErrUnsupported;
+  std::lock_guard<std::mutex> lock(g_update_scratch_mutex);
+  if (!g_update_scratch_ptr[dev]) {
+    void* addr = nullptr;
+    e = cudaGetSymbolAddress(&addr, g_update_scratch);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    g_update_scratch_ptr[dev] = static_cast<int32_t*>(addr);
+  }
+  *out = g_update_scratch_ptr[dev];
+  return 0;
+}
+}  // namespace
+
+extern "C" int peco_recompute_cluster_centers_static(const float* x, const int32_t* labels, const float* previous,
+                                                     float* sums, int32_t* counts, float* means, int batch,
+                                                     int tokens, int dims, int clusters, void* stream_ptr) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  if (batch < 1 || tokens < 1 || clusters < 1 || dims < 1) return kErrInvalidValue;
+  if (dims != 64 && dims != 128) return kErrUnsupported;
+  const long long n_perm = static_cast<long long>(batch) * tokens;
+  const long long n_off = static_cast<long long>(batch) * (clusters + 1);
+  if (n_perm + n_off > kStaticUpdateInts) return kErrCapacity;
+  int32_t* scratch = nullptr;
+  int rc = update_scratch(&scratch);
+  if (rc) return rc;
+  int32_t* perm = scratch;
+  int32_t* offsets = scratch + n_perm;
+  rc = launch_stable_sort(labels, tokens, batch, tokens, clusters, perm, counts, offsets, stream);
+  if (!rc) {
+    UpdateJobs uj{};
+    uj.job[0] = {x, tokens, tokens, clusters, perm, offsets, previous, means, sums, nullptr, nullptr};
+    rc = launch_update_t<float>(uj, 1, batch, dims, clusters, stream);
+  }
+  return rc;
+}
+
+extern "C" long long peco_recompute_cluster_centers_static_capacity(void) { return kStaticUpdateInts; }
 
 extern "C" int peco_kmeans_fit(const void* q_x, long long q_head_rows, int q_tokens, int q_clusters, int32_t* q_labels,
                                const float* q_init, float* q_centers, float* q_work, float* q_norms, int32_t* q_counts,
