@@ -29,6 +29,17 @@ int kmeans_fit_bf16(int njobs, const KmeansProblem* probs, int bh, int dims, int
 int launch_stable_sort(const int32_t* labels, long long label_stride, int rows, int tokens, int clusters,
                        int32_t* indices, int32_t* counts, int32_t* offsets, cudaStream_t stream);
 
+// One stable counting sort of labels [rows, tokens] (values in [0, clusters)).
+struct SortJobInput {
+  const int32_t* labels;
+  long long label_stride;
+  int rows, tokens, clusters;
+  int32_t* indices;   // [rows, tokens]
+  int32_t* counts;    // [rows, clusters] or null
+  int32_t* offsets;   // [rows, clusters + 1] or null
+};
+int launch_stable_sort_jobs(const SortJobInput* jobs, int njobs, cudaStream_t stream);
+
 int launch_select(const float* qc, const float* kc, const int32_t* qs, const int32_t* ks, uint8_t* map, int bh,
                   int cq, int ck, int dims, float top_p, int minimum, int extend, int valid_text, int text_length,
                   int32_t* q_ext, int32_t* k_ext, cudaStream_t stream);

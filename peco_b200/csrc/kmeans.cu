@@ -781,7 +781,7 @@ struct LaneRaw {
 // run strictly in ascending token order (bit-exact with a sequential
 // scatter-add).
 template <int D, typename T>
-__global__ void __launch_bounds__(256) kmeans_update_kernel(const UpdateJobs jobs, int bh, unsigned* status) {
+__global__ void __launch_bounds__(256, 2) kmeans_update_kernel(const UpdateJobs jobs, int bh, unsigned* status) {
   const UpdateJob& J = jobs.job[blockIdx.y];
   const long long w = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -789,7 +789,7 @@ __global__ void __launch_bounds__(256) kmeans_update_kernel(const UpdateJobs job
   const int head = static_cast<int>(w / J.clusters);
   const int c = static_cast<int>(w - static_cast<long long>(head) * J.clusters);
   constexpr int E = D / 32;                            // elements per lane
-  constexpr int kRows = sizeof(T) == 2 ? 32 : 16;      // rows in flight
+  constexpr int kRows = 16;                            // rows in flight
   const int start = J.offsets[static_cast<long long>(head) * (J.clusters + 1) + c];
   int end = J.offsets[static_cast<long long>(head) * (J.clusters + 1) + c + 1];
   const int32_t* perm = J.perm + static_cast<long long>(head) * J.tokens;
@@ -974,11 +974,13 @@ int kmeans_fit_bf16(int njobs, const KmeansProblem* probs, int bh, int dims, int
     rc = dims == 128 ? launch_assign_t<128, false>(aj, xs, none, rows, stream)
                      : launch_assign_t<64, false>(aj, xs, none, rows, stream);
     if (rc) return rc;
+    SortJobInput sj[2];
     for (int j = 0; j < njobs; ++j) {
       const KmeansProblem& p = probs[j];
-      rc = launch_stable_sort(p.labels, p.tokens, bh, p.tokens, p.clusters, p.perm, p.counts, p.offsets, stream);
-      if (rc) return rc;
+      sj[j] = {p.labels, p.tokens, bh, p.tokens, p.clusters, p.perm, p.counts, p.offsets};
     }
+    rc = launch_stable_sort_jobs(sj, njobs, stream);
+    if (rc) return rc;
     rc = launch_update_t<__nv_bfloat16>(uj, njobs, bh, dims, maxc, stream);
     if (rc) return rc;
   }

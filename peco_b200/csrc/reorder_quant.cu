@@ -73,10 +73,27 @@ inline int grid_for(long long n, int threads) {
 // token index first.  Optionally also emits counts [C] and offsets [C+1].
 constexpr int kSortThreads = 1024;
 
-__global__ void __launch_bounds__(kSortThreads) stable_sort_labels_kernel(
-    const int32_t* __restrict__ labels, long long label_stride, int tokens, int clusters, int parts,
-    int32_t* __restrict__ indices, int32_t* __restrict__ counts, int32_t* __restrict__ offsets,
-    unsigned* status) {
+struct SortJob {
+  const int32_t* labels;
+  long long label_stride;
+  int rows, tokens, clusters, parts;
+  int32_t* indices;
+  int32_t* counts;
+  int32_t* offsets;
+};
+struct SortJobs {
+  SortJob job[2];   // blockIdx.y selects the job (the Q and K sorts of one k-means iteration)
+};
+
+__global__ void __launch_bounds__(kSortThreads) stable_sort_labels_kernel(const SortJobs jobs, unsigned* status) {
+  const SortJob& J = jobs.job[blockIdx.y];
+  if (static_cast<int>(blockIdx.x) >= J.rows) return;
+  const int32_t* __restrict__ labels = J.labels;
+  const long long label_stride = J.label_stride;
+  const int tokens = J.tokens, clusters = J.clusters, parts = J.parts;
+  int32_t* __restrict__ indices = J.indices;
+  int32_t* __restrict__ counts = J.counts;
+  int32_t* __restrict__ offsets = J.offsets;
   extern __shared__ int32_t sm[];
   int32_t* hist = sm;                         // [parts][clusters]
   int32_t* colsum = sm + parts * clusters;    // [clusters]
@@ -405,21 +422,36 @@ __global__ void quant_gather_kernel(GatherJobs jobs, int bh, int seq, int video,
 // ---------------------------------------------------------------------------
 // host launchers
 // ---------------------------------------------------------------------------
-int launch_stable_sort(const int32_t* labels, long long label_stride, int rows, int tokens, int clusters,
-                       int32_t* indices, int32_t* counts, int32_t* offsets, cudaStream_t stream) {
-  if (rows < 1 || tokens < 1 || clusters < 1) return kErrInvalidValue;
-  int parts = 32;
-  while (parts > 1 && static_cast<long long>(parts) * clusters * 4 + clusters * 4 > 160 * 1024) parts >>= 1;
-  const size_t smem = (static_cast<size_t>(parts) * clusters + clusters) * sizeof(int32_t);
-  if (smem > 200 * 1024) return kErrUnsupported;
+// Stable counting sorts of up to two label sets in one launch.
+int launch_stable_sort_jobs(const SortJobInput* in, int njobs, cudaStream_t stream) {
+  if (njobs < 1 || njobs > 2) return kErrInvalidValue;
+  SortJobs jobs{};
+  size_t smem = 0;
+  int rows = 0;
+  for (int j = 0; j < njobs; ++j) {
+    const SortJobInput& a = in[j];
+    if (a.rows < 1 || a.tokens < 1 || a.clusters < 1) return kErrInvalidValue;
+    int parts = 32;
+    while (parts > 1 && static_cast<long long>(parts) * a.clusters * 4 + a.clusters * 4 > 160 * 1024) parts >>= 1;
+    const size_t need = (static_cast<size_t>(parts) * a.clusters + a.clusters) * sizeof(int32_t);
+    if (need > 200 * 1024) return kErrUnsupported;
+    smem = need > smem ? need : smem;
+    rows = a.rows > rows ? a.rows : rows;
+    jobs.job[j] = {a.labels, a.label_stride, a.rows, a.tokens, a.clusters, parts, a.indices, a.counts, a.offsets};
+  }
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(stable_sort_labels_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return static_cast<int>(e);
   }
-  stable_sort_labels_kernel<<<rows, kSortThreads, smem, stream>>>(labels, label_stride, tokens, clusters, parts,
-                                                                  indices, counts, offsets, device_status_ptr());
+  stable_sort_labels_kernel<<<dim3(rows, njobs), kSortThreads, smem, stream>>>(jobs, device_status_ptr());
   return launch_status();
+}
+
+int launch_stable_sort(const int32_t* labels, long long label_stride, int rows, int tokens, int clusters,
+                       int32_t* indices, int32_t* counts, int32_t* offsets, cudaStream_t stream) {
+  const SortJobInput in = {labels, label_stride, rows, tokens, clusters, indices, counts, offsets};
+  return launch_stable_sort_jobs(&in, 1, stream);
 }
 
 int launch_quant_gather(const void* q, const void* k, const void* v, void* qp, void* kp, void* vp,
