@@ -193,6 +193,18 @@ __global__ void __launch_bounds__(kSortThreads) stable_sort_labels_kernel(const 
 // Base-Offset quantization of one token row (peco/quantization.py:96-136)
 // ---------------------------------------------------------------------------
 // A group of G lanes (G = D/8) holds one row, 8 consecutive elements per lane.
+// Lanes of one row group: G consecutive lanes (G divides 32) handle one row.
+// Groups of a warp may take different paths, so their shuffles name only
+// their own lanes.
+template <int G>
+__device__ __forceinline__ unsigned row_group_mask() {
+  if constexpr (G >= 32) {
+    return 0xffffffffu;
+  } else {
+    return ((1u << G) - 1u) << ((threadIdx.x & 31) & ~(G - 1));
+  }
+}
+
 template <int G>
 struct RowQuant {
   // in: x[8], c[8] (fp32); out: xhat[8], code[8]; low/scale returned by ref.
@@ -206,16 +218,25 @@ struct RowQuant {
       lo = fminf(lo, r[i]);
       hi = fmaxf(hi, r[i]);
     }
+    const unsigned gmask = row_group_mask<G>();
 #pragma unroll
     for (int o = G / 2; o; o >>= 1) {
-      lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
-      hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+      lo = fminf(lo, __shfl_xor_sync(gmask, lo, o));
+      hi = fmaxf(hi, __shfl_xor_sync(gmask, hi, o));
     }
     const float raw = __fdiv_rn(__fsub_rn(hi, lo), levels);
     const float sc = raw > 0.0f ? raw : 1.0f;
+    // The code is rint(RN((r - lo) / sc)).  (r - lo) * (1/sc) is within a
+    // few ulp of that quotient (< 2^-19 absolute for quotients <= 255), so
+    // its rint is the same unless it sits within 1e-4 of a half-integer; only
+    // then is the exact division evaluated.
+    const float inv = __frcp_rn(sc);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      float q = rintf(__fdiv_rn(__fsub_rn(r[i], lo), sc));
+      const float num = __fsub_rn(r[i], lo);
+      const float qa = num * inv;
+      float q = rintf(qa);
+      if (fabsf(qa - q) > 0.4999f) q = rintf(__fdiv_rn(num, sc));
       q = fminf(fmaxf(q, 0.0f), levels);
       code[i] = q;
       xhat[i] = __fadd_rn(c[i], __fadd_rn(lo, __fmul_rn(sc, q)));
@@ -362,58 +383,91 @@ struct GatherJobs {
 };
 
 template <int D>
-__global__ void quant_gather_kernel(GatherJobs jobs, int bh, int seq, int video, int bits, unsigned* status) {
-  constexpr int G = D / 8;
+__global__ void __launch_bounds__(256) quant_gather_kernel(GatherJobs jobs, int bh, int seq, int video, int bits,
+                                                           unsigned* status) {
+  constexpr int G = D / 8;  // lanes per row, 8 elements (16 bytes) each
+  constexpr int R = 4;      // rows in flight per row group
   const GatherJob& J = jobs.job[blockIdx.y];
+  const bool to_blocks = jobs.plan && blockIdx.y > 0;
+  const bool quant = J.labels && bits != 0;
   const float levels = static_cast<float>((1 << bits) - 1);
   const long long rows = static_cast<long long>(bh) * seq;
   const int sub = threadIdx.x % G;
   const long long first = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) / G;
   const long long step = static_cast<long long>(gridDim.x) * blockDim.x / G;
-  for (long long row = first; row < rows; row += step) {
-    const long long head = row / seq;
-    const int j = static_cast<int>(row - head * seq);
-    __nv_bfloat16* dst = J.dst + row * D + sub * 8;
-    if (jobs.plan && blockIdx.y > 0) {
-      const int kr = jobs.plan[head * jobs.plan_stride + jobs.off_rows + j];
-      if (kr < 0) continue;  // key row outside every key cluster: never attended
-      if (kr >= jobs.blocks * kKeyBlockRows) {
+  for (long long r0 = first; r0 < rows; r0 += R * step) {
+    // phase 1: destination row (key blocks for K/V) and source token of R rows
+    long long head[R];
+    int j[R], t[R], kr[R];
+    bool live[R];
+#pragma unroll
+    for (int u = 0; u < R; ++u) {
+      const long long row = r0 + u * step;
+      live[u] = row < rows;
+      head[u] = live[u] ? row / seq : 0;
+      j[u] = live[u] ? static_cast<int>(row - head[u] * seq) : 0;
+      t[u] = j[u];
+      kr[u] = j[u];
+      if (live[u] && j[u] < video) t[u] = J.perm[head[u] * video + j[u]];
+      if (live[u] && to_blocks) kr[u] = jobs.plan[head[u] * jobs.plan_stride + jobs.off_rows + j[u]];
+    }
+    // phase 2: source chunks and labels
+    uint4 xr[R];
+    int lab[R];
+#pragma unroll
+    for (int u = 0; u < R; ++u) {
+      lab[u] = 0;
+      if (live[u] && (t[u] < 0 || t[u] >= (j[u] < video ? video : seq))) {
+        if (sub == 0) record_status(status, kDevBadIndex);
+        live[u] = false;
+      }
+      if (live[u] && to_blocks && kr[u] >= jobs.blocks * kKeyBlockRows) {
+        if (sub == 0) record_status(status, kDevBadIndex);
+        live[u] = false;
+      }
+      if (live[u] && to_blocks && kr[u] < 0) live[u] = false;  // key row outside every key cluster: never attended
+      if (live[u]) {
+        xr[u] = *reinterpret_cast<const uint4*>(J.src + (head[u] * seq + t[u]) * D + sub * 8);
+        if (quant && j[u] < video) lab[u] = J.labels[head[u] * video + t[u]];
+      }
+    }
+    // phase 3: centroid chunks, then quantise and store
+#pragma unroll
+    for (int u = 0; u < R; ++u) {
+      if (!live[u]) continue;
+      __nv_bfloat16* dst;
+      if (to_blocks) {
+        dst = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<unsigned char*>(J.dst) +
+                                               (head[u] * jobs.blocks + kr[u] / kKeyBlockRows) * (kKeyBlockRows * D * 2) +
+                                               key_block_offset(kr[u] % kKeyBlockRows, sub * 8));
+      } else {
+        dst = J.dst + (head[u] * seq + j[u]) * D + sub * 8;
+      }
+      if (!quant || j[u] >= video) {  // text rows and unquantised tensors: copy
+        *reinterpret_cast<uint4*>(dst) = xr[u];
+        continue;
+      }
+      if (lab[u] < 0 || lab[u] >= J.clusters) {
         if (sub == 0) record_status(status, kDevBadIndex);
         continue;
       }
-      dst = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<unsigned char*>(J.dst) +
-                                             (head * jobs.blocks + kr / kKeyBlockRows) * (kKeyBlockRows * D * 2) +
-                                             key_block_offset(kr % kKeyBlockRows, sub * 8));
+      const float* cen = J.centroids + (head[u] * J.clusters + lab[u]) * D + sub * 8;
+      float c[8], xv[8], xh[8], q[8];
+      const float4 a = reinterpret_cast<const float4*>(cen)[0];
+      const float4 b = reinterpret_cast<const float4*>(cen)[1];
+      c[0] = a.x; c[1] = a.y; c[2] = a.z; c[3] = a.w;
+      c[4] = b.x; c[5] = b.y; c[6] = b.z; c[7] = b.w;
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&xr[u]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(h2[e]);
+        xv[2 * e] = f.x;
+        xv[2 * e + 1] = f.y;
+      }
+      float lo, sc;
+      RowQuant<G>::run(xv, c, levels, xh, q, lo, sc);
+      Vec8<__nv_bfloat16>::store(dst, xh);
     }
-    if (j >= video) {
-      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(J.src + row * D + sub * 8);
-      continue;
-    }
-    int t = J.perm[head * video + j];
-    if (t < 0 || t >= video) {
-      if (sub == 0) record_status(status, kDevBadIndex);
-      continue;
-    }
-    const __nv_bfloat16* src = J.src + (head * seq + t) * D + sub * 8;
-    if (!J.labels || bits == 0) {
-      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
-      continue;
-    }
-    int lab = J.labels[head * video + t];
-    if (lab < 0 || lab >= J.clusters) {
-      if (sub == 0) record_status(status, kDevBadIndex);
-      continue;
-    }
-    const float* cen = J.centroids + (head * J.clusters + lab) * D + sub * 8;
-    float c[8], xv[8], xh[8], q[8];
-    const float4 a = reinterpret_cast<const float4*>(cen)[0];
-    const float4 b = reinterpret_cast<const float4*>(cen)[1];
-    c[0] = a.x; c[1] = a.y; c[2] = a.z; c[3] = a.w;
-    c[4] = b.x; c[5] = b.y; c[6] = b.z; c[7] = b.w;
-    Vec8<__nv_bfloat16>::load(src, xv);
-    float lo, sc;
-    RowQuant<G>::run(xv, c, levels, xh, q, lo, sc);
-    Vec8<__nv_bfloat16>::store(dst, xh);
   }
 }
 
