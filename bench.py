@@ -50,6 +50,11 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--config", default="hv480")
+    ap.add_argument("--top-k", type=int, default=0, help="override the config's top-k key clusters (config 3 sweep)")
+    ap.add_argument("--parallel", choices=("heads", "ulysses"), default="heads",
+                    help="heads: every rank runs all heads of its own call (weak scaling); ulysses: one call, "
+                         "tokens sequence-sharded over the ranks and resharded to heads by NCCL all-to-all "
+                         "(strong scaling, the long-video config)")
     ap.add_argument("--e2e-steps", type=int, default=100)
     ap.add_argument("--cpu-sample-heads", type=int, default=2)
     ap.add_argument("--baselines", choices=("all", "none"), default="all",
@@ -171,6 +176,96 @@ def make_processor(w, q, k):
     return proc, q_init, k_init
 
 
+def run_ulysses(args, world, rank, local):
+    """One PECO call per step on sequence-sharded Q/K/V [1, H, S/P, D]: NCCL
+    all-to-all to [1, H/P, S, D], the call on this rank's heads, all-to-all
+    back.  Device time per step (max over ranks) is the whole job's time."""
+    import torch
+    from peco_b200 import _native, synthetic
+    from peco_b200.distributed import heads_to_seq, seq_to_heads
+
+    w = synthetic.workload(args.config, **({"top_k": args.top_k} if args.top_k else {}))
+    h, s, d, nv = w.heads, w.seq, w.dims, w.video_tokens
+    if h % world or s % world:
+        raise SystemExit(f"{h} heads / {s} tokens do not split over {world} ranks")
+    dev = torch.device("cuda", local if world > 1 else 0)
+    hl, sl = h // world, s // world
+    q_f, k_f, v_f = synthetic.make_inputs(w, seed=1000, device=dev, generate_on="cuda")
+    q_sh, k_sh, v_sh = (t[:, :, rank * sl:(rank + 1) * sl].contiguous() for t in (q_f, k_f, v_f))
+    proc, q_init, k_init = make_processor(w, q_f[:, rank * hl:(rank + 1) * hl], k_f[:, rank * hl:(rank + 1) * hl])
+    del q_f, k_f, v_f
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    lib = _native.load()
+    ev_names = ("start", "resharded", "attended", "end")
+
+    def call(evs=None):
+        proc.q_centroids, proc.k_centroids = q_init, k_init
+        if evs:
+            evs["start"].record()
+        q, k, v = (seq_to_heads(t) for t in (q_sh, k_sh, v_sh))
+        if evs:
+            evs["resharded"].record()
+        o = proc.attention(q, k, v)
+        if evs:
+            evs["attended"].record()
+        out = heads_to_seq(o)
+        if evs:
+            evs["end"].record()
+        return out
+
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize()
+    steps = args.steps
+    evs = [{n: torch.cuda.Event(enable_timing=True) for n in ev_names} for _ in range(steps)]
+    sampler = ClockSampler(_smi_id(dev))
+    barrier(world)
+    torch.cuda.synchronize()
+    launches0 = lib.peco_launch_count()
+    sampler.start()
+    for i in range(steps):
+        flush.zero_()
+        call(evs[i])
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = sampler.stop()
+    launches = lib.peco_launch_count() - launches0
+    status = _native.device_status(clear=True)
+    step = statistics.mean(e["start"].elapsed_time(e["end"]) for e in evs)
+    a2a = statistics.mean(e["start"].elapsed_time(e["resharded"]) + e["attended"].elapsed_time(e["end"]) for e in evs)
+    att = statistics.mean(e["resharded"].elapsed_time(e["attended"]) for e in evs)
+    step_max = allreduce(step, world, "max")
+    a2a_max, att_max = allreduce(a2a, world, "max"), allreduce(att, world, "max")
+    launches_job = int(allreduce(launches, world, "sum"))
+    return {
+        "metric": METRIC.replace("7006", str(s)),
+        "value": round(step_max, 5),
+        "unit": "ms",
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(step_max, 5),
+        "higher_is_better": False,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: seeded Gaussian-mixture video Q/K (block-map centres, noise 0.3), N(0,1) text Q/K and V "
+                "(drawn with a CUDA generator)",
+        "config": {
+            "workload": f"{w.name}: {h} heads x {s} tokens ({nv} video + {w.text_length} text), d={d}, "
+                        f"CQ={w.q_clusters}, CK={w.k_clusters}, {w.iters} Lloyd iterations, top-{w.top_k}, "
+                        f"{w.bits}-bit Base-Offset",
+            "parallelism": f"ulysses: tokens sequence-sharded over {world} rank(s), NCCL all-to-all to {hl} heads "
+                           "per rank and back",
+            "l2": "flushed before every step (256 MB write), outside the step events",
+        },
+        "stages": {"all_to_all_ms": round(a2a_max, 5), "peco_call_ms": round(att_max, 5)},
+        "gpu_launches": launches_job,
+        "clocks": clocks,
+        "device_status": status,
+    }
+
+
 def attention_flops(emap, qs, ks, d):
     """4*D * sum over (query row, allowed key) pairs, from the extended map and sizes."""
     import torch
@@ -182,7 +277,7 @@ def run_ours(args, world, rank, local):
     import torch
     from peco_b200 import _native, synthetic
 
-    w = synthetic.workload(args.config)
+    w = synthetic.workload(args.config, **({"top_k": args.top_k} if args.top_k else {}))
     h, s, d, nv = w.heads, w.seq, w.dims, w.video_tokens
     dev = torch.device("cuda", local if world > 1 else 0)
     q_c, k_c, v_c = synthetic.make_inputs(w, seed=1000 + rank)
@@ -426,6 +521,11 @@ def main():
     import torch
     world, rank, local = dist_init(args.gpus)
     try:
+        if args.parallel == "ulysses":
+            result = run_ulysses(args, world, rank, local)
+            if rank == 0:
+                print(json.dumps(result), flush=True)
+            return
         result, (inputs_w) = run_ours(args, world, rank, local)
         if rank == 0 and world == 1 and args.baselines == "all":
             q_c, k_c, v_c, w = inputs_w
@@ -452,7 +552,7 @@ def main_reference(args):
         return 0
     import torch
     from peco_b200 import synthetic
-    w = synthetic.workload(args.config)
+    w = synthetic.workload(args.config, **({"top_k": args.top_k} if args.top_k else {}))
     inputs = synthetic.make_inputs(w, seed=1000)
     cores = len(os.sched_getaffinity(0))
     torch.set_num_threads(cores)

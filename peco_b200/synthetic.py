@@ -105,31 +105,35 @@ def _block_ids(w: Workload) -> tuple:
 
 def _mixture(w: Workload, gen: torch.Generator, heads: int) -> torch.Tensor:
     n, d = w.video_tokens, w.dims
+    dev = gen.device
     if w.mixture == "iid":
-        centres = torch.randn((heads, w.n_centres, d), generator=gen)
-        comp = torch.randint(w.n_centres, (heads, n), generator=gen)
+        centres = torch.randn((heads, w.n_centres, d), generator=gen, device=dev)
+        comp = torch.randint(w.n_centres, (heads, n), generator=gen, device=dev)
     else:
         ids, nb = _block_ids(w)
-        centres = torch.randn((heads, nb, d), generator=gen)
-        comp = ids.unsqueeze(0).expand(heads, -1)
+        centres = torch.randn((heads, nb, d), generator=gen, device=dev)
+        comp = ids.to(dev).unsqueeze(0).expand(heads, -1)
     base = centres.gather(1, comp.unsqueeze(-1).expand(-1, -1, d))
-    return base + w.noise * torch.randn((heads, n, d), generator=gen)
+    return base + w.noise * torch.randn((heads, n, d), generator=gen, device=dev)
 
 
-def make_inputs(w: Workload, seed: int = 0, heads: int | None = None, device="cpu"):
+def make_inputs(w: Workload, seed: int = 0, heads: int | None = None, device="cpu", generate_on=None):
     """Return q, k, v [1,H,S,D] in ``w.dtype`` (video tokens first, then text).
 
     Generated on the CPU with a seeded torch.Generator so every machine gets
-    the same bits, then moved to ``device``.
+    the same bits, then moved to ``device``.  ``generate_on="cuda"`` draws the
+    same distributions with a CUDA generator instead (fast for the 118k-token
+    config; the bits then differ from the CPU stream).
     """
     heads = w.heads if heads is None else heads
-    gen = torch.Generator().manual_seed(seed)
+    gen = torch.Generator(device=generate_on or "cpu").manual_seed(seed)
     t, d = w.text_length, w.dims
     qv = _mixture(w, gen, heads)
     kv = _mixture(w, gen, heads)
-    qt = torch.randn((heads, t, d), generator=gen)
-    kt = torch.randn((heads, t, d), generator=gen)
-    v = torch.randn((heads, w.seq, d), generator=gen)
+    dev = gen.device
+    qt = torch.randn((heads, t, d), generator=gen, device=dev)
+    kt = torch.randn((heads, t, d), generator=gen, device=dev)
+    v = torch.randn((heads, w.seq, d), generator=gen, device=dev)
     q = torch.cat((qv, qt), 1).unsqueeze(0).to(w.dtype)
     k = torch.cat((kv, kt), 1).unsqueeze(0).to(w.dtype)
     v = v.unsqueeze(0).to(w.dtype)
