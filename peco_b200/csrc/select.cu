@@ -1,5 +1,8 @@
 // Cluster-pair selection (peco/clustering.py:139-186) and the text partition
-// extension (peco/processor.py:68-84), one warp per query cluster.
+// extension (peco/processor.py:68-84).  Two kernels: a register-tiled fp32
+// score GEMM writes every (query, key cluster) logit to stream-ordered
+// scratch; then one CTA per query cluster does the softmax, the sort and the
+// keep rule.
 //
 // Per query cluster g of a head:
 //   s_c   = (Cq[g] . Ck[c]) * fp32(D^-0.5)
@@ -20,107 +23,164 @@
 namespace peco {
 namespace {
 
-constexpr int kSelWarps = 8;
-constexpr int kKeyChunk = 32;
+constexpr int kTile = 64;        // score tile: 64 query x 64 key clusters
+constexpr int kRowThreads = 256;  // row kernel: one CTA per query cluster
 
 __device__ __forceinline__ unsigned long long sort_key(float p, int idx) {
   // p >= 0: its bit pattern orders like the value; invert for descending.
   return (static_cast<unsigned long long>(~__float_as_uint(p)) << 32) | static_cast<unsigned>(idx);
 }
 
-// grid: (ceil(CQ / W), BH); block: 32 * W (W <= kSelWarps warps, one per query cluster).
-// smem: sort keys [W][np2] u64 | probabilities [W][np2] f32 | q rows [W][D] f32 |
-//       key chunk [kKeyChunk][D+1] f32
-__global__ void __launch_bounds__(32 * kSelWarps) select_kernel(
-    const float* __restrict__ qc, const float* __restrict__ kc, const int32_t* __restrict__ q_sizes,
-    const int32_t* __restrict__ k_sizes, uint8_t* __restrict__ map, int cq, int ck, int dims, int np2, float top_p,
-    int minimum, int extend, int out_cols) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  const int nwarps = blockDim.x >> 5;
-  unsigned long long* keys = reinterpret_cast<unsigned long long*>(smem);       // [W][np2]
-  float* probs = reinterpret_cast<float*>(keys + static_cast<long long>(nwarps) * np2);  // [W][np2]
-  float* qrow = probs + static_cast<long long>(nwarps) * np2;                  // [W][D]
-  float* kchunk = qrow + nwarps * dims;                                        // [kKeyChunk][D+1]
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int head = blockIdx.y;
-  const int g = blockIdx.x * nwarps + warp;
-  const bool active = g < cq;
-  const float* qh = qc + (static_cast<long long>(head) * cq) * dims;
-  const float* kh = kc + (static_cast<long long>(head) * ck) * dims;
+// logits[h, g, c] = (Cq[h,g] . Ck[h,c]) * fp32(D^-0.5) + log(count_c), -inf for
+// empty key clusters.  Each dot product is one fmaf chain in ascending d.
+// grid (ceil(CK/64), ceil(CQ/64), BH), 256 threads, each a 4x4 output block;
+// smem holds both tiles transposed ([d][row]) so a thread's 4 rows are one
+// float4.
+template <int D>
+__global__ void __launch_bounds__(256) select_scores_kernel(const float* __restrict__ qc, const float* __restrict__ kc,
+                                                            const int32_t* __restrict__ k_sizes,
+                                                            float* __restrict__ logits, int cq, int ck) {
+  extern __shared__ __align__(16) float ssm[];
+  float* qt = ssm;               // [D][64]
+  float* kt = ssm + D * kTile;   // [D][64]
+  const int head = blockIdx.z;
+  const int g0 = blockIdx.y * kTile, c0 = blockIdx.x * kTile;
+  const float* qh = qc + static_cast<long long>(head) * cq * D;
+  const float* kh = kc + static_cast<long long>(head) * ck * D;
+  for (int i = threadIdx.x; i < kTile * D / 4; i += blockDim.x) {
+    const int row = i / (D / 4), d4 = (i % (D / 4)) * 4;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+    if (g0 + row < cq) a = *reinterpret_cast<const float4*>(qh + static_cast<long long>(g0 + row) * D + d4);
+    if (c0 + row < ck) b = *reinterpret_cast<const float4*>(kh + static_cast<long long>(c0 + row) * D + d4);
+    qt[(d4 + 0) * kTile + row] = a.x;
+    qt[(d4 + 1) * kTile + row] = a.y;
+    qt[(d4 + 2) * kTile + row] = a.z;
+    qt[(d4 + 3) * kTile + row] = a.w;
+    kt[(d4 + 0) * kTile + row] = b.x;
+    kt[(d4 + 1) * kTile + row] = b.y;
+    kt[(d4 + 2) * kTile + row] = b.z;
+    kt[(d4 + 3) * kTile + row] = b.w;
+  }
+  __syncthreads();
+  const int ty = threadIdx.x / 16, tx = threadIdx.x % 16;
+  float acc[4][4];
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int b = 0; b < 4; ++b) acc[a][b] = 0.0f;
+#pragma unroll 8
+  for (int d = 0; d < D; ++d) {
+    const float4 qa = *reinterpret_cast<const float4*>(qt + d * kTile + 4 * ty);
+    const float4 kb = *reinterpret_cast<const float4*>(kt + d * kTile + 4 * tx);
+    const float qv[4] = {qa.x, qa.y, qa.z, qa.w}, kv[4] = {kb.x, kb.y, kb.z, kb.w};
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int b = 0; b < 4; ++b) acc[a][b] = fmaf(qv[a], kv[b], acc[a][b]);
+  }
+  const float scale = static_cast<float>(1.0 / sqrt(static_cast<double>(D)));
   const int32_t* ks = k_sizes + static_cast<long long>(head) * ck;
-  unsigned long long* mykeys = keys + static_cast<long long>(warp) * np2;
-  if (active)
-    for (int d = lane; d < dims; d += 32) qrow[warp * dims + d] = qh[static_cast<long long>(g) * dims + d];
-  const float scale = static_cast<float>(1.0 / sqrt(static_cast<double>(dims)));
-  float* logit = probs + static_cast<long long>(warp) * np2;
-  for (int c0 = 0; c0 < ck; c0 += kKeyChunk) {
-    __syncthreads();
-    for (int i = threadIdx.x; i < kKeyChunk * dims; i += blockDim.x) {
-      const int r = i / dims, d = i - r * dims;
-      kchunk[r * (dims + 1) + d] = (c0 + r < ck) ? kh[static_cast<long long>(c0 + r) * dims + d] : 0.0f;
-    }
-    __syncthreads();
-    const int c = c0 + lane;
-    if (active && c < ck) {
-      float s = 0.0f;
-      const float* kr = kchunk + lane * (dims + 1);
-      const float* qr = qrow + warp * dims;
-      for (int d = 0; d < dims; ++d) s = fmaf(qr[d], kr[d], s);
-      s = s * scale;
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    const int g = g0 + 4 * ty + a;
+    if (g >= cq) continue;
+    float* out = logits + (static_cast<long long>(head) * cq + g) * ck;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const int c = c0 + 4 * tx + b;
+      if (c >= ck) continue;
       const int n = ks[c];
-      logit[c] = n > 0 ? s + logf(static_cast<float>(n)) : -INFINITY;
+      out[c] = n > 0 ? acc[a][b] * scale + logf(static_cast<float>(n)) : -INFINITY;
     }
   }
-  __syncwarp();
-  if (!active) return;
+}
+
+__device__ __forceinline__ float block_reduce(float v, bool is_max, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const float u = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? fmaxf(v, u) : v + u;
+  }
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float r = is_max ? -INFINITY : 0.0f;
+  for (int w = 0; w < nw; ++w) r = is_max ? fmaxf(r, red[w]) : r + red[w];
+  return r;
+}
+// One CTA per (query cluster, head): softmax of the logits row, stable
+// descending sort of (p, index), running mass in double rounded to fp32 per
+// element, keep rule, map row.  smem: sort keys [np2] u64 | p [np2] f32.
+__global__ void __launch_bounds__(kRowThreads) select_row_kernel(const float* __restrict__ logits,
+                                                                 const int32_t* __restrict__ q_sizes,
+                                                                 const int32_t* __restrict__ k_sizes,
+                                                                 uint8_t* __restrict__ map, int cq, int ck, int np2,
+                                                                 float top_p, int minimum, int extend, int out_cols) {
+  extern __shared__ __align__(16) unsigned char rsm[];
+  unsigned long long* keys = reinterpret_cast<unsigned long long*>(rsm);
+  float* e = reinterpret_cast<float*>(keys + np2);
+  __shared__ float red[32];
+  __shared__ double dscan[32];
+  const int g = blockIdx.x, head = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const float* row_in = logits + (static_cast<long long>(head) * cq + g) * ck;
+  const int32_t* ks = k_sizes + static_cast<long long>(head) * ck;
   float mx = -INFINITY;
-  for (int c = lane; c < ck; c += 32) mx = fmaxf(mx, logit[c]);
-  mx = warp_max(mx);
+  for (int c = tid; c < ck; c += blockDim.x) {
+    const float l = row_in[c];
+    e[c] = l;
+    mx = fmaxf(mx, l);
+  }
+  mx = block_reduce(mx, true, red);
   if (!isfinite(mx)) mx = 0.0f;
   float sum = 0.0f;
-  for (int c = lane; c < ck; c += 32) {
-    const float e = expf(logit[c] - mx);
-    logit[c] = e;
-    sum += e;
+  for (int c = tid; c < ck; c += blockDim.x) {
+    const float v = expf(e[c] - mx);
+    e[c] = v;
+    sum += v;
   }
-  sum = fmaxf(warp_sum(sum), FLT_MIN);
-  __syncwarp();
-  for (int c = lane; c < np2; c += 32) mykeys[c] = c < ck ? sort_key(logit[c] / sum, c) : ~0ull;
-  __syncwarp();
+  sum = fmaxf(block_reduce(sum, false, red), FLT_MIN);
+  for (int c = tid; c < np2; c += blockDim.x) keys[c] = c < ck ? sort_key(e[c] / sum, c) : ~0ull;
+  __syncthreads();
   // bitonic sort ascending on keys (descending p, ascending index)
   for (int k = 2; k <= np2; k <<= 1) {
     for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = lane; i < np2; i += 32) {
+      for (int i = tid; i < np2; i += blockDim.x) {
         const int l = i ^ j;
         if (l > i) {
-          const unsigned long long a = mykeys[i], b = mykeys[l];
+          const unsigned long long a = keys[i], b = keys[l];
           const bool up = (i & k) == 0;
           if ((a > b) == up) {
-            mykeys[i] = b;
-            mykeys[l] = a;
+            keys[i] = b;
+            keys[l] = a;
           }
         }
       }
-      __syncwarp();
+      __syncthreads();
     }
   }
-  // running mass in double, per-element fp32 rounding; each lane owns a
-  // contiguous span of positions
-  const int per = (ck + 31) / 32;
-  const int p0 = lane * per, p1 = min(ck, p0 + per);
+  // running mass in double, per-element fp32 rounding; each thread owns a
+  // contiguous span of sorted positions
+  const int per = (ck + blockDim.x - 1) / blockDim.x;
+  const int p0 = min(ck, tid * per), p1 = min(ck, p0 + per);
   double local = 0.0;
-  for (int i = p0; i < p1; ++i) local += static_cast<double>(__uint_as_float(~static_cast<unsigned>(mykeys[i] >> 32)));
+  for (int i = p0; i < p1; ++i) local += static_cast<double>(__uint_as_float(~static_cast<unsigned>(keys[i] >> 32)));
   double incl = local;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const double v = __shfl_up_sync(0xffffffffu, incl, o);
     if (lane >= o) incl += v;
   }
-  double run = incl - local;
+  if (lane == 31) dscan[warp] = incl;
+  __syncthreads();
+  double carry = 0.0;
+  for (int w = 0; w < warp; ++w) carry += dscan[w];
+  double run = carry + incl - local;
   const int qn = q_sizes[static_cast<long long>(head) * cq + g];
   uint8_t* row = map + (static_cast<long long>(head) * (extend ? cq + 2 : cq) + g) * out_cols;
   for (int i = p0; i < p1; ++i) {
-    const unsigned long long key = mykeys[i];
+    const unsigned long long key = keys[i];
     const float p = __uint_as_float(~static_cast<unsigned>(key >> 32));
     const int c = static_cast<int>(key & 0xffffffffu);
     run += static_cast<double>(p);
@@ -129,7 +189,7 @@ __global__ void __launch_bounds__(32 * kSelWarps) select_kernel(
     keep = keep && ks[c] > 0 && qn > 0;
     row[c] = keep ? 1 : 0;
   }
-  if (extend && lane == 0) {
+  if (extend && tid == 0) {
     row[ck] = 1;      // every video query sees the valid text keys
     row[ck + 1] = 0;  // ... never the padding keys
   }
@@ -161,23 +221,41 @@ __global__ void text_partition_kernel(uint8_t* __restrict__ map, const int32_t* 
 int launch_select(const float* qc, const float* kc, const int32_t* qs, const int32_t* ks, uint8_t* map, int bh,
                   int cq, int ck, int dims, float top_p, int minimum, int extend, int valid_text, int text_length,
                   int32_t* q_ext, int32_t* k_ext, cudaStream_t stream) {
-  if (bh < 1 || cq < 1 || ck < 1 || dims < 1 || dims > 256) return kErrInvalidValue;
+  if (bh < 1 || bh > 65535 || cq < 1 || ck < 1 || cq > 65535) return kErrInvalidValue;
+  if (dims != 64 && dims != 128) return kErrUnsupported;
+  if ((reinterpret_cast<uintptr_t>(qc) | reinterpret_cast<uintptr_t>(kc)) & 15) return kErrInvalidValue;
   int np2 = 1;
   while (np2 < ck) np2 <<= 1;
-  int warps = kSelWarps;
-  auto bytes = [&](int w) {
-    return (sizeof(unsigned long long) + sizeof(float)) * static_cast<size_t>(w) * np2 +
-           sizeof(float) * (static_cast<size_t>(w) * dims + kKeyChunk * (dims + 1));
-  };
-  while (warps > 1 && bytes(warps) > 200 * 1024) --warps;
-  const size_t smem = bytes(warps);
-  if (smem > 220 * 1024) return kErrUnsupported;
-  cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  dim3 grid((cq + warps - 1) / warps, bh);
-  const int out_cols = extend ? ck + 2 : ck;
-  select_kernel<<<grid, 32 * warps, smem, stream>>>(qc, kc, qs, ks, map, cq, ck, dims, np2, top_p, minimum,
-                                                         extend, out_cols);
-  int rc = launch_status();
+  const size_t row_smem = (sizeof(unsigned long long) + sizeof(float)) * static_cast<size_t>(np2);
+  if (row_smem > 200 * 1024) return kErrUnsupported;
+  // logits in stream-ordered scratch of this call
+  void* scratch = nullptr;
+  cudaError_t e = cudaMallocAsync(&scratch, sizeof(float) * static_cast<size_t>(bh) * cq * ck, stream);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  float* logits = static_cast<float*>(scratch);
+  const size_t tile_smem = sizeof(float) * 2 * kTile * dims;
+  dim3 sgrid((ck + kTile - 1) / kTile, (cq + kTile - 1) / kTile, bh);
+  int rc = 0;
+  if (dims == 128) {
+    e = cudaFuncSetAttribute(select_scores_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(tile_smem));
+    if (e == cudaSuccess) select_scores_kernel<128><<<sgrid, 256, tile_smem, stream>>>(qc, kc, ks, logits, cq, ck);
+  } else {
+    e = cudaFuncSetAttribute(select_scores_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(tile_smem));
+    if (e == cudaSuccess) select_scores_kernel<64><<<sgrid, 256, tile_smem, stream>>>(qc, kc, ks, logits, cq, ck);
+  }
+  rc = e != cudaSuccess ? static_cast<int>(e) : launch_status();
+  if (!rc && row_smem > 48 * 1024) {
+    e = cudaFuncSetAttribute(select_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(row_smem));
+    if (e != cudaSuccess) rc = static_cast<int>(e);
+  }
+  if (!rc) {
+    const int out_cols = extend ? ck + 2 : ck;
+    select_row_kernel<<<dim3(cq, bh), kRowThreads, row_smem, stream>>>(logits, qs, ks, map, cq, ck, np2, top_p, minimum,
+                                                                       extend, out_cols);
+    rc = launch_status();
+  }
+  e = cudaFreeAsync(scratch, stream);
+  if (!rc && e != cudaSuccess) rc = static_cast<int>(e);
   if (rc || !extend) return rc;
   text_partition_kernel<<<bh, 256, 0, stream>>>(map, qs, ks, q_ext, k_ext, cq, ck, valid_text, text_length);
   return launch_status();
