@@ -11,7 +11,8 @@
  * peco_assign_tokens_to_centers (bf16 split of fp32 tokens and centres),
  * peco_recompute_cluster_centers (sort scratch) and peco_sparse_attention
  * (attention plan and key blocks) take it from the stream-ordered allocator
- * (cudaMallocAsync / cudaFreeAsync on the caller's stream).
+ * (cudaMallocAsync / cudaFreeAsync on the caller's stream), as do the two
+ * selection entry points for their [BH,CQ,CK] fp32 logits.
  *
  * Device-side faults are never raised with traps: kernels skip out-of-range
  * indices and give up bounded waits, OR-ing a bit into a per-device status
