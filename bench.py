@@ -371,6 +371,19 @@ def run_ours(args, world, rank, local):
     e2e_max = allreduce(e2e_rank, world, "max")
     barrier(world)
 
+    # host enqueue time of the eager call (no device waits inside)
+    n_host = 10
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(n_host):
+        call()
+    host_eager_us = (time.perf_counter() - t0) / n_host * 1e6
+    torch.cuda.synchronize()
+
+    # the same call replayed as one CUDA graph (peco_b200.graph)
+    graph = _graph_leg(proc, q_init, k_init, q, k, v, flush, steps, world)
+    barrier(world)
+
     hbm, tf_burst, tf_sus, peak_kind = load_peaks()
     attn_ms = statistics.mean(stage["attention"])
     km_ms = statistics.mean(stage["kmeans"])
@@ -428,6 +441,7 @@ def run_ours(args, world, rank, local):
             "e2e": {"value": round(e2e_max / world, 5), "unit": "ms", "h2d_bytes_per_step": 3 * q.numel() * 2 * world,
                     "d2h_bytes_per_step": q.numel() * 2 * world,
                     "api": "peco_b200.processor.PecoAttention.attention with pinned host Q/K/V and output"},
+            "graph": dict(graph, host_enqueue_us_eager=round(host_eager_us, 1)),
             "gpu_launches": launches_job,
             "launches_per_call": round(launches / steps, 2),
             "clocks": clocks,
@@ -435,6 +449,44 @@ def run_ours(args, world, rank, local):
             "wall_s_timed_region": round(t_wall, 3),
         }
     return result, (q_c, k_c, v_c, w)
+
+
+def _graph_leg(proc, q_init, k_init, q, k, v, flush, steps, world):
+    """Device time per call of the steady-state call captured as one CUDA graph
+    (same work: centroids reset to the init before every replay, inputs
+    resident), plus the host time to enqueue one replay."""
+    import torch
+    from peco_b200.graph import PecoCallGraph
+    proc.q_centroids, proc.k_centroids = q_init, k_init
+    g = PecoCallGraph(proc, q, k, v)
+    inputs = g.inputs
+
+    def replay():
+        g.set_centroids(q_init, k_init)
+        return g(*inputs)
+
+    for _ in range(3):
+        replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for i in range(steps):
+        flush.zero_()
+        starts[i].record()
+        replay()
+        ends[i].record()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(10):
+        replay()
+    host_us = (time.perf_counter() - t0) / 10 * 1e6
+    torch.cuda.synchronize()
+    mean = allreduce(sum(a.elapsed_time(b) for a, b in zip(starts, ends)) / steps, world, "max")
+    proc.update_centroids_in_place = False
+    del g
+    return {"ms_per_call": round(mean / world, 5), "host_enqueue_us_graph": round(host_us, 1),
+            "api": "peco_b200.graph.PecoCallGraph (one graph launch per call)"}
 
 
 def _smi_id(dev):

@@ -51,10 +51,14 @@ def _initial_centers(x, n_clusters, init_centroids):
 class KmeansBuffers:
     """Device buffers of one fixed-iteration clustering (fused path)."""
 
-    def __init__(self, bh, tokens, clusters, dims, device):
+    def __init__(self, bh, tokens, clusters, dims, device, centers=None):
         f32, i32 = torch.float32, torch.int32
         self.labels = torch.empty((bh, tokens), dtype=i32, device=device)
-        self.centers = torch.empty((bh, clusters, dims), dtype=f32, device=device)
+        if centers is None:
+            centers = torch.empty((bh, clusters, dims), dtype=f32, device=device)
+        elif centers.shape != (bh, clusters, dims) or centers.dtype != f32 or not centers.is_contiguous():
+            raise ValueError("centers must be a contiguous fp32 [BH, C, D] tensor")
+        self.centers = centers
         # ping-pong centres + the centres' bf16 tensor-core image
         self.work = torch.empty((bh, int(_native.load().peco_kmeans_work_floats(clusters, dims))), dtype=f32,
                                 device=device)
@@ -68,17 +72,19 @@ class KmeansBuffers:
 
 
 def kmeans_fit_pair(q_rows, q_head_rows, q_tokens, q_init, k_rows, k_head_rows, k_tokens, k_init, bh, dims,
-                    iters):
+                    iters, *, q_centers=None, k_centers=None):
     """Fixed-iteration k-means of two bf16 problems in one library call.
 
     ``*_rows`` are bf16 tensors whose head b starts at row b*head_rows (the
     video prefix of a [B,H,S,D] tensor qualifies without a copy).  ``k_rows``
-    may be None.  Returns KmeansBuffers per problem.
+    may be None.  ``q_centers``/``k_centers`` optionally name the fp32 output
+    centres (they may be the init tensors themselves: the fit then updates
+    the centroids in place).  Returns KmeansBuffers per problem.
     """
     lib = _native.load()
     dev = _native.require_cuda(q_rows, q_init)
-    qb = KmeansBuffers(bh, q_tokens, q_init.shape[1], dims, dev)
-    kb = KmeansBuffers(bh, k_tokens, k_init.shape[1], dims, dev) if k_rows is not None else None
+    qb = KmeansBuffers(bh, q_tokens, q_init.shape[1], dims, dev, q_centers)
+    kb = KmeansBuffers(bh, k_tokens, k_init.shape[1], dims, dev, k_centers) if k_rows is not None else None
     z = _native.P(0)
 
     def args(rows, head_rows, tokens, init, b):

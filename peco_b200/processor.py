@@ -69,7 +69,16 @@ class InferenceContext:
 
 def dense_attention(query, key, value, valid_length):
     """Warmup path: full attention over [0, valid) and [valid, S) separately
-    (peco/processor.py:52-65)."""
+    (peco/processor.py:52-65).
+
+    CUDA fp16/bf16 inputs with D in {64, 128} run on the tcgen05 attention
+    kernel as a two-group partition -- groups [0, valid) and [valid, S), each
+    attending only to itself -- which is exactly the reference's pair of
+    varlen SDPA calls.  Other inputs take the reference's SDPA route."""
+    if (query.is_cuda and query.dtype in (torch.float16, torch.bfloat16) and query.shape[-1] in (64, 128)
+            and key.dtype == query.dtype and value.dtype == query.dtype and key.shape == query.shape
+            and value.shape == query.shape):
+        return _dense_attention_tc(query.contiguous(), key.contiguous(), value.contiguous(), valid_length)
     output = torch.empty_like(query)
     backend = SDPBackend.FLASH_ATTENTION if query.is_cuda else SDPBackend.MATH
     with sdpa_kernel(backend):
@@ -79,6 +88,21 @@ def dense_attention(query, key, value, valid_length):
                     query[:, :, start:end].contiguous(), key[:, :, start:end].contiguous(),
                     value[:, :, start:end].contiguous(), dropout_p=0.0)
     return output
+
+
+def _dense_attention_tc(query, key, value, valid_length):
+    """Block-diagonal partition of the sequence into [0, valid) and [valid, S)
+    on the sparse kernel (built on the device, so the call never synchronises
+    and can be captured in a CUDA graph)."""
+    from .attention_cuda import sparse_attention
+    b, h, s, _ = query.shape
+    if not 0 <= valid_length <= s:
+        raise ValueError("valid_length must lie in [0, S]")
+    sizes = torch.empty((b, h, 2), dtype=torch.int32, device=query.device)
+    sizes[..., 0] = valid_length
+    sizes[..., 1] = s - valid_length
+    groups = torch.eye(2, dtype=torch.bool, device=query.device).expand(b, h, 2, 2).contiguous()
+    return sparse_attention(query, key, value, groups, sizes, sizes, validate_sizes=False)
 
 
 def extend_text_partition(dynamic_map, q_sizes, k_sizes, valid_text, text_length):
@@ -114,6 +138,10 @@ class PecoAttention:
         # events recorded on the current stream at the stage boundaries
         # (kmeans, select, quantize_gather, attention) for profiling.
         self.stage_events = None
+        # When set, steady-state calls write the new fp32 centroids into the
+        # cached centroid tensors instead of fresh ones (fixed addresses, as a
+        # captured CUDA graph of the call needs; see peco_b200.graph).
+        self.update_centroids_in_place = False
 
     def reset(self):
         self.q_centroids = self.k_centroids = None
@@ -143,7 +171,9 @@ class PecoAttention:
                                                                              self.config.num_q_centroids)
         k_init = self.k_centroids if not initializing else _first_tokens_init(key.reshape(b * h, n, d),
                                                                              self.config.num_k_centroids)
-        qb, kb = kmeans_fit_pair(q_rows, q_stride, n, q_init, k_rows, k_stride, n, k_init, b * h, d, iters)
+        in_place = self.update_centroids_in_place and not initializing
+        qb, kb = kmeans_fit_pair(q_rows, q_stride, n, q_init, k_rows, k_stride, n, k_init, b * h, d, iters,
+                                 q_centers=q_init if in_place else None, k_centers=k_init if in_place else None)
         self.q_centroids, self.k_centroids = qb.centers, kb.centers
         return qb, kb
 

@@ -119,6 +119,47 @@ def test_warmup_then_sparse_state_machine():
     cached = proc.q_centroids.clone()
     out = proc.attention(q, k, v)
     assert torch.isfinite(out.float()).all()
-    assert not torch.equal(cached, proc.q_centroids) or True
+    # the step call refines the cached centres with kmeans_iter_step iterations
+    nv = w.video_tokens
+    _, ref_centers, _ = O.fit_token_clusters(q[0, :, :nv].float().cpu(), 16, 2, cached.cpu())
+    assert (proc.q_centroids.cpu() - ref_centers).abs().max() < 1e-2
     proc.reset()
     assert proc.q_centroids is None
+
+
+@pytest.mark.parametrize("dtype,dims,valid", [(torch.bfloat16, 128, 700), (torch.float16, 64, 1000),
+                                              (torch.bfloat16, 128, 1000), (torch.bfloat16, 64, 0)])
+def test_dense_warmup_attention_on_tc_kernel(dtype, dims, valid):
+    """dense_attention (peco/processor.py:52-65) on the tcgen05 kernel vs an fp32
+    torch restatement: softmax(QK^T/sqrt(D))V within [0,valid) and [valid,S)."""
+    from peco_b200.processor import dense_attention
+    g = torch.Generator().manual_seed(5)
+    s = 1000
+    q, k, v = (torch.randn((1, 3, s, dims), generator=g).to(dtype) for _ in range(3))
+    got = dense_attention(q.to(DEV), k.to(DEV), v.to(DEV), valid)
+    ref = torch.empty((1, 3, s, dims))
+    for a, b in ((0, valid), (valid, s)):
+        if a < b:
+            ref[:, :, a:b] = torch.nn.functional.scaled_dot_product_attention(
+                q[:, :, a:b].float(), k[:, :, a:b].float(), v[:, :, a:b].float())
+    check(got, ref)
+
+
+def test_graph_replay_matches_eager_calls():
+    """Three steady-state calls replayed from one captured CUDA graph equal three
+    eager calls bit for bit (outputs and the chained centroids)."""
+    from peco_b200.graph import PecoCallGraph
+    w = synthetic.workload("hv480", heads=2, grid=(2, 12, 18), text_length=32, valid_text=24, q_clusters=16,
+                           k_clusters=32, top_k=8, iters=2)
+    inputs = [tuple(t.to(DEV) for t in synthetic.make_inputs(w, seed=10 + i)) for i in range(3)]
+    eager = make_processor(w, *[t.cpu() for t in inputs[0][:2]])
+    graphed = make_processor(w, *[t.cpu() for t in inputs[0][:2]])
+    assert torch.equal(eager.q_centroids, graphed.q_centroids)
+    g = PecoCallGraph(graphed, *inputs[0])
+    for q, k, v in inputs:
+        want = eager.attention(q, k, v)
+        got = g(q, k, v)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want)
+        assert torch.equal(graphed.q_centroids, eager.q_centroids)
+        assert torch.equal(graphed.k_centroids, eager.k_centroids)
