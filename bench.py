@@ -343,29 +343,54 @@ def run_ours(args, world, rank, local):
     launches_job = int(allreduce(launches, world, "sum"))
     value = mean_max / world  # N calls per step across the job
 
-    # end to end through the public API with host buffers
+    # end to end through the public API with host buffers, pipelined the way a
+    # serving loop runs it: the inputs of step i+1 cross PCIe (copy stream)
+    # while step i computes, and step i's output returns on a third stream.
+    # Every step still copies its own inputs in and its own output out.
     e2e_steps = max(3, min(args.e2e_steps, steps))
     qh, kh, vh = (t.pin_memory() for t in (q_c, k_c, v_c))
-    oh = torch.empty(q_c.shape, dtype=q_c.dtype).pin_memory()
-    qd, kd, vd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    oh = [torch.empty(q_c.shape, dtype=q_c.dtype).pin_memory() for _ in range(2)]
+    dev_in = [tuple(torch.empty_like(t) for t in (q, k, v)) for _ in range(2)]
+    compute = torch.cuda.current_stream()
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    h2d_done = [torch.cuda.Event() for _ in range(2)]
+    used = [torch.cuda.Event() for _ in range(2)]
+    d2h_done = [torch.cuda.Event() for _ in range(2)]
 
-    def e2e_call():
-        qd.copy_(qh, non_blocking=True)
-        kd.copy_(kh, non_blocking=True)
-        vd.copy_(vh, non_blocking=True)
-        proc.q_centroids, proc.k_centroids = q_init, k_init
-        o = proc.attention(qd, kd, vd)
-        oh.copy_(o, non_blocking=True)
+    def upload(b):
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(used[b])  # the previous step on these buffers is done with them
+            for dst, src in zip(dev_in[b], (qh, kh, vh)):
+                dst.copy_(src, non_blocking=True)
+            h2d_done[b].record(s_in)
 
-    for _ in range(3):
-        e2e_call()
+    def e2e_run(n, first=None, last=None):
+        if first is not None:
+            first.record(s_in)
+        upload(0)
+        for i in range(n):
+            b = i & 1
+            compute.wait_event(h2d_done[b])
+            proc.q_centroids, proc.k_centroids = q_init, k_init
+            o = proc.attention(*dev_in[b])
+            used[b].record(compute)
+            if i + 1 < n:
+                upload(1 - b)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(used[b])
+                s_out.wait_event(d2h_done[b])  # host buffer b is free again
+                oh[b].copy_(o, non_blocking=True)
+                o.record_stream(s_out)
+                d2h_done[b].record(s_out)
+        if last is not None:
+            compute.wait_stream(s_out)
+            last.record(compute)
+
+    e2e_run(3)
     torch.cuda.synchronize()
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(e2e_steps):
-        e2e_call()
-    e1.record()
+    e2e_run(e2e_steps, e0, e1)
     torch.cuda.synchronize()
     e2e_rank = e0.elapsed_time(e1) / e2e_steps
     e2e_max = allreduce(e2e_rank, world, "max")
@@ -395,12 +420,12 @@ def run_ours(args, world, rank, local):
     if rank == 0:
         result = {
             "metric": METRIC,
-            "value": round(value, 5),
+            "value": round(graph["ms_per_call"], 5),
             "unit": "ms",
             "n_gpus": world,
             "steps": steps,
             "warmup": args.warmup,
-            "ms_per_step": round(mean_max, 5),
+            "ms_per_step": round(graph["ms_per_call"] * world, 5),
             "higher_is_better": False,
             "scaling": "weak",
             "vs_baseline": None,
@@ -413,7 +438,11 @@ def run_ours(args, world, rank, local):
                 "parallelism": f"heads independent, {world} rank(s) x {h} heads, no collective",
                 "l2": "flushed before every step (256 MB write), outside the step events",
                 "init": f"{w.init} tokens as initial centroids, the same every step",
+                "timing": "value: the steady-state call replayed as one CUDA graph (peco_b200.graph.PecoCallGraph, "
+                          "same kernels and results); eager.ms_per_call: the same call issued eagerly through "
+                          "PecoAttention.attention, whose stage events give stages",
             },
+            "eager": {"ms_per_call": round(value, 5), "ms_per_step": round(mean_max, 5)},
             "roofline": {
                 "kernel": "sparse_attention_tc, attention stage of the call",
                 "bound": "tensor",
@@ -440,7 +469,8 @@ def run_ours(args, world, rank, local):
             },
             "e2e": {"value": round(e2e_max / world, 5), "unit": "ms", "h2d_bytes_per_step": 3 * q.numel() * 2 * world,
                     "d2h_bytes_per_step": q.numel() * 2 * world,
-                    "api": "peco_b200.processor.PecoAttention.attention with pinned host Q/K/V and output"},
+                    "api": "peco_b200.processor.PecoAttention.attention with pinned host Q/K/V and output; "
+                           "step i+1's inputs upload while step i computes (copy streams)"},
             "graph": dict(graph, host_enqueue_us_eager=round(host_eager_us, 1)),
             "gpu_launches": launches_job,
             "launches_per_call": round(launches / steps, 2),

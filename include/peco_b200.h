@@ -110,8 +110,9 @@ int peco_sort_labels(const int32_t* labels, int32_t* indices, int32_t* counts, i
  * (Q and K of one call) in the same launches.  Head b of problem x starts at
  * row b*head_rows (so the video prefix of a [BH,S,D] tensor needs no copy).
  * Per problem: init [BH,C,D] fp32 (read), centers (final means of the last
- * partition, may alias init), work (BH * peco_kmeans_work_floats(C, D)
- * floats: ping-pong centres and the centres' bf16 tensor-core image), norms [BH,C],
+ * partition, may alias init), work (BH * peco_kmeans_work_floats(C, D, N)
+ * floats: ping-pong centres, the centres' bf16 tensor-core image and the
+ * token norms the first iteration records for the rest), norms [BH,C],
  * labels [BH,N], counts [BH,C], offsets [BH,C+1], perm [BH,N] (stable
  * argsort of the final labels).  Pass k_x = NULL for a single problem.
  * Replaces fit_token_clusters' CUDA loop, peco/clustering.py:59-88 with tol=0. */
@@ -123,7 +124,7 @@ int peco_kmeans_fit(const void* q_x, long long q_head_rows, int q_tokens, int q_
                     int iters, void* stream);
 
 /* Floats of ``work`` per head for peco_kmeans_fit (-1 for unsupported sizes). */
-long long peco_kmeans_work_floats(int clusters, int dims);
+long long peco_kmeans_work_floats(int clusters, int dims, int tokens);
 
 /* Boolean map [BH,CQ,CK] of kept (query cluster, key cluster) pairs: stable
  * descending sort of softmax(Cq.Ck^T/sqrt(D) + log count_k), keep while the

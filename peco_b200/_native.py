@@ -40,7 +40,7 @@ _SIGNATURES = {
     "peco_sparse_attention_restore": [P] * 5 + [I] * 6 + [P, I, P],
     "peco_attention_workspace_stride": [I, I, I, I],
     "peco_key_block_rows": [I, I],
-    "peco_kmeans_work_floats": [I, I],
+    "peco_kmeans_work_floats": [I, I, I],
     "peco_device_status": [P, I, P],
     "peco_error_string": [I],
     "peco_cluster_error_message": [I],

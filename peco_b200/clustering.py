@@ -59,9 +59,9 @@ class KmeansBuffers:
         elif centers.shape != (bh, clusters, dims) or centers.dtype != f32 or not centers.is_contiguous():
             raise ValueError("centers must be a contiguous fp32 [BH, C, D] tensor")
         self.centers = centers
-        # ping-pong centres + the centres' bf16 tensor-core image
-        self.work = torch.empty((bh, int(_native.load().peco_kmeans_work_floats(clusters, dims))), dtype=f32,
-                                device=device)
+        # ping-pong centres, the centres' bf16 tensor-core image, token norms
+        self.work = torch.empty((bh, int(_native.load().peco_kmeans_work_floats(clusters, dims, tokens))),
+                                dtype=f32, device=device)
         self.norms = torch.empty((bh, clusters), dtype=f32, device=device)
         self.counts = torch.empty((bh, clusters), dtype=i32, device=device)
         self.offsets = torch.empty((bh, clusters + 1), dtype=i32, device=device)

@@ -5,10 +5,16 @@
 // with no allowed key -> 0.
 //
 // Three kernels:
-//  * planner (one CTA per head): clamped cluster prefixes, the work units
-//    (up to 128 query rows of ONE query group, so masking is per key column
-//    only), the key-row -> key-block map, zeroed padding rows of the key
-//    blocks, and per unit the list of selected key clusters as block ranges;
+//  * planner (one CTA per head): clamped cluster prefixes, the work units,
+//    the key-row -> key-block map, zeroed padding rows of the key blocks, and
+//    per unit the list of selected key clusters as block ranges.  A unit is
+//    up to 128 consecutive query rows made of up to four whole consecutive
+//    query groups (a group larger than 128 rows gets units of its own); its
+//    key list is the union of its groups' selections, each entry tagged with
+//    the groups that selected it, so the masks are per (row group, key
+//    column).  Packing groups shares the key blocks they have in common (the
+//    text groups every video group attends, and neighbouring clusters'
+//    selections) and fills the 128-row tensor-core tile;
 //  * pack (drop-in path only): row-major K/V -> key blocks (internal.h).  The
 //    fused path writes key blocks straight from its quantise/gather kernel;
 //  * main kernel (persistent, one CTA per SM).  Per unit, the selected key
@@ -28,7 +34,9 @@
 //    peco/clustering.py:127-136 into the output store).
 // The MMA issuer runs one tile ahead (QK of tile t+1 before PV of tile t), so
 // the tensor core computes the next scores while the softmax warps work on the
-// current ones.  K and V stream through a 6-slot ring (three tiles in flight).
+// current ones.  K and V stream through a 5-slot ring (two and a half tiles
+// in flight), and Q is double-buffered so the next unit's tile arrives while
+// the current unit runs.
 //
 // Warp roles: warp 0 = producer (unit claims, bulk copies, tile masks), warp
 // 1 = MMA issuer (one thread) and TMEM owner, warps 2-9 = softmax + epilogue.
@@ -45,8 +53,10 @@ namespace {
 constexpr int kBM = kUnitRows;   // query rows per unit
 constexpr int kBN = 128;         // keys per tile
 constexpr int kTileBlocks = kBN / kKeyBlockRows;
-constexpr int kSlots = 6;        // K/V ring: slot of K(t) = 2t mod 6, V(t) = 2t+1 mod 6
+constexpr int kSlots = 5;        // K/V ring: slot of K(t) = 2t mod 5, V(t) = 2t+1 mod 5
+constexpr int kQBufs = 2;        // Q tiles: the next unit's loads while this one runs
 constexpr int kRing = 8;         // tile-info ring depth
+constexpr int kMaxGroups = 4;    // query groups per unit
 constexpr int kSoftmaxWarps = 8;
 constexpr int kThreads = 32 * (2 + kSoftmaxWarps);
 constexpr uint32_t kTmemCols = 512;  // S0 | S1 | O_0 | O_1, 128 columns each
@@ -69,13 +79,15 @@ struct AttnArgs {
 };
 
 struct TileInfo {
-  uint32_t mask[4];           // key columns of the tile that are valid
+  uint32_t mask[kMaxGroups][4];  // per row group: key columns of the tile it attends
   int unit;                   // virtual unit index (local * BH + head)
   uint32_t flags;
+  int shift;                  // TMEM lanes below this hold no row of the unit
+  uint32_t bounds;            // bytes 0-2: first row (within the unit) of groups 1-3, 0xff = none
 };
 
 struct __align__(8) Shared {
-  uint64_t q_full, q_empty;
+  uint64_t q_full[kQBufs], q_empty[kQBufs];
   uint64_t slot_full[kSlots], slot_empty[kSlots];
   uint64_t s_full[2], s_free[2], p_full[2];
   uint64_t o_full;
@@ -95,9 +107,10 @@ struct Layout {
   static constexpr int kBlockBytes = kKeyBlockRows * D * 2;
   static constexpr int kQPanel = kBM * 128;
   static constexpr int kQ0 = 0;
-  static constexpr int kSlot0 = kTileBytes;
+  static constexpr int kSlot0 = kQBufs * kTileBytes;
   static constexpr int kShared = kSlot0 + kSlots * kTileBytes;
   static constexpr int kSmem = 1024 + kShared + static_cast<int>(sizeof(Shared));
+  static_assert(kSmem <= 227 * 1024, "shared memory per CTA exceeds the sm_100a limit");
 };
 
 __device__ __forceinline__ int* work_counter(const AttnArgs& a) {
@@ -202,29 +215,54 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(const uint8_t* __restri
     if (tid == last) carry[0] = pre + v;
     __syncthreads();
   }
-  if (tid == 0) carry[0] = 0;
-  __syncthreads();
   int* units = w + g.off_units;
-  for (int o0 = 0; o0 < g.gq; o0 += blockDim.x) {
-    const int o = o0 + tid;
-    const int q = g.gq - 1 - o;
-    const int n = o < g.gq ? gcount[q] : 0;
-    const long long nu = (n + kBM - 1) / kBM;
-    const long long u0 = carry[0] + block_exclusive_scan(nu, tmp);
-    for (int i = 0; i < nu; ++i) {
-      int* rec = units + 4 * (u0 + i);
-      rec[0] = gstart[q] + i * kBM;
-      rec[1] = min(kBM, n - i * kBM);
-      ugroup[u0 + i] = q;
-    }
-    __syncthreads();
-    if (tid == last) carry[0] = u0 + nu;
-    __syncthreads();
-  }
+  // Units, later groups first (so the text groups, which attend every key,
+  // start early): consecutive whole groups are packed while the rows fit in
+  // kBM and there are at most kMaxGroups of them (a run of groups [lo, lo +
+  // ng), empty ones included); a group larger than kBM rows gets units alone.
   if (tid == 0) {
-    n_units = static_cast<int>(carry[0]);
+    int nu = 0, cur_lo = 0, cur_rows = 0, cur_ng = 0;
+    auto emit = [&](int q_start, int q_count, int lo, int ng, unsigned bounds) {
+      if (nu < g.max_units) {
+        int* rec = units + kUnitInts * nu;
+        rec[0] = q_start;
+        rec[1] = q_count;
+        rec[4] = lo;
+        rec[5] = ng;
+        rec[6] = static_cast<int>(bounds);
+        rec[7] = 0;
+        ugroup[nu] = (lo << 3) | ng;
+      }
+      ++nu;
+    };
+    auto close = [&]() {
+      if (cur_ng == 0) return;
+      unsigned bounds = 0xffffffu;
+      for (int m = 1; m < cur_ng; ++m) {
+        const unsigned off = static_cast<unsigned>(gstart[cur_lo + m] - gstart[cur_lo]);
+        bounds = (bounds & ~(0xffu << (8 * (m - 1)))) | (off << (8 * (m - 1)));
+      }
+      emit(gstart[cur_lo], cur_rows, cur_lo, cur_ng, bounds);
+      cur_rows = cur_ng = 0;
+    };
+    for (int q = g.gq - 1; q >= 0; --q) {
+      const int n = gcount[q];
+      if (n > kBM) {
+        close();
+        for (int i = 0; i * kBM < n; ++i) emit(gstart[q] + i * kBM, min(kBM, n - i * kBM), q, 1, 0xffffffu);
+        continue;
+      }
+      if (cur_ng == kMaxGroups || cur_rows + n > kBM) close();
+      if (n == 0 && cur_ng == 0) continue;  // a unit never starts with an empty group
+      cur_lo = q;  // groups are visited in descending order
+      cur_rows += n;
+      ++cur_ng;
+    }
+    close();
+    n_units = min(nu, static_cast<int>(g.max_units));
     w[0] = n_units;
   }
+  __syncthreads();
   // key row -> row of the key-block image
   int* rows = w + g.off_rows;
   for (int j = tid; j < g.sk; j += blockDim.x) {
@@ -259,16 +297,17 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(const uint8_t* __restri
   // per unit: the selected key clusters as entries over the unit's block list
   int2* ent_all = reinterpret_cast<int2*>(w + g.off_ent);
   for (int u = warp; u < n_units; u += nwarps) {
-    const int q = ugroup[u];
-    const uint8_t* mrow = map + (static_cast<long long>(head) * g.gq + q) * g.gk;
+    const int lo = ugroup[u] >> 3, ng = ugroup[u] & 7;
+    const uint8_t* mrow = map + (static_cast<long long>(head) * g.gq + lo) * g.gk;
     int2* ent = ent_all + static_cast<long long>(u) * g.gk;
     int nent = 0, blocks = 0;
     for (int c0 = 0; c0 < g.gk; c0 += 32) {
       const int c = c0 + lane;
-      int n = 0, nb = 0;
+      int n = 0, nb = 0, gm = 0;
       if (c < g.gk) {
         n = skp[c + 1] - skp[c];
-        if (n > 0 && mrow[c]) nb = sgp[c + 1] - sgp[c];
+        for (int m = 0; m < ng; ++m) gm |= (mrow[static_cast<long long>(m) * g.gk + c] ? 1 : 0) << m;
+        if (n > 0 && gm) nb = sgp[c + 1] - sgp[c];
       }
       const unsigned bal = __ballot_sync(0xffffffffu, nb > 0);
       int incl = nb;
@@ -280,14 +319,15 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(const uint8_t* __restri
       if (nb > 0) {
         const int pe = blocks + incl;
         const int idx = nent + __popc(bal & ((1u << lane) - 1u));
-        ent[idx] = make_int2(sgp[c] - (pe - nb), (pe << 4) | (n - kKeyBlockRows * (nb - 1)));
+        // (end position, groups that selected the cluster, rows in its last block)
+        ent[idx] = make_int2(sgp[c] - (pe - nb), (pe << 8) | (gm << 4) | (n - kKeyBlockRows * (nb - 1)));
       }
       nent += __popc(bal);
       blocks += __shfl_sync(0xffffffffu, incl, 31);
     }
     if (lane == 0) {
-      units[4 * u + 2] = nent;
-      units[4 * u + 3] = blocks;
+      units[kUnitInts * u + 2] = nent;
+      units[kUnitInts * u + 3] = blocks;
     }
   }
 }
@@ -334,8 +374,10 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
   const long long total_units = static_cast<long long>(args.bh) * g.max_units;
 
   if (threadIdx.x == 0) {
-    mbar_init(&sh.q_full, 1);
-    mbar_init(&sh.q_empty, 1);
+    for (int i = 0; i < kQBufs; ++i) {
+      mbar_init(&sh.q_full[i], 1);
+      mbar_init(&sh.q_empty[i], 1);
+    }
     for (int i = 0; i < kSlots; ++i) {
       mbar_init(&sh.slot_full[i], 1);
       mbar_init(&sh.slot_empty[i], 1);
@@ -377,19 +419,22 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
     int tile = 0;      // tiles issued by this CTA
     int entry = 0;     // info entries pushed
     int qloads = 0;    // Q tiles loaded
-    auto push_info = [&](const uint32_t (&mask)[4], int unit, uint32_t flags) {
+    // lane i < 16 writes mask word i (group i / 4, word i % 4)
+    auto push_info = [&](uint32_t my_word, int unit, uint32_t flags, int shift, uint32_t bounds) {
       const int slot = entry % kRing;
       if (ok && entry >= kRing) ok = mbar_wait_warp(&sh.info_empty[slot], ((entry / kRing) - 1) & 1, abort_flag, args.status);
-      if (lane == 0 && ok) {
+      if (ok) {
         TileInfo& ti = sh.info[slot];
-        ti.mask[0] = mask[0];
-        ti.mask[1] = mask[1];
-        ti.mask[2] = mask[2];
-        ti.mask[3] = mask[3];
-        ti.unit = unit;
-        ti.flags = flags;
-        mbar_arrive(&sh.info_full[slot]);
+        if (lane < 4 * kMaxGroups) ti.mask[lane >> 2][lane & 3] = my_word;
+        if (lane == 0) {
+          ti.unit = unit;
+          ti.flags = flags;
+          ti.shift = shift;
+          ti.bounds = bounds;
+        }
       }
+      __syncwarp();
+      if (lane == 0 && ok) mbar_arrive(&sh.info_full[slot]);
       __syncwarp();
       ++entry;
     };
@@ -403,32 +448,40 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
       const int local = static_cast<int>(v / args.bh);
       const int* w = args.ws + static_cast<long long>(head) * g.stride;
       if (local >= w[0] || local >= g.max_units) continue;
-      const int4 rec = *reinterpret_cast<const int4*>(w + g.off_units + 4 * local);
+      const int4 rec = *reinterpret_cast<const int4*>(w + g.off_units + kUnitInts * local);
+      const int4 rec2 = *reinterpret_cast<const int4*>(w + g.off_units + kUnitInts * local + 4);
+      const uint32_t bounds = static_cast<uint32_t>(rec2.z);
       const int q_start = rec.x;
+      // the unit's rows fill the TOP lanes of the 128-row tile (lanes
+      // shift..127): lane quarters 0 and 1, whose schedulers also run the
+      // producer and MMA warps, are the ones left without rows
+      const int shift = kBM - min(max(rec.y, 0), kBM);
       int nent = rec.z, nblk = rec.w;
       if (nent < 0 || nent > g.gk || nblk < 0) {  // not a plan of this geometry
         if (lane == 0) record_status(args.status, kDevBadIndex);
         nent = nblk = 0;
       }
       if (nblk == 0) {
-        const uint32_t zero[4] = {0, 0, 0, 0};
-        push_info(zero, static_cast<int>(v), kEmpty);  // no key at all: rows are zero
+        push_info(0u, static_cast<int>(v), kEmpty, shift, bounds);  // no key at all: rows are zero
         if (!ok) break;
         continue;
       }
       const int2* ents = reinterpret_cast<const int2*>(w + g.off_ent) + static_cast<long long>(local) * g.gk;
       const long long block0 = static_cast<long long>(head) * g.blocks;
-      // window of 32 entries, one per lane: block offset, end position, rows in last block
-      int w0 = 0, wz = 0, wend = 0x7fffffff, wlast = 0;
+      // window of 32 entries, one per lane: block offset, end position, rows
+      // in the last block, groups of the unit that attend the cluster
+      int w0 = 0, wz = 0, wend = 0x7fffffff, wlast = 0, wgm = 0;
       auto load_window = [&](int from) {
         w0 = from;
         wz = 0;
         wend = 0x7fffffff;
         wlast = 0;
+        wgm = 0;
         if (from + lane < nent) {
           const int2 e = ents[from + lane];
           wz = e.x;
-          wend = e.y >> 4;
+          wend = e.y >> 8;
+          wgm = (e.y >> 4) & 15;
           wlast = e.y & 15;
         }
       };
@@ -449,6 +502,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
         const int kz = __shfl_sync(0xffffffffu, wz, k);
         const int kend = __shfl_sync(0xffffffffu, wend, k);
         const int klast = __shfl_sync(0xffffffffu, wlast, k);
+        const int kgm = __shfl_sync(0xffffffffu, wgm, k);
         const int ngroups = min(kTileBlocks, nblk - p0);
         int blk = 0, valid = 0;
         if (lane < ngroups) {
@@ -493,30 +547,41 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
         if (t == 0) {
           // first tile of the unit: its Q tile, once the previous unit's last
           // QK has released the buffer (its K/V are already in flight)
-          if (ok && qloads > 0) ok = mbar_wait_warp(&sh.q_empty, (qloads - 1) & 1, abort_flag, args.status);
+          const int qb = qloads % kQBufs, qu = qloads / kQBufs;
+          if (ok && qu > 0) ok = mbar_wait_warp(&sh.q_empty[qb], (qu - 1) & 1, abort_flag, args.status);
           if (lane == 0 && ok) {
-            mbar_arrive_expect_tx(&sh.q_full, L::kTileBytes);
+            mbar_arrive_expect_tx(&sh.q_full[qb], L::kTileBytes);
 #pragma unroll
             for (int p = 0; p < D / 64; ++p)
-              tma_load_2d(base + L::kQ0 + p * L::kQPanel, &qmap, 64 * p,
-                          static_cast<int>(static_cast<long long>(head) * g.sq + q_start), &sh.q_full);
+              tma_load_2d(base + L::kQ0 + qb * L::kTileBytes + p * L::kQPanel, &qmap, 64 * p,
+                          static_cast<int>(static_cast<long long>(head) * g.sq + q_start - shift), &sh.q_full[qb]);
           }
           __syncwarp();
           ++qloads;
         }
+        // per block (lane): valid rows, one byte per group that attends it;
+        // lane i < 16 then assembles mask word i % 4 of group i / 4 (the
+        // bytes of blocks 4 (i % 4) .. 4 (i % 4) + 3)
         const unsigned bits = lane < ngroups ? ((1u << valid) - 1u) : 0u;
-        uint32_t word[4] = {0, 0, 0, 0};
+        unsigned bytes = 0;
 #pragma unroll
-        for (int b = 0; b < kTileBlocks; ++b) word[b >> 2] |= __shfl_sync(0xffffffffu, bits, b) << (8 * (b & 3));
-        push_info(word, static_cast<int>(v), (t == 0 ? kFirst : 0u) | (t == ntiles - 1 ? kLast : 0u));
+        for (int m = 0; m < kMaxGroups; ++m) bytes |= ((kgm >> m) & 1) ? bits << (8 * m) : 0u;
+        const int wi = lane & 3, gi = (lane >> 2) & 3;
+        uint32_t my_word = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const unsigned bb = __shfl_sync(0xffffffffu, bytes, 4 * wi + e);
+          my_word |= ((bb >> (8 * gi)) & 0xffu) << (8 * e);
+        }
+        push_info(my_word, static_cast<int>(v), (t == 0 ? kFirst : 0u) | (t == ntiles - 1 ? kLast : 0u), shift,
+                  bounds);
         ++tile;
         if (*abort_flag) ok = false;
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       }
       if (!ok) break;
     }
-    const uint32_t zero[4] = {0, 0, 0, 0};
-    push_info(zero, -1, kEnd);
+    push_info(0u, -1, kEnd, 0, 0xffffffu);
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA
@@ -524,7 +589,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
       constexpr uint32_t idesc_qk = instr_desc(128, kBN, AB, false, false);
       constexpr uint32_t idesc_pv = instr_desc(128, D, AB, false, true);
       bool ok = true;
-      int entry = 0, t = 0, qloads = 0;
+      int entry = 0, t = 0, qloads = 0, qbuf = 0;
       int cur = -1;  // tile whose P.V is pending
       uint32_t cur_flags = 0;
       auto issue_pv = [&]() {
@@ -560,14 +625,15 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
         // ---- S[t%2] = Q K^T for the next tile
         const int b = t & 1, item = 2 * t, sl = item % kSlots;
         if (fl & kFirst) {
-          ok = mbar_wait(&sh.q_full, qloads & 1, abort_flag, args.status);
+          qbuf = qloads % kQBufs;
+          ok = mbar_wait(&sh.q_full[qbuf], (qloads / kQBufs) & 1, abort_flag, args.status);
           ++qloads;
         }
         if (ok) ok = mbar_wait(&sh.slot_full[sl], (item / kSlots) & 1, abort_flag, args.status);
         if (ok && t >= 2) ok = mbar_wait(&sh.s_free[b], ((t >> 1) - 1) & 1, abort_flag, args.status);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t qa = smem_u32(base + L::kQ0);
+        const uint32_t qa = smem_u32(base + L::kQ0 + qbuf * L::kTileBytes);
         const uint32_t ka = smem_u32(base + L::kSlot0 + sl * L::kTileBytes);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -577,7 +643,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
         }
         umma_commit(&sh.s_full[b]);
         umma_commit(&sh.slot_empty[sl]);
-        if (fl & kLast) umma_commit(&sh.q_empty);
+        if (fl & kLast) umma_commit(&sh.q_empty[qbuf]);
         // ---- O += P V for the previous tile
         if (cur >= 0) {
           issue_pv();
@@ -606,10 +672,11 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
     // output row of unit v for this thread (nullptr: not a real row)
     auto out_row = [&](int v) -> T* {
       const int head = v % args.bh, local = v / args.bh;
-      const int* rec = args.ws + static_cast<long long>(head) * g.stride + g.off_units + 4 * local;
-      const int q_start = rec[0], q_count = rec[1];
-      if (r >= q_count) return nullptr;
-      const int prow = q_start + r;
+      const int* rec = args.ws + static_cast<long long>(head) * g.stride + g.off_units + kUnitInts * local;
+      const int q_start = rec[0], q_count = min(max(rec[1], 0), kBM);
+      const int rr = r - (kBM - q_count);  // rows fill the top lanes
+      if (rr < 0) return nullptr;
+      const int prow = q_start + rr;
       long long orow = prow;
       if (args.perm && prow < args.video) orow = args.perm[static_cast<long long>(head) * args.video + prow];
       if (orow < 0 || orow >= args.out_rows) {
@@ -622,7 +689,18 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
       const int slot = entry % kRing;
       ok = mbar_wait_warp(&sh.info_full[slot], (entry / kRing) & 1, abort_flag, args.status);
       if (!ok) break;
-      const TileInfo ti = sh.info[slot];
+      // read what this thread needs before the slot is released: the tile's
+      // flags and unit, and the two mask words of this row's group
+      const TileInfo& ts = sh.info[slot];
+      TileInfo ti;
+      ti.flags = ts.flags;
+      ti.unit = ts.unit;
+      ti.shift = ts.shift;
+      const uint32_t tb = ts.bounds;
+      const int rr = r - ti.shift;
+      const int grp = (rr >= static_cast<int>(tb & 0xffu)) + (rr >= static_cast<int>((tb >> 8) & 0xffu)) +
+                      (rr >= static_cast<int>((tb >> 16) & 0xffu));
+      const uint32_t mw[2] = {ts.mask[grp][2 * half], ts.mask[grp][2 * half + 1]};
       __syncwarp();
       if (lane == 0) mbar_arrive(&sh.info_empty[slot]);
       ++entry;
@@ -643,6 +721,11 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
       const int b = t & 1;
       ok = mbar_wait_warp(&sh.s_full[b], (t >> 1) & 1, abort_flag, args.status);
       if (!ok) break;
+      // a warp whose 32 lanes hold no row of the unit skips the softmax: the
+      // P.V of its lanes then reads stale TMEM, which only feeds O rows that
+      // are never stored
+      const bool idle = quarter * 32 + 31 < ti.shift;
+      if (!idle) {
       tc_fence_after();
       constexpr int kCols = kBN / 2;
       float s[kCols];
@@ -659,7 +742,6 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
       float mxc[kChains];
 #pragma unroll
       for (int i = 0; i < kChains; ++i) mxc[i] = -INFINITY;
-      const uint32_t mw[2] = {half ? ti.mask[2] : ti.mask[0], half ? ti.mask[3] : ti.mask[1]};
 #pragma unroll
       for (int j = 0; j < kCols; ++j) {
         const bool valid = (mw[j >> 5] >> (j & 31)) & 1u;
@@ -727,6 +809,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
       }
       tmem_st_wait();
       tc_fence_before();
+      }  // !idle
       __syncwarp();
       if (lane == 0) mbar_arrive(&sh.p_full[b]);
       ++t;
@@ -763,10 +846,10 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
           if (lane == 0) mbar_arrive(&sh.xch_back[quarter]);
         }
         ++units_done;
-        T* dst = out_row(ti.unit);
+        T* dst = idle ? nullptr : out_row(ti.unit);
         __syncwarp();
 #pragma unroll
-        for (int c = 0; c < D / 64; ++c) {
+        for (int c = 0; c < D / 64 && !idle; ++c) {
           // this warp writes output dims [D/2 half, D/2 (half + 1))
           uint32_t v0[32], v1[32];
           tmem_ld32_sync(tmem + 256 + lane_off + (D / 2) * half + c * 32, v0);
@@ -832,8 +915,9 @@ int check_shape(int bh, int sq, int sk, int d, int gq, int gk) {
   if (bh < 1 || bh > 65535 || sq < 0 || sk < 0 || gq < 1 || gk < 1) return kErrInvalidValue;
   if (d != 64 && d != 128) return kErrUnsupported;
   const PlanGeom g = plan_geom(sq, sk, gq, gk);
-  // int32 positions (entries pack end << 4), unit indices and per-head offsets
-  if (g.blocks * kKeyBlockRows > (1LL << 26) || static_cast<long long>(bh) * g.max_units > 2147483647LL ||
+  // int32 positions (entries pack the end position << 8, so blocks < 2^23),
+  // unit indices and per-head offsets
+  if (g.blocks >= (1LL << 23) || static_cast<long long>(bh) * g.max_units > 2147483647LL ||
       g.stride > 2147483647LL)
     return kErrUnsupported;
   return kOk;

@@ -100,6 +100,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete is
+// parked by the hardware until the phase completes or ``kSuspendHintNs``
+// passes, instead of re-issuing the poll (spinning warps otherwise take issue
+// slots from the warps that share their scheduler).
+constexpr uint32_t kSuspendHintNs = 20000;
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait on an mbarrier phase.  Returns false when the wait expired or
 // another warp of the CTA already gave up (``abort_flag`` set); the caller
 // must then stop issuing work.
@@ -108,7 +125,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
   for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_suspend(bar, parity)) return true;
     if ((it & 63u) == 0) {
       if (*abort_flag) return false;
       if (globaltimer() - t0 > kWaitTimeoutNs || it > kWaitMaxSpins) {

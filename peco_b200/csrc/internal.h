@@ -22,6 +22,7 @@ struct KmeansProblem {
   int32_t* offsets;       // [B, C+1] cluster starts in the packed order
   int32_t* perm;          // [B, tokens] stable argsort of the last labels
   unsigned char* image;   // [B, image bytes per head] bf16 hi/lo image of the centres being assigned against
+  float* xnorm;           // [B, tokens] token norms |x| (written by the first assignment, read by the rest)
 };
 
 int kmeans_fit_bf16(int njobs, const KmeansProblem* probs, int bh, int dims, int iters, cudaStream_t stream);
@@ -66,6 +67,10 @@ constexpr int kUnitRows = 128;  // query rows per attention work unit
 //                           (first block - first position, end position << 4 | rows in last block)
 // The last int of the last head's region is the work counter of the
 // persistent attention kernel.
+// ints per work unit in the plan: q_start, q_count, entries, blocks, first
+// query group, groups, group bounds, padding
+constexpr int kUnitInts = 8;
+
 struct PlanGeom {
   int sq, sk, gq, gk;
   long long max_units, blocks;
@@ -83,7 +88,7 @@ __host__ __device__ inline PlanGeom plan_geom(int sq, int sk, int gq, int gk) {
   g.off_kp = 4;
   g.off_gp = g.off_kp + gk + 1;
   g.off_units = (g.off_gp + gk + 1 + 3) & ~3LL;
-  g.off_rows = g.off_units + 4 * g.max_units;
+  g.off_rows = g.off_units + kUnitInts * g.max_units;
   g.off_ent = (g.off_rows + sk + 3) & ~3LL;
   g.stride = (g.off_ent + 2 * g.max_units * gk + 1 + 3) & ~3LL;
   return g;

@@ -53,7 +53,15 @@ constexpr int kMaxCand = 8;
 constexpr int kEpiWarps = 8;
 constexpr int kMmaWarp = 1, kEpiWarp0 = 2;
 constexpr int kAssignThreads = 32 * (kEpiWarp0 + kEpiWarps);
-constexpr float kBoundScale = 2.44140625e-4f;      // 2^-12
+// Near-tie tolerance of the tensor-core distance d' = |c|^2 - 2 x.(c_hi + c_lo)
+// against the fp32 distance: |d' - d| <= kBoundScale |x| max|c| + kBoundTiny
+// (max|c|^2 + 2 |x| max|c|).  The split residual is <= 2^-18 |x||c| and the
+// largest accumulation error measured on B200 (1.3M tokens of the HV-480
+// mixture, fp32 centres at four noise scales, compared with fp64) is
+// 2^-18.2 |x| max|c|, so 2^-15 keeps a 9x margin over what was seen.  Any
+// centre within twice the tolerance of the best is settled by an exact fp32
+// recompute, so a label can only differ from the fp32 argmin at a tie.
+constexpr float kBoundScale = 3.0517578125e-5f;    // 2^-15
 constexpr float kBoundTiny = 9.5367431640625e-7f;  // 2^-20
 constexpr int kCopyPiece = 32768;                  // bytes per bulk copy
 
@@ -161,6 +169,8 @@ struct AssignJob {
   const float* norms;           // [B, C]
   const unsigned char* image;   // [B, nchunks * b_bytes]
   int32_t* labels;              // [B, tokens]
+  const float* xn_in;           // optional [B, tokens] token norms |x| (skips recomputing them)
+  float* xn_out;                // optional [B, tokens]: |x| written for later iterations
 };
 
 struct AssignJobs {
@@ -443,8 +453,14 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
       ok = mbar_wait_warp(&sb.a_full[s], (i / NA) & 1, abort_flag, status);
       if (!ok) break;
       const unsigned char* a_hi = base + S.a_off + s * S.a_bytes;
-      // this half's share of |x|^2: dims [half D/2, (half + 1) D/2)
+      // the token norm: cached by an earlier iteration, or this half's share
+      // of |x|^2 (dims [half D/2, (half + 1) D/2)), merged below
+      const int tok_r = it.tile * kTileM + r;
+      const bool cached_xn = J.xn_in != nullptr;
+      float xn_cached = 0.0f;
+      if (cached_xn && half == 0 && tok_r < J.tokens) xn_cached = J.xn_in[static_cast<long long>(it.head) * J.tokens + tok_r];
       float ss = 0.0f;
+      if (!cached_xn)
 #pragma unroll
       for (int h8 = 0; h8 < D / 16; ++h8) {
         const int ch = half * (D / 16) + h8;
@@ -580,7 +596,8 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
           if (o.x < m1 || (o.x == m1 && oi < i1)) i1 = oi;
           m1 = fminf(m1, o.x);
           if (k == 0) {
-            const float xn = sqrtf(ss + o.w);
+            const float xn = cached_xn ? xn_cached : sqrtf(ss + o.w);
+            if (J.xn_out && tok_r < J.tokens) J.xn_out[static_cast<long long>(it.head) * J.tokens + tok_r] = xn;
             E2 = 2.0f * (kBoundScale * xn * cmax + kBoundTiny * (cmax * cmax + 2.0f * xn * cmax));
           }
         }
@@ -775,13 +792,15 @@ struct LaneRaw {
   __device__ __forceinline__ float get(int e) const { return to_f32<T>(reinterpret_cast<const T*>(w)[e]); }
 };
 
-// One warp per cluster; lane l owns elements [l*E, (l+1)*E).  The cluster's
-// token ids arrive 32 at a time in one coalesced load (the next batch is
-// prefetched), the rows of a batch are all in flight at once, and the sums
-// run strictly in ascending token order (bit-exact with a sequential
-// scatter-add).
+// One warp per cluster, two warps per block (a block slot frees as soon as its
+// two clusters are done, so uneven cluster sizes hold few warps back); lane l
+// owns elements [l*E, (l+1)*E).  The cluster's token ids arrive 32 at a time
+// in one coalesced load (the next batch is prefetched), 16 rows are in flight
+// at once, and the sums run strictly in ascending token order (bit-exact with
+// a sequential scatter-add).
+constexpr int kUpdateThreads = 64;
 template <int D, typename T>
-__global__ void __launch_bounds__(256, 2) kmeans_update_kernel(const UpdateJobs jobs, int bh, unsigned* status) {
+__global__ void __launch_bounds__(kUpdateThreads, 8) kmeans_update_kernel(const UpdateJobs jobs, int bh, unsigned* status) {
   const UpdateJob& J = jobs.job[blockIdx.y];
   const long long w = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -923,9 +942,9 @@ long long image_bytes_per_head(int C, int dims) {
 template <typename T>
 int launch_update_t(const UpdateJobs& jobs, int njobs, int bh, int dims, int max_clusters, cudaStream_t stream) {
   const long long warps = static_cast<long long>(bh) * max_clusters;
-  dim3 grid(static_cast<unsigned>((warps * 32 + 255) / 256), njobs);
-  if (dims == 128) kmeans_update_kernel<128, T><<<grid, 256, 0, stream>>>(jobs, bh, device_status_ptr());
-  else if (dims == 64) kmeans_update_kernel<64, T><<<grid, 256, 0, stream>>>(jobs, bh, device_status_ptr());
+  dim3 grid(static_cast<unsigned>((warps * 32 + kUpdateThreads - 1) / kUpdateThreads), njobs);
+  if (dims == 128) kmeans_update_kernel<128, T><<<grid, kUpdateThreads, 0, stream>>>(jobs, bh, device_status_ptr());
+  else if (dims == 64) kmeans_update_kernel<64, T><<<grid, kUpdateThreads, 0, stream>>>(jobs, bh, device_status_ptr());
   else return kErrUnsupported;
   return launch_status();
 }
@@ -966,7 +985,9 @@ int kmeans_fit_bf16(int njobs, const KmeansProblem* probs, int bh, int dims, int
       const bool even_left = ((iters - 1 - it) & 1) == 0;
       const float* cur = (it == 0) ? p.centers_a : (even_left ? p.centers_b : p.centers_out);
       float* nxt = even_left ? p.centers_out : p.centers_b;  // in-place is safe: each lane reads then writes
-      aj.job[j] = {p.tokens, p.clusters, p.head_rows, nullptr, cur, p.norms, p.image, p.labels};
+      // the first iteration records the token norms, later ones read them
+      aj.job[j] = {p.tokens, p.clusters, p.head_rows, nullptr, cur, p.norms, p.image, p.labels,
+                   it > 0 ? p.xnorm : nullptr, it == 0 ? p.xnorm : nullptr};
       // the last update needs no image: nothing assigns against it
       uj.job[j] = {p.x, p.head_rows, p.tokens, p.clusters, p.perm, p.offsets, cur, nxt, nullptr, p.norms,
                    it + 1 < iters ? p.image : nullptr};
@@ -987,9 +1008,9 @@ int kmeans_fit_bf16(int njobs, const KmeansProblem* probs, int bh, int dims, int
   return 0;
 }
 
-long long kmeans_work_floats(int clusters, int dims) {
-  if (clusters < 1 || (dims != 64 && dims != 128)) return -1;
-  return static_cast<long long>(clusters) * dims + image_bytes_per_head(clusters, dims) / 4;
+long long kmeans_work_floats(int clusters, int dims, int tokens) {
+  if (clusters < 1 || tokens < 1 || (dims != 64 && dims != 128)) return -1;
+  return static_cast<long long>(clusters) * dims + image_bytes_per_head(clusters, dims) / 4 + tokens;
 }
 
 }  // namespace peco
@@ -1032,7 +1053,7 @@ extern "C" int peco_assign_tokens_to_centers(const float* x, const float* center
     AssignJobs jobs{};
     jobs.njobs = 1;
     jobs.bh = batch;
-    jobs.job[0] = {tokens, clusters, tokens, x, centers, center_norms, img, labels};
+    jobs.job[0] = {tokens, clusters, tokens, x, centers, center_norms, img, labels, nullptr, nullptr};
     const void* xh[2] = {hi, hi};
     const void* xl[2] = {lo, lo};
     const long long nrows[2] = {rows, rows};
@@ -1129,17 +1150,24 @@ extern "C" int peco_kmeans_fit(const void* q_x, long long q_head_rows, int q_tok
                                int k_clusters, int32_t* k_labels, const float* k_init, float* k_centers, float* k_work,
                                float* k_norms, int32_t* k_counts, int32_t* k_offsets, int32_t* k_perm, int bh, int dims,
                                int iters, void* stream) {
-  // work per problem: [bh, C, D] ping-pong centres, then the bh centroid images
+  // work per problem: [bh, C, D] ping-pong centres, the bh centroid images,
+  // then the [bh, tokens] token norms
   auto image_of = [&](float* work, int clusters) {
     return work ? reinterpret_cast<unsigned char*>(work + static_cast<long long>(bh) * clusters * dims) : nullptr;
   };
+  auto xnorm_of = [&](float* work, int clusters) {
+    if (!work || clusters < 1 || (dims != 64 && dims != 128)) return static_cast<float*>(nullptr);
+    return work + static_cast<long long>(bh) * clusters * dims + static_cast<long long>(bh) * (image_bytes_per_head(clusters, dims) / 4);
+  };
   KmeansProblem p[2];
   p[0] = {q_x, q_head_rows, q_tokens, q_clusters, q_init, q_work, q_centers, q_norms, q_labels, q_counts, q_offsets, q_perm,
-          image_of(q_work, q_clusters)};
+          image_of(q_work, q_clusters), xnorm_of(q_work, q_clusters)};
   p[1] = {k_x, k_head_rows, k_tokens, k_clusters, k_init, k_work, k_centers, k_norms, k_labels, k_counts, k_offsets, k_perm,
-          image_of(k_work, k_clusters)};
+          image_of(k_work, k_clusters), xnorm_of(k_work, k_clusters)};
   const int njobs = k_x ? 2 : 1;
   return kmeans_fit_bf16(njobs, p, bh, dims, iters, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" long long peco_kmeans_work_floats(int clusters, int dims) { return peco::kmeans_work_floats(clusters, dims); }
+extern "C" long long peco_kmeans_work_floats(int clusters, int dims, int tokens) {
+  return peco::kmeans_work_floats(clusters, dims, tokens);
+}

@@ -86,7 +86,7 @@ struct SortJobs {
 };
 
 __global__ void __launch_bounds__(kSortThreads) stable_sort_labels_kernel(const SortJobs jobs, unsigned* status) {
-  const SortJob& J = jobs.job[blockIdx.y];
+  const SortJob J = blockIdx.y ? jobs.job[1] : jobs.job[0];  // no dynamic index into the parameters
   if (static_cast<int>(blockIdx.x) >= J.rows) return;
   const int32_t* __restrict__ labels = J.labels;
   const long long label_stride = J.label_stride;
@@ -107,16 +107,33 @@ __global__ void __launch_bounds__(kSortThreads) stable_sort_labels_kernel(const 
   for (int i = threadIdx.x; i < parts * clusters; i += blockDim.x) hist[i] = 0;
   __syncthreads();
   const int plen = (tokens + parts - 1) / parts;
+  // The first kSortCache batches of each partition are loaded once, all in
+  // flight together, and kept in registers for both passes (the labels of a
+  // 6750-token head fit); longer partitions load the rest as they go.
+  constexpr int kSortCache = 8;
+  int cached[kSortCache];
+  const int p0 = warp * plen, p1 = min(tokens, p0 + plen);
+  auto label_at = [&](int t, bool report) {
+    int l = (t < p1) ? lab[t] : -1;
+    if (l >= clusters || (t < p1 && l < 0)) {
+      if (report) record_status(status, kDevBadIndex);
+      l = -1;
+    }
+    return l;
+  };
+#pragma unroll
+  for (int i = 0; i < kSortCache; ++i) cached[i] = (warp < parts) ? label_at(p0 + 32 * i + lane, true) : -1;
   // phase 1: per-partition histograms (warp-aggregated, no atomics: one leader per label)
   if (warp < parts) {
-    const int p0 = warp * plen, p1 = min(tokens, p0 + plen);
-    for (int base = p0; base < p1; base += 32) {
-      const int t = base + lane;
-      int l = (t < p1) ? lab[t] : -1;
-      if (l >= clusters || (t < p1 && l < 0)) {
-        record_status(status, kDevBadIndex);
-        l = -1;
-      }
+#pragma unroll
+    for (int i = 0; i < kSortCache; ++i) {
+      const int l = cached[i];
+      const unsigned peers = __match_any_sync(0xffffffffu, l);
+      if (l >= 0 && (peers & lt_mask) == 0) hist[warp * clusters + l] += __popc(peers);
+      __syncwarp();
+    }
+    for (int base = p0 + 32 * kSortCache; base < p1; base += 32) {
+      const int l = label_at(base + lane, true);
       const unsigned peers = __match_any_sync(0xffffffffu, l);
       if (l >= 0 && (peers & lt_mask) == 0) hist[warp * clusters + l] += __popc(peers);
       __syncwarp();
@@ -171,11 +188,7 @@ __global__ void __launch_bounds__(kSortThreads) stable_sort_labels_kernel(const 
   __syncthreads();
   // phase 3: stable placement
   if (warp < parts) {
-    const int p0 = warp * plen, p1 = min(tokens, p0 + plen);
-    for (int base = p0; base < p1; base += 32) {
-      const int t = base + lane;
-      int l = (t < p1) ? lab[t] : -1;
-      if (l >= clusters || l < 0) l = -1;
+    auto place = [&](int t, int l) {
       const unsigned peers = __match_any_sync(0xffffffffu, l);
       int pos = 0;
       if (l >= 0) pos = hist[warp * clusters + l] + __popc(peers & lt_mask);
@@ -185,7 +198,10 @@ __global__ void __launch_bounds__(kSortThreads) stable_sort_labels_kernel(const 
         if ((peers & lt_mask) == 0) hist[warp * clusters + l] += __popc(peers);
       }
       __syncwarp();
-    }
+    };
+#pragma unroll
+    for (int i = 0; i < kSortCache; ++i) place(p0 + 32 * i + lane, cached[i]);
+    for (int base = p0 + 32 * kSortCache; base < p1; base += 32) place(base + lane, label_at(base + lane, false));
   }
 }
 

@@ -46,14 +46,14 @@ def test_pure_host_functions(lib):
     assert l.peco_library_version() == 1
     assert b"no error" in l.peco_error_string(0)
     assert b"workspace" in l.peco_error_string(20005)
-    # plan workspace: header, two cluster prefixes, units, the key-row map
+    # plan workspace: header, two cluster prefixes, units (8 ints each), the key-row map
     # and one int2 entry per (unit, key cluster); key blocks: one 8-row block
     # per started 8 rows plus one padding block per cluster at most
     for sq, sk, gq, gk in ((11776, 11776, 130, 258), (119056, 119056, 1026, 2050), (64, 80, 64, 64), (1, 1, 1, 1)):
         units = (sq + 127) // 128 + gq
         stride = l.peco_attention_workspace_stride(sq, sk, gq, gk)
-        assert stride % 4 == 0 and stride >= 4 + 2 * (gk + 1) + 4 * units + sk + 2 * units * gk + 1
-        assert stride <= 4 + 2 * (gk + 1) + 4 * units + sk + 2 * units * gk + 16
+        assert stride % 4 == 0 and stride >= 4 + 2 * (gk + 1) + 8 * units + sk + 2 * units * gk + 1
+        assert stride <= 4 + 2 * (gk + 1) + 8 * units + sk + 2 * units * gk + 16
         assert l.peco_key_block_rows(sk, gk) == 8 * ((sk + 7) // 8 + gk)
     assert l.peco_attention_workspace_stride(1, 1, 0, 1) == -1
 
