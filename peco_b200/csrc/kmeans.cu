@@ -165,6 +165,7 @@ struct AssignJob {
   int tokens, clusters;
   long long head_rows;          // rows between consecutive heads in the token maps
   const float* x32;             // fp32 rows for the exact recompute (split mode), else null
+  const __nv_bfloat16* xb;      // bf16 rows for the exact recompute (bf16 mode), else null
   const float* centers;         // [B, C, D] fp32 (exact recompute of near-ties)
   const float* norms;           // [B, C]
   const unsigned char* image;   // [B, nchunks * b_bytes]
@@ -261,6 +262,11 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
   const long long f_end = item_at(jobs, total_cost * (blockIdx.x + 1) / jobs.ncta);
   if (f_begin >= f_end) return;
   const AssignSmem S = assign_smem(jobs.job[0].clusters, jobs.njobs > 1 ? jobs.job[1].clusters : 1, jobs.njobs, D, SPLIT);
+  // The token tile in shared memory is read by the MMA, and by the epilogue
+  // only to compute |x| (when no cached norms are given): the exact recompute
+  // of near-ties reads its rows from global memory, so a slot is free for the
+  // next tile as soon as the MMAs (and the |x| pass, if any) are done.
+  const bool epi_reads_a = jobs.job[0].xn_in == nullptr || (jobs.njobs > 1 && jobs.job[1].xn_in == nullptr);
 
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -275,7 +281,9 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
     mbar_init(&sb.g_free, 1 + kEpiWarps);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sb.a_full[i], 1);
-      mbar_init(&sb.a_empty[i], kEpiWarps);
+      // the tile's MMAs always release it; the epilogue warps too when they
+      // read it for the token norms
+      mbar_init(&sb.a_empty[i], 1 + (epi_reads_a ? kEpiWarps : 0));
       mbar_init(&sb.b_full[i], 1);
       mbar_init(&sb.b_empty[i], 1);
       mbar_init(&sb.acc_full[i], 1);
@@ -419,6 +427,7 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
           umma_commit(&sb.acc_full[as]);
           if (!S.resident) umma_commit(&sb.b_empty[bs]);
         }
+        if (ok) umma_commit(&sb.a_empty[s]);
         if (ok && last_of_group(f, it)) umma_commit(&sb.g_free);
       }
       // drain our MMAs before TMEM is released
@@ -450,7 +459,11 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
         ++ngroups;
       }
       const int s = static_cast<int>(i % NA);
-      ok = mbar_wait_warp(&sb.a_full[s], (i / NA) & 1, abort_flag, status);
+      // Only a launch whose epilogue reads the tile waits for it (and holds
+      // the slot until it has): otherwise the MMA may already have released
+      // the slot and the producer refilled it, so this phase parity would
+      // name a later tile.  acc_full below orders everything else.
+      if (epi_reads_a) ok = mbar_wait_warp(&sb.a_full[s], (i / NA) & 1, abort_flag, status);
       if (!ok) break;
       const unsigned char* a_hi = base + S.a_off + s * S.a_bytes;
       // the token norm: cached by an earlier iteration, or this half's share
@@ -481,6 +494,10 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
           ss = fmaf(x0, x0, ss);
           ss = fmaf(x1, x1, ss);
         }
+      }
+      if (epi_reads_a) {  // done with the tile in shared memory
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sb.a_empty[s]);
       }
       float E2 = 0.0f;  // half 0: bound once both norm halves are known
       float best = INFINITY;
@@ -661,13 +678,10 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
 #pragma unroll
             for (int e = 0; e < E; ++e) xv[e] = xr[e];
           } else {
-            const int srow = quarter * 32 + src;
-            const int d0 = lane * E;
-            const uint4 u = *reinterpret_cast<const uint4*>(a_hi + (d0 >> 6) * a_panel + srow * 128 +
-                                                            ((((d0 & 63) >> 3) ^ (srow & 7)) << 4));
-            const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u) + (d0 & 7);
+            // the token row from global memory (its shared-memory tile may already hold the next tile)
+            const __nv_bfloat16* xr = J.xb + (static_cast<long long>(it.head) * J.head_rows + stok) * D + lane * E;
 #pragma unroll
-            for (int e = 0; e < E; ++e) xv[e] = __bfloat162float(h[e]);
+            for (int e = 0; e < E; ++e) xv[e] = __bfloat162float(xr[e]);
           }
           float bd = INFINITY;
           int bl = 0x7fffffff;
@@ -717,10 +731,7 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
         if (valid) J.labels[static_cast<long long>(it.head) * J.tokens + tok] = label;
       }
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&sb.a_empty[s]);
-        if (last_of_group(f, it)) mbar_arrive(&sb.g_free);
-      }
+      if (lane == 0 && last_of_group(f, it)) mbar_arrive(&sb.g_free);
     }
   }
   __syncwarp();
@@ -986,8 +997,8 @@ int kmeans_fit_bf16(int njobs, const KmeansProblem* probs, int bh, int dims, int
       const float* cur = (it == 0) ? p.centers_a : (even_left ? p.centers_b : p.centers_out);
       float* nxt = even_left ? p.centers_out : p.centers_b;  // in-place is safe: each lane reads then writes
       // the first iteration records the token norms, later ones read them
-      aj.job[j] = {p.tokens, p.clusters, p.head_rows, nullptr, cur, p.norms, p.image, p.labels,
-                   it > 0 ? p.xnorm : nullptr, it == 0 ? p.xnorm : nullptr};
+      aj.job[j] = {p.tokens, p.clusters, p.head_rows, nullptr, static_cast<const __nv_bfloat16*>(p.x), cur, p.norms,
+                   p.image, p.labels, it > 0 ? p.xnorm : nullptr, it == 0 ? p.xnorm : nullptr};
       // the last update needs no image: nothing assigns against it
       uj.job[j] = {p.x, p.head_rows, p.tokens, p.clusters, p.perm, p.offsets, cur, nxt, nullptr, p.norms,
                    it + 1 < iters ? p.image : nullptr};
@@ -1053,7 +1064,7 @@ extern "C" int peco_assign_tokens_to_centers(const float* x, const float* center
     AssignJobs jobs{};
     jobs.njobs = 1;
     jobs.bh = batch;
-    jobs.job[0] = {tokens, clusters, tokens, x, centers, center_norms, img, labels, nullptr, nullptr};
+    jobs.job[0] = {tokens, clusters, tokens, x, nullptr, centers, center_norms, img, labels, nullptr, nullptr};
     const void* xh[2] = {hi, hi};
     const void* xl[2] = {lo, lo};
     const long long nrows[2] = {rows, rows};

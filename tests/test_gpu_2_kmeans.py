@@ -182,3 +182,28 @@ def test_headline_shape_subset():
         assert mism <= 1e-3, mism
         if mism == 0:
             assert torch.equal(cen.cpu(), rc)
+
+
+def test_full_headline_pair_reuses_tile_slots():
+    """All 24 HV-480 heads, Q and K in one fused fit (about 17 token tiles per
+    CTA, so every shared-memory slot and accumulator is reused many times, and
+    iterations after the first read the cached token norms); heads 0 and 23
+    are checked against the oracle."""
+    from peco_b200.clustering import kmeans_fit_pair
+    w = synthetic.workload("hv480")
+    q, k, _ = synthetic.make_inputs(w, seed=3)
+    nv, d, h, iters = w.video_tokens, w.dims, w.heads, 3
+    qv, kv = video(q, nv).contiguous(), video(k, nv).contiguous()
+    qi = synthetic.init_centroids(qv, w.q_clusters, w.init)
+    ki = synthetic.init_centroids(kv, w.k_clusters, w.init)
+    qd, kd = q.to(DEV).contiguous(), k.to(DEV).contiguous()
+    qb, kb = kmeans_fit_pair(qd, w.seq, nv, qi.to(DEV), kd, w.seq, nv, ki.to(DEV), h, d, iters)
+    for xv, init, b, c in ((qv, qi, qb, w.q_clusters), (kv, ki, kb, w.k_clusters)):
+        for head in (0, h - 1):
+            rl, rc, rn = O.fit_token_clusters(xv[head:head + 1], c, iters, init[head:head + 1])
+            got = b.labels[head:head + 1].cpu()
+            mism = (got != rl).float().mean().item()
+            assert mism <= 1e-3, mism
+            if mism == 0:
+                assert torch.equal(b.centers[head:head + 1].cpu(), rc)
+                assert torch.equal(b.counts[head:head + 1].cpu(), rn)
