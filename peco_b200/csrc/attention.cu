@@ -366,7 +366,9 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
                                                                   const AttnArgs args) {
   using L = Layout<D>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1 KB-aligned base, derived from smem_raw by pointer arithmetic so that
+  // the compiler keeps shared-memory (not generic) accesses through it
+  unsigned char* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   Shared& sh = *reinterpret_cast<Shared*>(base + L::kShared);
   volatile int* abort_flag = &sh.abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

@@ -46,11 +46,13 @@ namespace peco {
 namespace {
 
 constexpr int kTileM = 128;
-constexpr int kMaxCand = 8;
+constexpr int kMaxCand = 4;
 // warp 0: TMA / bulk-copy producer (and the centroid norms of each head);
 // warp 1: MMA issuer and TMEM owner; warps 2-9: epilogue, two warps per TMEM
-// lane quarter, each scanning half of the centroid columns
+// lane quarter, each scanning half of the centroid columns (measured: three
+// or four warps per quarter gain nothing, and four spill registers)
 constexpr int kEpiWarps = 8;
+constexpr int kParts = kEpiWarps / 4;  // column parts per row
 constexpr int kMmaWarp = 1, kEpiWarp0 = 2;
 constexpr int kAssignThreads = 32 * (kEpiWarp0 + kEpiWarps);
 // Near-tie tolerance of the tensor-core distance d' = |c|^2 - 2 x.(c_hi + c_lo)
@@ -191,8 +193,8 @@ struct __align__(8) AssignBars {
   uint64_t a_full[2], a_empty[2];
   uint64_t b_full[2], b_empty[2];
   uint64_t acc_full[2], acc_empty[2];
-  uint64_t xch_full[2];        // half 1 -> half 0 hand-off, per accumulator slot
-  float4 xch[2][kTileM];       // (best, runner-up, index bits, partial |x|^2)
+  uint64_t xch_full[2];        // parts 1.. -> part 0 hand-off, per accumulator slot
+  float4 xch[2][kParts - 1][kTileM];  // (best, runner-up, index bits, partial |x|^2)
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -269,7 +271,9 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
   const bool epi_reads_a = jobs.job[0].xn_in == nullptr || (jobs.njobs > 1 && jobs.job[1].xn_in == nullptr);
 
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1 KB-aligned base, derived from smem_raw by pointer arithmetic so that
+  // the compiler keeps shared-memory (not generic) accesses through it
+  unsigned char* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   float* cn = reinterpret_cast<float*>(base + S.cn_off);  // centroid norms of the current head (+inf past C)
   __shared__ AssignBars sb;
   volatile int* abort_flag = &sb.abort_flag;
@@ -288,7 +292,7 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
       mbar_init(&sb.b_empty[i], 1);
       mbar_init(&sb.acc_full[i], 1);
       mbar_init(&sb.acc_empty[i], kEpiWarps);
-      mbar_init(&sb.xch_full[i], kEpiWarps / 2);
+      mbar_init(&sb.xch_full[i], kEpiWarps - kEpiWarps / kParts);
     }
     sb.abort_flag = 0;
     fence_barrier_init();
@@ -437,7 +441,7 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
   } else {
     // ------------------------------------------------------------- epilogue
     const int quarter = warp & 3;
-    const int half = (warp - kEpiWarp0) >> 2;  // which half of the columns (and of x's dims)
+    const int part = (warp - kEpiWarp0) >> 2;  // which part of the columns (and of x's dims)
     const int r = quarter * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     bool ok = true;
@@ -466,17 +470,16 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
       if (epi_reads_a) ok = mbar_wait_warp(&sb.a_full[s], (i / NA) & 1, abort_flag, status);
       if (!ok) break;
       const unsigned char* a_hi = base + S.a_off + s * S.a_bytes;
-      // the token norm: cached by an earlier iteration, or this half's share
-      // of |x|^2 (dims [half D/2, (half + 1) D/2)), merged below
+      // the token norm: cached by an earlier iteration, or this part's share
+      // of |x|^2 (dims [part D/kParts, (part + 1) D/kParts)), merged below
       const int tok_r = it.tile * kTileM + r;
       const bool cached_xn = J.xn_in != nullptr;
       float xn_cached = 0.0f;
-      if (cached_xn && half == 0 && tok_r < J.tokens) xn_cached = J.xn_in[static_cast<long long>(it.head) * J.tokens + tok_r];
+      if (cached_xn && part == 0 && tok_r < J.tokens) xn_cached = J.xn_in[static_cast<long long>(it.head) * J.tokens + tok_r];
       float ss = 0.0f;
       if (!cached_xn)
-#pragma unroll
-      for (int h8 = 0; h8 < D / 16; ++h8) {
-        const int ch = half * (D / 16) + h8;
+#pragma unroll 1
+      for (int ch = part * (D / 8) / kParts; ch < (part + 1) * (D / 8) / kParts; ++ch) {
         const int off = (ch >> 3) * a_panel + r * 128 + (((ch & 7) ^ (r & 7)) << 4);
         const uint4 u = *reinterpret_cast<const uint4*>(a_hi + off);
         const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
@@ -499,7 +502,7 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
         __syncwarp();
         if (lane == 0) mbar_arrive(&sb.a_empty[s]);
       }
-      float E2 = 0.0f;  // half 0: bound once both norm halves are known
+      float E2 = 0.0f;  // part 0: bound once every part's share of |x|^2 is known
       float best = INFINITY;
       float cd[kMaxCand];
       int ci[kMaxCand];
@@ -542,16 +545,17 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
         const uint32_t acc = tmem + as * 256 + lane_off;
         const float* cnk = cn + k * cg.nc;
         const int nblk = cg.nc / 32 + ((cg.nc & 31) ? 1 : 0);
-        const int nb0 = (nblk + 1) >> 1;  // half 0 takes blocks [0, nb0), half 1 the rest
-        const int blo = half ? nb0 : 0, bhi = half ? nblk : nb0;
-        // One pass over this half's blocks: best distance d = |c|^2 - 2 x.c,
+        // part p takes blocks [nblk p / kParts, nblk (p + 1) / kParts)
+        const int blo = nblk * part / kParts, bhi = nblk * (part + 1) / kParts;
+        // One pass over this part's blocks: best distance d = |c|^2 - 2 x.c,
         // its index and the runner-up, in four independent chains (column
         // j mod 4); 64 columns per TMEM wait.  Block loops stay rolled: the
         // unrolled body must fit the instruction cache.
-        float b1[4], b2[4];
-        int bi[4];
+        constexpr int kChains = 8;  // independent compare chains (column j -> chain j % kChains)
+        float b1[kChains], b2[kChains];
+        int bi[kChains];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
+        for (int e = 0; e < kChains; ++e) {
           b1[e] = INFINITY;
           b2[e] = INFINITY;
           bi[e] = 0x7fffffff;
@@ -564,38 +568,33 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
             const float4 nq = c4[q];
             const float nv[4] = {nq.x, nq.y, nq.z, nq.w};
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float d = fmaf(-2.0f, __uint_as_float(v[4 * q + e]), nv[e]);
+            for (int e4 = 0; e4 < 4; ++e4) {
+              const int j = 4 * q + e4, e = j % kChains;
+              const float d = fmaf(-2.0f, __uint_as_float(v[j]), nv[e4]);
               const bool lt = d < b1[e];
               b2[e] = fminf(b2[e], fmaxf(d, b1[e]));
-              bi[e] = lt ? cbase + 4 * q + e : bi[e];
+              bi[e] = lt ? cbase + j : bi[e];
               b1[e] = fminf(b1[e], d);
             }
           }
         };
 #pragma unroll 1
-        for (int b = blo; b + 1 < bhi; b += 2) {
-          uint32_t v[64];
-          tmem_ld64_sync(acc + b * 32, v);
-          scan_block(v, b);
-          scan_block(v + 32, b + 1);
-        }
-        if ((bhi - blo) & 1) {
+        for (int b = blo; b < bhi; ++b) {
           uint32_t v[32];
-          tmem_ld32_sync(acc + (bhi - 1) * 32, v);
-          scan_block(v, bhi - 1);
+          tmem_ld32_sync(acc + b * 32, v);
+          scan_block(v, b);
         }
         float m1 = b1[0], m2 = b2[0];
         int i1 = bi[0];
 #pragma unroll
-        for (int e = 1; e < 4; ++e) {
+        for (int e = 1; e < kChains; ++e) {
           m2 = fminf(fminf(m2, b2[e]), fmaxf(m1, b1[e]));
           if (b1[e] < m1 || (b1[e] == m1 && bi[e] < i1)) i1 = bi[e];
           m1 = fminf(m1, b1[e]);
         }
-        if (half == 1) {
-          // hand this half's result to half 0 and move on
-          sb.xch[as][r] = make_float4(m1, m2, __int_as_float(i1), ss);
+        if (part > 0) {
+          // hand this part's result to part 0 and move on
+          sb.xch[as][part - 1][r] = make_float4(m1, m2, __int_as_float(i1), ss);
           tc_fence_before();
           __syncwarp();
           if (lane == 0) {
@@ -607,13 +606,18 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
         ok = mbar_wait_warp(&sb.xch_full[as], (gacc >> 1) & 1, abort_flag, status);
         if (!ok) break;
         {
-          const float4 o = sb.xch[as][r];
-          const int oi = __float_as_int(o.z);
-          m2 = fminf(fminf(m2, o.y), fmaxf(m1, o.x));
-          if (o.x < m1 || (o.x == m1 && oi < i1)) i1 = oi;
-          m1 = fminf(m1, o.x);
+          // parts in ascending column order, so an equal distance keeps the lower index
+#pragma unroll
+          for (int pp = 0; pp < kParts - 1; ++pp) {
+            const float4 o = sb.xch[as][pp][r];
+            const int oi = __float_as_int(o.z);
+            m2 = fminf(fminf(m2, o.y), fmaxf(m1, o.x));
+            if (o.x < m1 || (o.x == m1 && oi < i1)) i1 = oi;
+            m1 = fminf(m1, o.x);
+            ss += o.w;
+          }
           if (k == 0) {
-            const float xn = cached_xn ? xn_cached : sqrtf(ss + o.w);
+            const float xn = cached_xn ? xn_cached : sqrtf(ss);
             if (J.xn_out && tok_r < J.tokens) J.xn_out[static_cast<long long>(it.head) * J.tokens + tok_r] = xn;
             E2 = 2.0f * (kBoundScale * xn * cmax + kBoundTiny * (cmax * cmax + 2.0f * xn * cmax));
           }
@@ -655,7 +659,7 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
         if (lane == 0) mbar_arrive(&sb.acc_empty[as]);
       }
       if (!ok) break;
-      if (half == 0) {
+      if (part == 0) {
         const int tok = it.tile * kTileM + r;
         const bool valid = tok < J.tokens;
         if (ncand > 1) prune(best + E2);
