@@ -53,6 +53,7 @@ constexpr int kMaxCand = 4;
 // or four warps per quarter gain nothing, and four spill registers)
 constexpr int kEpiWarps = 8;
 constexpr int kParts = kEpiWarps / 4;  // column parts per row
+constexpr int kMaxASlots = 4;          // token-tile ring depth when a CTA's centroid image leaves room
 constexpr int kMmaWarp = 1, kEpiWarp0 = 2;
 constexpr int kAssignThreads = 32 * (kEpiWarp0 + kEpiWarps);
 // Near-tie tolerance of the tensor-core distance d' = |c|^2 - 2 x.(c_hi + c_lo)
@@ -182,6 +183,11 @@ struct AssignJobs {
   long long items[2];   // (head, tile) items per problem
   long long cost[2];    // cost of one item (centroid columns)
   int ncta;
+  // split[j] > 0: each (problem j, head) group is cut into split[j] CTAs of
+  // consecutive tiles, so no CTA changes centroid sets mid-launch; 0: CTAs
+  // take equal-cost ranges of the flattened item list
+  int split[2];
+  int dyn_smem;  // dynamic shared memory of the launch (bytes)
 };
 
 struct AssignMaps {
@@ -190,7 +196,7 @@ struct AssignMaps {
 
 struct __align__(8) AssignBars {
   uint64_t g_full, g_free;
-  uint64_t a_full[2], a_empty[2];
+  uint64_t a_full[kMaxASlots], a_empty[kMaxASlots];
   uint64_t b_full[2], b_empty[2];
   uint64_t acc_full[2], acc_empty[2];
   uint64_t xch_full[2];        // parts 1.. -> part 0 hand-off, per accumulator slot
@@ -247,6 +253,39 @@ __device__ __forceinline__ Item decode_item(const AssignJobs& a, long long f) {
   it.tile = static_cast<int>(local % nt);
   return it;
 }
+// The items of a CTA are consecutive: decode the first once, then step
+// (tile, head, problem) without 64-bit divisions in the per-item loops.
+struct ItemCursor {
+  Item it;
+  int nt;  // tiles per head of the current problem
+  __device__ __forceinline__ void start(const AssignJobs& a, long long f) {
+    it = decode_item(a, f);
+    nt = (a.job[it.j].tokens + kTileM - 1) / kTileM;
+  }
+  __device__ __forceinline__ bool last_in_group() const { return it.tile + 1 == nt; }
+  __device__ __forceinline__ void next(const AssignJobs& a) {
+    if (++it.tile == nt) {
+      it.tile = 0;
+      if (++it.head == a.bh) {
+        it.head = 0;
+        ++it.j;
+        nt = (a.job[it.j & 1].tokens + kTileM - 1) / kTileM;
+      }
+    }
+  }
+};
+// position in a ring of n slots: slot s in its round's phase parity p
+struct Ring {
+  int s = 0, n = 1;
+  uint32_t p = 0;
+  __device__ __forceinline__ void next() {
+    if (++s == n) {
+      s = 0;
+      p ^= 1u;
+    }
+  }
+};
+
 // first item whose cumulative cost reaches x
 __device__ __forceinline__ long long item_at(const AssignJobs& a, long long x) {
   const long long c0 = a.items[0] * a.cost[0];
@@ -259,9 +298,21 @@ __device__ __forceinline__ long long item_at(const AssignJobs& a, long long x) {
 template <int D, bool SPLIT>
 __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const __grid_constant__ AssignMaps maps,
                                                                         const AssignJobs jobs, unsigned* status) {
-  const long long total_cost = jobs.items[0] * jobs.cost[0] + (jobs.njobs > 1 ? jobs.items[1] * jobs.cost[1] : 0);
-  const long long f_begin = item_at(jobs, total_cost * blockIdx.x / jobs.ncta);
-  const long long f_end = item_at(jobs, total_cost * (blockIdx.x + 1) / jobs.ncta);
+  long long f_begin, f_end;
+  if (jobs.split[0] > 0) {
+    const int b = static_cast<int>(blockIdx.x);
+    const int j = b < jobs.bh * jobs.split[0] ? 0 : 1;
+    const int local = j ? b - jobs.bh * jobs.split[0] : b;
+    const int head = local / jobs.split[j], piece = local % jobs.split[j];
+    const long long nt = (jobs.job[j].tokens + kTileM - 1) / kTileM;
+    const long long first = (j ? jobs.items[0] : 0) + head * nt;
+    f_begin = first + nt * piece / jobs.split[j];
+    f_end = first + nt * (piece + 1) / jobs.split[j];
+  } else {
+    const long long total_cost = jobs.items[0] * jobs.cost[0] + (jobs.njobs > 1 ? jobs.items[1] * jobs.cost[1] : 0);
+    f_begin = item_at(jobs, total_cost * blockIdx.x / jobs.ncta);
+    f_end = item_at(jobs, total_cost * (blockIdx.x + 1) / jobs.ncta);
+  }
   if (f_begin >= f_end) return;
   const AssignSmem S = assign_smem(jobs.job[0].clusters, jobs.njobs > 1 ? jobs.job[1].clusters : 1, jobs.njobs, D, SPLIT);
   // The token tile in shared memory is read by the MMA, and by the epilogue
@@ -274,20 +325,36 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
   // 1 KB-aligned base, derived from smem_raw by pointer arithmetic so that
   // the compiler keeps shared-memory (not generic) accesses through it
   unsigned char* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  float* cn = reinterpret_cast<float*>(base + S.cn_off);  // centroid norms of the current head (+inf past C)
+  // Token-tile ring: a CTA that serves one resident group takes every slot its
+  // own image leaves free (up to kMaxASlots), the norms sit at the end.
+  int a_off = S.a_off, cn_off = S.cn_off, NA = S.naslots;
+  if (jobs.split[0] > 0 && S.resident) {
+    const Item first = decode_item(jobs, f_begin);
+    a_off = center_geom(jobs.job[first.j].clusters, D).b_bytes;
+    cn_off = (jobs.dyn_smem - 1024 - S.cn_cap * 4) & ~1023;
+    const int fit = (cn_off - a_off) / S.a_bytes;
+    NA = fit < kMaxASlots ? fit : kMaxASlots;
+    if (NA < S.naslots) {  // never fewer than the launch-wide layout
+      a_off = S.a_off;
+      cn_off = S.cn_off;
+      NA = S.naslots;
+    }
+  }
+  float* cn = reinterpret_cast<float*>(base + cn_off);  // centroid norms of the current head (+inf past C)
   __shared__ AssignBars sb;
   volatile int* abort_flag = &sb.abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int NA = S.naslots;
 
   if (threadIdx.x == 0) {
     mbar_init(&sb.g_full, 32);
     mbar_init(&sb.g_free, 1 + kEpiWarps);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < NA; ++i) {
       mbar_init(&sb.a_full[i], 1);
       // the tile's MMAs always release it; the epilogue warps too when they
       // read it for the token norms
       mbar_init(&sb.a_empty[i], 1 + (epi_reads_a ? kEpiWarps : 0));
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&sb.b_full[i], 1);
       mbar_init(&sb.b_empty[i], 1);
       mbar_init(&sb.acc_full[i], 1);
@@ -307,11 +374,8 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
   const int a_panel = kTileM * 128;  // bytes per 64-column panel of an A tile
   // group = (problem, head): the centroids in smem change with it
   auto group_of = [&](const Item& it) { return it.j * jobs.bh + it.head; };
-  auto last_of_group = [&](long long f, const Item& it) {
-    if (f + 1 >= f_end) return true;
-    const Item nx = decode_item(jobs, f + 1);
-    return group_of(nx) != group_of(it);
-  };
+  // the item is its group's last in this CTA (the next is another group, or none)
+  auto last_of_group = [&](long long f, const ItemCursor& cur) { return f + 1 >= f_end || cur.last_in_group(); };
 
   if (warp == 0) {
     // ------------------------------------------------ TMA / bulk producer
@@ -321,9 +385,13 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
     }
     bool ok = true;
     int group = -1, ngroups = 0, bchunk = 0;
-    long long i = 0;
-    for (long long f = f_begin; f < f_end && ok; ++f, ++i) {
-      const Item it = decode_item(jobs, f);
+    int i = 0;
+    ItemCursor cur;
+    cur.start(jobs, f_begin);
+    Ring ring;
+    ring.n = NA;
+    for (long long f = f_begin; f < f_end && ok; ++f, ++i, cur.next(jobs), ring.next()) {
+      const Item it = cur.it;
       const AssignJob& J = jobs.job[it.j];
       const CenterGeom cg = center_geom(J.clusters, D);
       const unsigned char* img = J.image + static_cast<long long>(it.head) * cg.nchunks * cg.b_bytes;
@@ -344,11 +412,11 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
         group = group_of(it);
         ++ngroups;
       }
-      const int s = static_cast<int>(i % NA);
-      if (i >= NA) ok = mbar_wait_warp(&sb.a_empty[s], ((i / NA) - 1) & 1, abort_flag, status);
+      const int s = ring.s;
+      if (i >= NA) ok = mbar_wait_warp(&sb.a_empty[s], ring.p ^ 1u, abort_flag, status);
       if (!ok) break;
       if (lane == 0) {
-        unsigned char* a = base + S.a_off + s * S.a_bytes;
+        unsigned char* a = base + a_off + s * S.a_bytes;
         mbar_arrive_expect_tx(&sb.a_full[s], S.a_bytes);
         const int row = static_cast<int>(static_cast<long long>(it.head) * J.head_rows + static_cast<long long>(it.tile) * kTileM);
 #pragma unroll
@@ -378,9 +446,13 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
     if (lane == 0) {
       bool ok = true;
       int group = -1, ngroups = 0, bchunk = 0, gacc = 0;
-      long long i = 0;
-      for (long long f = f_begin; f < f_end && ok; ++f, ++i) {
-        const Item it = decode_item(jobs, f);
+      int i = 0;
+      ItemCursor cur;
+      cur.start(jobs, f_begin);
+      Ring ring;
+      ring.n = NA;
+      for (long long f = f_begin; f < f_end && ok; ++f, ++i, cur.next(jobs), ring.next()) {
+        const Item it = cur.it;
         const CenterGeom cg = center_geom(jobs.job[it.j].clusters, D);
         const uint32_t idesc = instr_desc(128, cg.nc, 1, false, false);
         if (group_of(it) != group) {
@@ -388,10 +460,10 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
           group = group_of(it);
           ++ngroups;
         }
-        const int s = static_cast<int>(i % NA);
-        if (ok) ok = mbar_wait(&sb.a_full[s], (i / NA) & 1, abort_flag, status);
+        const int s = ring.s;
+        if (ok) ok = mbar_wait(&sb.a_full[s], ring.p, abort_flag, status);
         if (!ok) break;
-        const uint32_t a_hi = smem_u32(base + S.a_off + s * S.a_bytes);
+        const uint32_t a_hi = smem_u32(base + a_off + s * S.a_bytes);
         const uint32_t a_lo = a_hi + kTileM * D * 2;
         for (int k = 0; k < cg.nchunks && ok; ++k, ++gacc) {
           const int as = gacc & 1;
@@ -432,7 +504,7 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
           if (!S.resident) umma_commit(&sb.b_empty[bs]);
         }
         if (ok) umma_commit(&sb.a_empty[s]);
-        if (ok && last_of_group(f, it)) umma_commit(&sb.g_free);
+        if (ok && last_of_group(f, cur)) umma_commit(&sb.g_free);
       }
       // drain our MMAs before TMEM is released
       if (gacc > 0) mbar_wait(&sb.acc_full[(gacc - 1) & 1], ((gacc - 1) >> 1) & 1, abort_flag, status);
@@ -447,9 +519,13 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
     bool ok = true;
     int group = -1, ngroups = 0, gacc = 0;
     float cmax = 0.0f;
-    long long i = 0;
-    for (long long f = f_begin; f < f_end && ok; ++f, ++i) {
-      const Item it = decode_item(jobs, f);
+    int i = 0;
+    ItemCursor cur;
+    cur.start(jobs, f_begin);
+    Ring ring;
+    ring.n = NA;
+    for (long long f = f_begin; f < f_end && ok; ++f, ++i, cur.next(jobs), ring.next()) {
+      const Item it = cur.it;
       const AssignJob& J = jobs.job[it.j];
       const int C = J.clusters;
       const CenterGeom cg = center_geom(C, D);
@@ -462,14 +538,14 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
         group = group_of(it);
         ++ngroups;
       }
-      const int s = static_cast<int>(i % NA);
+      const int s = ring.s;
       // Only a launch whose epilogue reads the tile waits for it (and holds
       // the slot until it has): otherwise the MMA may already have released
       // the slot and the producer refilled it, so this phase parity would
       // name a later tile.  acc_full below orders everything else.
-      if (epi_reads_a) ok = mbar_wait_warp(&sb.a_full[s], (i / NA) & 1, abort_flag, status);
+      if (epi_reads_a) ok = mbar_wait_warp(&sb.a_full[s], ring.p, abort_flag, status);
       if (!ok) break;
-      const unsigned char* a_hi = base + S.a_off + s * S.a_bytes;
+      const unsigned char* a_hi = base + a_off + s * S.a_bytes;
       // the token norm: cached by an earlier iteration, or this part's share
       // of |x|^2 (dims [part D/kParts, (part + 1) D/kParts)), merged below
       const int tok_r = it.tile * kTileM + r;
@@ -735,7 +811,7 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
         if (valid) J.labels[static_cast<long long>(it.head) * J.tokens + tok] = label;
       }
       __syncwarp();
-      if (lane == 0 && last_of_group(f, it)) mbar_arrive(&sb.g_free);
+      if (lane == 0 && last_of_group(f, cur)) mbar_arrive(&sb.g_free);
     }
   }
   __syncwarp();
@@ -929,9 +1005,35 @@ int launch_assign_t(AssignJobs jobs, const void* const (&x_hi)[2], const void* c
     }
   }
   const long long items = jobs.items[0] + jobs.items[1];
-  jobs.ncta = static_cast<int>(items < sm_count() ? items : sm_count());
-  // one CTA per SM: its 512 TMEM columns are then always free
-  const int smem = S.smem > 116 * 1024 ? S.smem : 116 * 1024;
+  const int sms = sm_count();
+  jobs.ncta = static_cast<int>(items < sms ? items : sms);
+  jobs.split[0] = jobs.split[1] = 0;
+  if (static_cast<long long>(jobs.bh) * jobs.njobs <= sms) {
+    // CTAs per group in proportion to the group's cost, at most one CTA per SM
+    long long ctas = 0;
+    for (int j = 0; j < jobs.njobs; ++j) {
+      const long long nt = (jobs.job[j].tokens + kTileM - 1) / kTileM;
+      const long long share = nt * jobs.cost[j] * sms / total_cost;
+      jobs.split[j] = static_cast<int>(share < 1 ? 1 : (share > nt ? nt : share));
+      ctas += static_cast<long long>(jobs.bh) * jobs.split[j];
+    }
+    if (ctas <= sms) jobs.ncta = static_cast<int>(ctas);
+    else jobs.split[0] = jobs.split[1] = 0;
+  }
+  // one CTA per SM (its 512 TMEM columns are then always free); CTAs that
+  // serve one resident group use the room left for a deeper token-tile ring
+  int smem = S.smem > 116 * 1024 ? S.smem : 116 * 1024;
+  if (jobs.split[0] > 0 && S.resident) {
+    // the per-block opt-in limit less the kernel's static shared memory
+    cudaFuncAttributes fa;
+    int dev = 0, optin = 0;
+    if (cudaFuncGetAttributes(&fa, kmeans_assign_kernel<D, SPLIT>) == cudaSuccess && cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) == cudaSuccess) {
+      const int full = (optin - static_cast<int>(fa.sharedSizeBytes)) & ~1023;
+      smem = full > smem ? full : smem;
+    }
+  }
+  jobs.dyn_smem = smem;
   cudaError_t e = cudaFuncSetAttribute(kmeans_assign_kernel<D, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return static_cast<int>(e);
   kmeans_assign_kernel<D, SPLIT><<<jobs.ncta, kAssignThreads, smem, stream>>>(maps, jobs, device_status_ptr());
