@@ -57,6 +57,7 @@ constexpr int kSlots = 5;        // K/V ring: slot of K(t) = 2t mod 5, V(t) = 2t
 constexpr int kQBufs = 2;        // Q tiles: the next unit's loads while this one runs
 constexpr int kRing = 8;         // tile-info ring depth
 constexpr int kMaxGroups = 4;    // query groups per unit
+constexpr int kPlanParts = 4;    // planner CTAs per head
 constexpr int kSoftmaxWarps = 8;
 constexpr int kThreads = 32 * (2 + kSoftmaxWarps);
 constexpr uint32_t kTmemCols = 512;  // S0 | S1 | O_0 | O_1, 128 columns each
@@ -148,22 +149,30 @@ __device__ long long block_exclusive_scan(long long v, long long* tmp) {
 // Group extents are clamped the way the reference's work map clamps them
 // (sparse_attention.cu:25-31): start_g = min(S, sum_{g'<g} max(0, size_g')).
 // Units of later query groups come first, so the text groups (which attend to
-// every key) start early.  Dynamic smem: 2 (gk + 1) + 2 gq + max_units ints.
+// every key) start early.  kPlanParts CTAs share a head (grid (BH,
+// kPlanParts)): each recomputes the head's prefixes and unit list (cheap) and
+// takes its slice of the key-row map, the padding rows and the units' entry
+// lists; part 0 writes the per-head records.  Dynamic smem: 2 (gk + 1) + 2 gq
+// + 2 max_units ints, then (when ``map_in_smem``) the head's gq x gk map bytes,
+// staged once so the per-unit entry scans read shared rather than global
+// memory.
 __global__ void __launch_bounds__(1024) attn_plan_kernel(const uint8_t* __restrict__ map,
                                                          const int* __restrict__ q_sizes,
                                                          const int* __restrict__ k_sizes, int* __restrict__ ws,
                                                          const PlanGeom g, unsigned char* k_blocks,
-                                                         unsigned char* v_blocks, int block_bytes) {
+                                                         unsigned char* v_blocks, int block_bytes, int map_in_smem) {
   extern __shared__ int plan_sm[];
   int* skp = plan_sm;
   int* sgp = skp + g.gk + 1;
   int* gstart = sgp + g.gk + 1;
   int* gcount = gstart + g.gq;
-  int* ugroup = gcount + g.gq;
+  int* ugroup = gcount + g.gq;             // per unit: first group << 3 | groups
+  int* urows = ugroup + g.max_units;         // per unit: rows
+  uint8_t* smap = reinterpret_cast<uint8_t*>(urows + g.max_units);
   __shared__ long long tmp[32];
   __shared__ long long carry[2];
   __shared__ int n_units;
-  const int head = blockIdx.x;
+  const int head = blockIdx.x, part = blockIdx.y, parts = gridDim.y;
   const int tid = threadIdx.x, last = blockDim.x - 1;
   const int lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   int* w = ws + static_cast<long long>(head) * g.stride;
@@ -173,7 +182,7 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(const uint8_t* __restri
     carry[0] = carry[1] = 0;
     skp[0] = 0;
     sgp[0] = 0;
-    if (head == gridDim.x - 1) w[g.stride - 1] = 0;  // work counter
+    if (head == gridDim.x - 1 && part == 0) w[g.stride - 1] = 0;  // work counter
   }
   __syncthreads();
   // key clusters: clamped row prefix and block prefix
@@ -195,10 +204,11 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(const uint8_t* __restri
     }
     __syncthreads();
   }
-  for (int c = tid; c <= g.gk; c += blockDim.x) {
-    w[g.off_kp + c] = skp[c];
-    w[g.off_gp + c] = sgp[c];
-  }
+  if (part == 0)
+    for (int c = tid; c <= g.gk; c += blockDim.x) {
+      w[g.off_kp + c] = skp[c];
+      w[g.off_gp + c] = sgp[c];
+    }
   // query groups -> units
   if (tid == 0) carry[0] = 0;
   __syncthreads();
@@ -220,52 +230,76 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(const uint8_t* __restri
   // start early): consecutive whole groups are packed while the rows fit in
   // kBM and there are at most kMaxGroups of them (a run of groups [lo, lo +
   // ng), empty ones included); a group larger than kBM rows gets units alone.
+  // One thread decides the units (shared memory only); all threads then write
+  // the records.
   if (tid == 0) {
     int nu = 0, cur_lo = 0, cur_rows = 0, cur_ng = 0;
-    auto emit = [&](int q_start, int q_count, int lo, int ng, unsigned bounds) {
-      if (nu < g.max_units) {
-        int* rec = units + kUnitInts * nu;
-        rec[0] = q_start;
-        rec[1] = q_count;
-        rec[4] = lo;
-        rec[5] = ng;
-        rec[6] = static_cast<int>(bounds);
-        rec[7] = 0;
-        ugroup[nu] = (lo << 3) | ng;
-      }
-      ++nu;
-    };
-    auto close = [&]() {
-      if (cur_ng == 0) return;
-      unsigned bounds = 0xffffffu;
-      for (int m = 1; m < cur_ng; ++m) {
-        const unsigned off = static_cast<unsigned>(gstart[cur_lo + m] - gstart[cur_lo]);
-        bounds = (bounds & ~(0xffu << (8 * (m - 1)))) | (off << (8 * (m - 1)));
-      }
-      emit(gstart[cur_lo], cur_rows, cur_lo, cur_ng, bounds);
-      cur_rows = cur_ng = 0;
-    };
+    const int cap = static_cast<int>(g.max_units);
     for (int q = g.gq - 1; q >= 0; --q) {
       const int n = gcount[q];
       if (n > kBM) {
-        close();
-        for (int i = 0; i * kBM < n; ++i) emit(gstart[q] + i * kBM, min(kBM, n - i * kBM), q, 1, 0xffffffu);
+        if (cur_ng > 0) {
+          if (nu < cap) {
+            ugroup[nu] = (cur_lo << 3) | cur_ng;
+            urows[nu] = cur_rows;
+          }
+          ++nu;
+          cur_rows = cur_ng = 0;
+        }
+        for (int i = 0; i * kBM < n; ++i, ++nu)
+          if (nu < cap) {
+            ugroup[nu] = (q << 3) | 1;
+            urows[nu] = -1 - i;  // piece i of a large group
+          }
         continue;
       }
-      if (cur_ng == kMaxGroups || cur_rows + n > kBM) close();
+      if (cur_ng == kMaxGroups || cur_rows + n > kBM) {
+        if (nu < cap) {
+          ugroup[nu] = (cur_lo << 3) | cur_ng;
+          urows[nu] = cur_rows;
+        }
+        ++nu;
+        cur_rows = cur_ng = 0;
+      }
       if (n == 0 && cur_ng == 0) continue;  // a unit never starts with an empty group
       cur_lo = q;  // groups are visited in descending order
       cur_rows += n;
       ++cur_ng;
     }
-    close();
-    n_units = min(nu, static_cast<int>(g.max_units));
-    w[0] = n_units;
+    if (cur_ng > 0) {
+      if (nu < cap) {
+        ugroup[nu] = (cur_lo << 3) | cur_ng;
+        urows[nu] = cur_rows;
+      }
+      ++nu;
+    }
+    n_units = min(nu, cap);
+    if (part == 0) w[0] = n_units;
   }
   __syncthreads();
+  if (part == 0)
+    for (int u = tid; u < n_units; u += blockDim.x) {
+      const int lo = ugroup[u] >> 3, ng = ugroup[u] & 7;
+      int* rec = units + kUnitInts * u;
+      if (urows[u] < 0) {  // piece of a large group
+        const int i = -1 - urows[u];
+        rec[0] = gstart[lo] + i * kBM;
+        rec[1] = min(kBM, gcount[lo] - i * kBM);
+      } else {
+        rec[0] = gstart[lo];
+        rec[1] = urows[u];
+      }
+      unsigned bounds = 0xffffffu;  // bytes 0-2: first row of groups 1-3 within the unit
+      for (int m = 1; m < ng; ++m)
+        bounds = (bounds & ~(0xffu << (8 * (m - 1)))) | (static_cast<unsigned>(gstart[lo + m] - gstart[lo]) << (8 * (m - 1)));
+      rec[4] = lo;
+      rec[5] = ng;
+      rec[6] = static_cast<int>(bounds);
+      rec[7] = 0;
+    }
   // key row -> row of the key-block image
   int* rows = w + g.off_rows;
-  for (int j = tid; j < g.sk; j += blockDim.x) {
+  for (int j = part * blockDim.x + tid; j < g.sk; j += parts * blockDim.x) {
     int lo = 0, hi = g.gk;  // largest c in [0, gk] with skp[c] <= j
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;
@@ -274,31 +308,44 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(const uint8_t* __restri
     }
     rows[j] = lo < g.gk ? kKeyBlockRows * sgp[lo] + (j - skp[lo]) : -1;
   }
-  // zero the padding rows of every cluster's last block
+  // zero the padding rows of every cluster's last block: eight lanes per
+  // 128-byte row, so each warp store writes whole rows
   if (k_blocks) {
     const int panels = block_bytes / 1024;
-    for (int idx = tid; idx < g.gk * kKeyBlockRows; idx += blockDim.x) {
-      const int c = idx / kKeyBlockRows, i = idx % kKeyBlockRows;
+    const int e = tid & 7;
+    const long long n = static_cast<long long>(g.gk) * kKeyBlockRows * panels;
+    for (long long idx = (part * blockDim.x + tid) >> 3; idx < n; idx += (parts * blockDim.x) >> 3) {
+      const int p = static_cast<int>(idx % panels);
+      const int ci = static_cast<int>(idx / panels);
+      const int c = ci / kKeyBlockRows, i = ci % kKeyBlockRows;
       const int r = (skp[c + 1] - skp[c]) % kKeyBlockRows;
       if (r == 0 || i < r) continue;
-      const long long off = (static_cast<long long>(head) * g.blocks + sgp[c + 1] - 1) * block_bytes + i * 128;
-      for (int p = 0; p < panels; ++p) {
-        uint4* kd = reinterpret_cast<uint4*>(k_blocks + off + p * 1024);
-        uint4* vd = reinterpret_cast<uint4*>(v_blocks + off + p * 1024);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          kd[e] = make_uint4(0, 0, 0, 0);
-          vd[e] = make_uint4(0, 0, 0, 0);
-        }
-      }
+      const long long off = (static_cast<long long>(head) * g.blocks + sgp[c + 1] - 1) * block_bytes + p * 1024 + i * 128;
+      reinterpret_cast<uint4*>(k_blocks + off)[e] = make_uint4(0, 0, 0, 0);
+      reinterpret_cast<uint4*>(v_blocks + off)[e] = make_uint4(0, 0, 0, 0);
     }
   }
   __syncthreads();
+  const uint8_t* head_map = map + static_cast<long long>(head) * g.gq * g.gk;
+  if (map_in_smem) {
+    // eight independent loads in flight per thread
+    const int n = g.gq * g.gk;
+    for (int i0 = tid; i0 < n; i0 += 8 * blockDim.x) {
+      uint8_t b[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) b[e] = i0 + e * blockDim.x < n ? head_map[i0 + e * blockDim.x] : 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (i0 + e * blockDim.x < n) smap[i0 + e * blockDim.x] = b[e];
+    }
+    __syncthreads();
+    head_map = smap;
+  }
   // per unit: the selected key clusters as entries over the unit's block list
   int2* ent_all = reinterpret_cast<int2*>(w + g.off_ent);
-  for (int u = warp; u < n_units; u += nwarps) {
+  for (int u = part * nwarps + warp; u < n_units; u += parts * nwarps) {
     const int lo = ugroup[u] >> 3, ng = ugroup[u] & 7;
-    const uint8_t* mrow = map + (static_cast<long long>(head) * g.gq + lo) * g.gk;
+    const uint8_t* mrow = head_map + static_cast<long long>(lo) * g.gk;
     int2* ent = ent_all + static_cast<long long>(u) * g.gk;
     int nent = 0, blocks = 0;
     for (int c0 = 0; c0 < g.gk; c0 += 32) {
@@ -444,10 +491,10 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
       // ---- claim a unit
       int got = 0;
       if (lane == 0) got = atomicAdd(work_counter(args), 1);
-      const long long v = __shfl_sync(0xffffffffu, got, 0);
+      const int v = __shfl_sync(0xffffffffu, got, 0);  // unit indices fit in int (checked at launch)
       if (v >= total_units || !ok) break;
-      const int head = static_cast<int>(v % args.bh);
-      const int local = static_cast<int>(v / args.bh);
+      const int head = v % args.bh;
+      const int local = v / args.bh;
       const int* w = args.ws + static_cast<long long>(head) * g.stride;
       if (local >= w[0] || local >= g.max_units) continue;
       const int4 rec = *reinterpret_cast<const int4*>(w + g.off_units + kUnitInts * local);
@@ -936,14 +983,17 @@ int launch_attention_plan(const uint8_t* map, const int* q_sizes, const int* k_s
   if ((reinterpret_cast<uintptr_t>(ws) | reinterpret_cast<uintptr_t>(k_blocks) | reinterpret_cast<uintptr_t>(v_blocks)) & 15)
     return kErrInvalidValue;
   const PlanGeom g = plan_geom(sq, sk, gq, gk);
-  const size_t smem = sizeof(int) * (2 * static_cast<size_t>(gk + 1) + 2 * static_cast<size_t>(gq) + g.max_units);
+  size_t smem = sizeof(int) * (2 * static_cast<size_t>(gk + 1) + 2 * static_cast<size_t>(gq) + 2 * g.max_units);
   if (smem > 200 * 1024) return kErrUnsupported;
+  const size_t map_bytes = static_cast<size_t>(gq) * gk;
+  const int map_in_smem = smem + map_bytes <= 160 * 1024 ? 1 : 0;
+  if (map_in_smem) smem += map_bytes;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(attn_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return static_cast<int>(e);
   }
-  attn_plan_kernel<<<bh, 1024, smem, stream>>>(map, q_sizes, k_sizes, ws, g, static_cast<unsigned char*>(k_blocks),
-                                               static_cast<unsigned char*>(v_blocks), kKeyBlockRows * d * 2);
+  attn_plan_kernel<<<dim3(bh, kPlanParts), 1024, smem, stream>>>(map, q_sizes, k_sizes, ws, g, static_cast<unsigned char*>(k_blocks),
+                                               static_cast<unsigned char*>(v_blocks), kKeyBlockRows * d * 2, map_in_smem);
   return launch_status();
 }
 

@@ -399,11 +399,12 @@ struct GatherJobs {
 };
 
 template <int D>
-__global__ void __launch_bounds__(256) quant_gather_kernel(GatherJobs jobs, int bh, int seq, int video, int bits,
+__global__ void __launch_bounds__(256, 4) quant_gather_kernel(GatherJobs jobs, int bh, int seq, int video, int bits,
                                                            unsigned* status) {
   constexpr int G = D / 8;  // lanes per row, 8 elements (16 bytes) each
   constexpr int R = 4;      // rows in flight per row group
-  const GatherJob& J = jobs.job[blockIdx.y];
+  // no dynamic index into the kernel parameters (it would copy them to local memory)
+  const GatherJob J = blockIdx.y == 0 ? jobs.job[0] : (blockIdx.y == 1 ? jobs.job[1] : jobs.job[2]);
   const bool to_blocks = jobs.plan && blockIdx.y > 0;
   const bool quant = J.labels && bits != 0;
   const float levels = static_cast<float>((1 << bits) - 1);
@@ -411,21 +412,41 @@ __global__ void __launch_bounds__(256) quant_gather_kernel(GatherJobs jobs, int 
   const int sub = threadIdx.x % G;
   const long long first = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) / G;
   const long long step = static_cast<long long>(gridDim.x) * blockDim.x / G;
+  // rows advance by ``step``: keep (head, token) of the current row and add
+  // step's own (head, token) split, so the loop never divides by seq
+  const int step_h = static_cast<int>(step / seq);  // heads fit in int (bh <= 65535)
+  const int step_j = static_cast<int>(step - static_cast<long long>(step_h) * seq);
+  int h0 = static_cast<int>(first / seq);
+  int j0 = static_cast<int>(first - static_cast<long long>(h0) * seq);
+  auto advance = [&](int& h, int& jj) {
+    h += step_h;
+    jj += step_j;
+    if (jj >= seq) {
+      jj -= seq;
+      ++h;
+    }
+  };
   for (long long r0 = first; r0 < rows; r0 += R * step) {
     // phase 1: destination row (key blocks for K/V) and source token of R rows
-    long long head[R];
-    int j[R], t[R], kr[R];
+    int head[R], j[R], t[R], kr[R];
     bool live[R];
+    int hu = h0;
+    int ju = j0;
 #pragma unroll
     for (int u = 0; u < R; ++u) {
       const long long row = r0 + u * step;
       live[u] = row < rows;
-      head[u] = live[u] ? row / seq : 0;
-      j[u] = live[u] ? static_cast<int>(row - head[u] * seq) : 0;
+      head[u] = live[u] ? hu : 0;
+      j[u] = live[u] ? ju : 0;
+      advance(hu, ju);  // row r0 + (u + 1) step
+      if (u == R - 1) {
+        h0 = hu;
+        j0 = ju;
+      }
       t[u] = j[u];
       kr[u] = j[u];
-      if (live[u] && j[u] < video) t[u] = J.perm[head[u] * video + j[u]];
-      if (live[u] && to_blocks) kr[u] = jobs.plan[head[u] * jobs.plan_stride + jobs.off_rows + j[u]];
+      if (live[u] && j[u] < video) t[u] = J.perm[static_cast<long long>(head[u]) * video + j[u]];
+      if (live[u] && to_blocks) kr[u] = jobs.plan[static_cast<long long>(head[u]) * jobs.plan_stride + jobs.off_rows + j[u]];
     }
     // phase 2: source chunks and labels
     uint4 xr[R];
@@ -443,8 +464,8 @@ __global__ void __launch_bounds__(256) quant_gather_kernel(GatherJobs jobs, int 
       }
       if (live[u] && to_blocks && kr[u] < 0) live[u] = false;  // key row outside every key cluster: never attended
       if (live[u]) {
-        xr[u] = *reinterpret_cast<const uint4*>(J.src + (head[u] * seq + t[u]) * D + sub * 8);
-        if (quant && j[u] < video) lab[u] = J.labels[head[u] * video + t[u]];
+        xr[u] = *reinterpret_cast<const uint4*>(J.src + (static_cast<long long>(head[u]) * seq + t[u]) * D + sub * 8);
+        if (quant && j[u] < video) lab[u] = J.labels[static_cast<long long>(head[u]) * video + t[u]];
       }
     }
     // phase 3: centroid chunks, then quantise and store
@@ -454,10 +475,10 @@ __global__ void __launch_bounds__(256) quant_gather_kernel(GatherJobs jobs, int 
       __nv_bfloat16* dst;
       if (to_blocks) {
         dst = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<unsigned char*>(J.dst) +
-                                               (head[u] * jobs.blocks + kr[u] / kKeyBlockRows) * (kKeyBlockRows * D * 2) +
+                                               (static_cast<long long>(head[u]) * jobs.blocks + kr[u] / kKeyBlockRows) * (kKeyBlockRows * D * 2) +
                                                key_block_offset(kr[u] % kKeyBlockRows, sub * 8));
       } else {
-        dst = J.dst + (head[u] * seq + j[u]) * D + sub * 8;
+        dst = J.dst + (static_cast<long long>(head[u]) * seq + j[u]) * D + sub * 8;
       }
       if (!quant || j[u] >= video) {  // text rows and unquantised tensors: copy
         *reinterpret_cast<uint4*>(dst) = xr[u];
@@ -467,7 +488,7 @@ __global__ void __launch_bounds__(256) quant_gather_kernel(GatherJobs jobs, int 
         if (sub == 0) record_status(status, kDevBadIndex);
         continue;
       }
-      const float* cen = J.centroids + (head[u] * J.clusters + lab[u]) * D + sub * 8;
+      const float* cen = J.centroids + (static_cast<long long>(head[u]) * J.clusters + lab[u]) * D + sub * 8;
       float c[8], xv[8], xh[8], q[8];
       const float4 a = reinterpret_cast<const float4*>(cen)[0];
       const float4 b = reinterpret_cast<const float4*>(cen)[1];
