@@ -786,16 +786,19 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
         for (int j = 0; j < 32; ++j) s[c * 32 + j] = __uint_as_float(vv[j]);
       }
       // raw scores of masked keys become -inf; the row max runs in kChains
-      // independent chains (scale > 0, so it commutes with the max)
+      // independent chains over column pairs (three-input max), and the
+      // scale (> 0) commutes with it
       constexpr int kChains = 8;
       float mxc[kChains];
 #pragma unroll
       for (int i = 0; i < kChains; ++i) mxc[i] = -INFINITY;
 #pragma unroll
-      for (int j = 0; j < kCols; ++j) {
-        const bool valid = (mw[j >> 5] >> (j & 31)) & 1u;
-        s[j] = valid ? s[j] : -INFINITY;
-        mxc[j % kChains] = fmaxf(mxc[j % kChains], s[j]);
+      for (int j = 0; j < kCols; j += 2) {
+        const bool v0 = (mw[j >> 5] >> (j & 31)) & 1u;
+        const bool v1 = (mw[j >> 5] >> ((j + 1) & 31)) & 1u;
+        s[j] = v0 ? s[j] : -INFINITY;
+        s[j + 1] = v1 ? s[j + 1] : -INFINITY;
+        mxc[(j / 2) % kChains] = fmaxf(mxc[(j / 2) % kChains], fmaxf(s[j], s[j + 1]));
       }
 #pragma unroll
       for (int i = kChains / 2; i > 0; i >>= 1) {
@@ -829,26 +832,27 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
         }
       }
       if (grow) m = mx;
-      // p = 2^(s*c - m): one FFMA and one ex2 per score (masked: 2^-inf = 0)
+      // p = 2^(s*c - m): one paired FFMA per two scores and one ex2 per score
+      // (masked: 2^-inf = 0); the row sum runs in kChains / 2 paired chains
       const float neg_m = (m == -INFINITY) ? 0.0f : -m;
-      float sumc[kChains];
+      const float2 c2 = make_float2(args.scale_log2, args.scale_log2), nm2 = make_float2(neg_m, neg_m);
+      float2 sum2[kChains / 2];
 #pragma unroll
-      for (int i = 0; i < kChains; ++i) sumc[i] = 0.0f;
+      for (int i = 0; i < kChains / 2; ++i) sum2[i] = make_float2(0.0f, 0.0f);
       uint32_t packed[kCols / 2];
 #pragma unroll
       for (int j = 0; j < kCols; j += 2) {
-        const float p0 = exp2_approx(fmaf(s[j], args.scale_log2, neg_m));
-        const float p1 = exp2_approx(fmaf(s[j + 1], args.scale_log2, neg_m));
-        sumc[(j / 2) % kChains] += p0;
-        sumc[(j / 2 + kChains / 2) % kChains] += p1;
+        const float2 a2 = ffma2(make_float2(s[j], s[j + 1]), c2, nm2);
+        const float p0 = exp2_approx(a2.x), p1 = exp2_approx(a2.y);
+        sum2[(j / 2) % (kChains / 2)] = fadd2(sum2[(j / 2) % (kChains / 2)], make_float2(p0, p1));
         packed[j >> 1] = AB ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
       }
 #pragma unroll
-      for (int i = kChains / 2; i > 0; i >>= 1) {
+      for (int i = kChains / 4; i > 0; i >>= 1) {
 #pragma unroll
-        for (int k2 = 0; k2 < i; ++k2) sumc[k2] += sumc[k2 + i];
+        for (int k2 = 0; k2 < i; ++k2) sum2[k2] = fadd2(sum2[k2], sum2[k2 + i]);
       }
-      l += sumc[0];
+      l += sum2[0].x + sum2[0].y;
 #pragma unroll
       for (int c = 0; c < kCols / 32; ++c) {
         uint32_t part[16];

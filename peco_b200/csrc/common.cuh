@@ -150,6 +150,30 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, v
   return ok != 0;
 }
 
+// ---- packed fp32 pairs (sm_100 f32x2 arithmetic: two lanes of math per instruction)
+__device__ __forceinline__ unsigned long long f2_pack(float x, float y) {
+  unsigned long long u;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(u) : "f"(x), "f"(y));
+  return u;
+}
+__device__ __forceinline__ float2 f2_unpack(unsigned long long u) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(u));
+  return r;
+}
+// a * b + c, each lane rounded to nearest (as two fmaf)
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(f2_pack(a.x, a.y)), "l"(f2_pack(b.x, b.y)), "l"(f2_pack(c.x, c.y)));
+  return f2_unpack(d);
+}
+// a + b, each lane rounded to nearest
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  unsigned long long d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_pack(a.x, a.y)), "l"(f2_pack(b.x, b.y)));
+  return f2_unpack(d);
+}
+
 // ---- TMA (tensor maps are __grid_constant__ kernel parameters) --------------
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
