@@ -47,8 +47,10 @@ __global__ void __launch_bounds__(256) select_scores_kernel(const float* __restr
   const int g0 = blockIdx.y * kTile, c0 = blockIdx.x * kTile;
   const float* qh = qc + static_cast<long long>(head) * cq * D;
   const float* kh = kc + static_cast<long long>(head) * ck * D;
+  // consecutive threads take consecutive rows, so the transposed stores hit
+  // consecutive shared-memory words (no bank conflicts)
   for (int i = threadIdx.x; i < kTile * D / 4; i += blockDim.x) {
-    const int row = i / (D / 4), d4 = (i % (D / 4)) * 4;
+    const int row = i % kTile, d4 = (i / kTile) * 4;
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
     if (g0 + row < cq) a = *reinterpret_cast<const float4*>(qh + static_cast<long long>(g0 + row) * D + d4);
     if (c0 + row < ck) b = *reinterpret_cast<const float4*>(kh + static_cast<long long>(c0 + row) * D + d4);
@@ -195,6 +197,113 @@ __global__ void __launch_bounds__(kRowThreads) select_row_kernel(const float* __
   }
 }
 
+// The same row computation with one WARP per (query cluster, head) for up to
+// 256 key clusters: element i = r * 32 + lane lives in register r of a lane,
+// so the bitonic sort runs on shuffles (partner lanes) and register swaps
+// (partner registers) with no block barrier, and the running mass is NPL
+// warp scans.  Sums use a different order than the CTA kernel (per-lane
+// partials, then a butterfly), so p can differ from it in the last ulp.
+template <int NPL>  // keys per lane: np2 = 32 * NPL
+__global__ void __launch_bounds__(256) select_row_warp_kernel(const float* __restrict__ logits,
+                                                              const int32_t* __restrict__ q_sizes,
+                                                              const int32_t* __restrict__ k_sizes,
+                                                              uint8_t* __restrict__ map, int cq, int ck, float top_p,
+                                                              int minimum, int extend, int out_cols, int rows) {
+  const int wid = static_cast<int>((static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (wid >= rows) return;
+  const int head = wid / cq, g = wid - head * cq;
+  const float* row_in = logits + (static_cast<long long>(head) * cq + g) * ck;
+  const int32_t* ks = k_sizes + static_cast<long long>(head) * ck;
+  float e[NPL];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int r = 0; r < NPL; ++r) {
+    const int c = r * 32 + lane;
+    e[r] = c < ck ? row_in[c] : -INFINITY;
+    mx = fmaxf(mx, e[r]);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (!isfinite(mx)) mx = 0.0f;
+  float sum = 0.0f;
+#pragma unroll
+  for (int r = 0; r < NPL; ++r) {
+    const int c = r * 32 + lane;
+    e[r] = c < ck ? expf(e[r] - mx) : 0.0f;
+    sum += e[r];
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  sum = fmaxf(sum, FLT_MIN);
+  unsigned long long key[NPL];
+#pragma unroll
+  for (int r = 0; r < NPL; ++r) {
+    const int c = r * 32 + lane;
+    key[r] = c < ck ? sort_key(e[r] / sum, c) : ~0ull;
+  }
+  // bitonic sort, ascending keys (descending p, ascending index)
+#pragma unroll
+  for (int k = 2; k <= 32 * NPL; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j >= 32) {  // partner in this lane: register r ^ (j / 32)
+        const int jr = j >> 5;
+#pragma unroll
+        for (int r = 0; r < NPL; ++r) {
+          const int pr = r ^ jr;
+          if (pr > r) {
+            const int i = r * 32 + lane;
+            const bool up = (i & k) == 0;
+            const unsigned long long a = key[r], b = key[pr];
+            if ((a > b) == up) {
+              key[r] = b;
+              key[pr] = a;
+            }
+          }
+        }
+      } else {  // partner lane ^ j, same register
+#pragma unroll
+        for (int r = 0; r < NPL; ++r) {
+          const int i = r * 32 + lane;
+          const bool up = (i & k) == 0, lower = (lane & j) == 0;
+          const unsigned long long other = __shfl_xor_sync(0xffffffffu, key[r], j);
+          const unsigned long long lo = key[r] < other ? key[r] : other, hi = key[r] < other ? other : key[r];
+          key[r] = (lower == up) ? lo : hi;
+        }
+      }
+    }
+  }
+  // running mass over sorted positions i = r * 32 + lane, in double
+  const int qn = q_sizes[static_cast<long long>(head) * cq + g];
+  uint8_t* row = map + (static_cast<long long>(head) * (extend ? cq + 2 : cq) + g) * out_cols;
+  double carry = 0.0;
+#pragma unroll
+  for (int r = 0; r < NPL; ++r) {
+    const int i = r * 32 + lane;
+    const float p = i < ck ? __uint_as_float(~static_cast<unsigned>(key[r] >> 32)) : 0.0f;
+    double incl = static_cast<double>(p);
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    const double run = carry + incl;
+    carry += __shfl_sync(0xffffffffu, incl, 31);
+    if (i < ck) {
+      const int c = static_cast<int>(key[r] & 0xffffffffu);
+      const float before = __fsub_rn(static_cast<float>(run), p);
+      bool keep = (before < top_p) || (top_p >= 1.0f) || (i == 0) || (i < minimum);
+      keep = keep && ks[c] > 0 && qn > 0;
+      row[c] = keep ? 1 : 0;
+    }
+  }
+  if (extend && lane == 0) {
+    row[ck] = 1;      // every video query sees the valid text keys
+    row[ck + 1] = 0;  // ... never the padding keys
+  }
+}
+
 // Text rows of the extended map and the extended size vectors.
 __global__ void text_partition_kernel(uint8_t* __restrict__ map, const int32_t* __restrict__ q_sizes,
                                       const int32_t* __restrict__ k_sizes, int32_t* __restrict__ q_ext,
@@ -250,8 +359,20 @@ int launch_select(const float* qc, const float* kc, const int32_t* qs, const int
   }
   if (!rc) {
     const int out_cols = extend ? ck + 2 : ck;
-    select_row_kernel<<<dim3(cq, bh), kRowThreads, row_smem, stream>>>(logits, qs, ks, map, cq, ck, np2, top_p, minimum,
-                                                                       extend, out_cols);
+    const int rows = bh * cq;
+    const int wgrid = (rows + 7) / 8;  // 8 warps (rows) per block
+    if (np2 <= 32) {
+      select_row_warp_kernel<1><<<wgrid, 256, 0, stream>>>(logits, qs, ks, map, cq, ck, top_p, minimum, extend, out_cols, rows);
+    } else if (np2 == 64) {
+      select_row_warp_kernel<2><<<wgrid, 256, 0, stream>>>(logits, qs, ks, map, cq, ck, top_p, minimum, extend, out_cols, rows);
+    } else if (np2 == 128) {
+      select_row_warp_kernel<4><<<wgrid, 256, 0, stream>>>(logits, qs, ks, map, cq, ck, top_p, minimum, extend, out_cols, rows);
+    } else if (np2 == 256) {
+      select_row_warp_kernel<8><<<wgrid, 256, 0, stream>>>(logits, qs, ks, map, cq, ck, top_p, minimum, extend, out_cols, rows);
+    } else {
+      select_row_kernel<<<dim3(cq, bh), kRowThreads, row_smem, stream>>>(logits, qs, ks, map, cq, ck, np2, top_p,
+                                                                         minimum, extend, out_cols);
+    }
     rc = launch_status();
   }
   e = cudaFreeAsync(scratch, stream);
