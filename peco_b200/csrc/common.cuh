@@ -167,6 +167,14 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(f2_pack(a.x, a.y)), "l"(f2_pack(b.x, b.y)), "l"(f2_pack(c.x, c.y)));
   return f2_unpack(d);
 }
+// a * b, each lane rounded to nearest.  Note: a paired multiply whose result
+// feeds a paired add may be contracted into one fused multiply-add; where the
+// separate roundings matter, multiply with __fmul_rn instead.
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  unsigned long long d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_pack(a.x, a.y)), "l"(f2_pack(b.x, b.y)));
+  return f2_unpack(d);
+}
 // a + b, each lane rounded to nearest
 __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
   unsigned long long d;

@@ -226,13 +226,16 @@ struct RowQuant {
   // in: x[8], c[8] (fp32); out: xhat[8], code[8]; low/scale returned by ref.
   __device__ __forceinline__ static void run(const float (&x)[8], const float (&c)[8], float levels,
                                              float (&xhat)[8], float (&code)[8], float& low, float& scale) {
-    float r[8];
+    // Every step is the reference's own fp32 operation rounded to nearest,
+    // done two elements per instruction where sm_100 has a paired form
+    // (x - c as x + (-c) is the same IEEE result).
+    float2 r[4];
     float lo = INFINITY, hi = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      r[i] = __fsub_rn(x[i], c[i]);
-      lo = fminf(lo, r[i]);
-      hi = fmaxf(hi, r[i]);
+    for (int i = 0; i < 4; ++i) {
+      r[i] = fadd2(make_float2(x[2 * i], x[2 * i + 1]), make_float2(-c[2 * i], -c[2 * i + 1]));
+      lo = fminf(lo, fminf(r[i].x, r[i].y));
+      hi = fmaxf(hi, fmaxf(r[i].x, r[i].y));
     }
     const unsigned gmask = row_group_mask<G>();
 #pragma unroll
@@ -245,17 +248,39 @@ struct RowQuant {
     // The code is rint(RN((r - lo) / sc)).  (r - lo) * (1/sc) is within a
     // few ulp of that quotient (< 2^-19 absolute for quotients <= 255), so
     // its rint is the same unless it sits within 1e-4 of a half-integer; only
-    // then is the exact division evaluated.
+    // then is the exact division evaluated.  r - lo >= 0 and 1/sc > 0, so
+    // the code is never negative; the upper clamp is the reference's.
     const float inv = __frcp_rn(sc);
+    const float2 nlo = make_float2(-lo, -lo), inv2 = make_float2(inv, inv);
+    float2 num[4], q[4];
+    bool exact = false;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float num = __fsub_rn(r[i], lo);
-      const float qa = num * inv;
-      float q = rintf(qa);
-      if (fabsf(qa - q) > 0.4999f) q = rintf(__fdiv_rn(num, sc));
-      q = fminf(fmaxf(q, 0.0f), levels);
-      code[i] = q;
-      xhat[i] = __fadd_rn(c[i], __fadd_rn(lo, __fmul_rn(sc, q)));
+    for (int i = 0; i < 4; ++i) {
+      num[i] = fadd2(r[i], nlo);
+      const float2 qa = fmul2(num[i], inv2);
+      q[i] = make_float2(rintf(qa.x), rintf(qa.y));
+      exact |= fabsf(qa.x - q[i].x) > 0.4999f || fabsf(qa.y - q[i].y) > 0.4999f;
+    }
+    if (exact) {  // rare: settle near-half quotients with the exact division
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        q[i].x = rintf(__fdiv_rn(num[i].x, sc));
+        q[i].y = rintf(__fdiv_rn(num[i].y, sc));
+      }
+    }
+    const float2 lo2 = make_float2(lo, lo);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      q[i] = make_float2(fminf(q[i].x, levels), fminf(q[i].y, levels));
+      code[2 * i] = q[i].x;
+      code[2 * i + 1] = q[i].y;
+      // x_hat = c + (low + scale * code), three separately rounded steps; the
+      // product stays a scalar __fmul_rn, which is never fused into the add
+      // that follows (a paired multiply feeding a paired add can be)
+      const float2 prod = make_float2(__fmul_rn(sc, q[i].x), __fmul_rn(sc, q[i].y));
+      const float2 xh = fadd2(make_float2(c[2 * i], c[2 * i + 1]), fadd2(lo2, prod));
+      xhat[2 * i] = xh.x;
+      xhat[2 * i + 1] = xh.y;
     }
     low = lo;
     scale = sc;
