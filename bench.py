@@ -266,6 +266,113 @@ def run_ulysses(args, world, rank, local):
     }
 
 
+STEP_METRIC = "ms per denoising step of a HunyuanVideo-architecture transformer (60 blocks, PECO attention)"
+
+
+def run_step(args, world, rank, local):
+    """Config 5: one full denoising step (transformer forward) of a random-init
+    HunyuanVideo-architecture model at 544x960x61 frames (latent 16x17x68x120,
+    34680 video + 256 text tokens), PECO attention in every block (256 / 512
+    clusters, 5 iterations, top-32, 4-bit Base-Offset) through
+    peco_b200.model.install_attention.  Each rank runs its own step (replicas:
+    the step is not sharded).  Also times the same step with exact SDPA
+    attention in every block."""
+    import torch
+    from peco_b200 import _native
+    from peco_b200.hunyuan import HunyuanConfig, Pipe, build_transformer, use_dense_attention
+    from peco_b200.model import install_attention
+    from peco_b200.processor import InferenceContext, PecoConfig
+    dev = torch.device("cuda", local if world > 1 else 0)
+    # a step takes about a second: keep the default run short
+    args.steps, args.warmup = min(args.steps, 5), min(max(args.warmup, 1), 2)
+    hcfg = HunyuanConfig()
+    model = build_transformer(hcfg, device=dev, dtype=torch.bfloat16, seed=0)
+    pipe = Pipe(model)
+    top_k, ck = 32, 512
+    pcfg = PecoConfig(num_q_centroids=256, num_k_centroids=ck, top_p=1e-9, min_kc_ratio=top_k / ck, kmeans_iter_init=5,
+                      kmeans_iter_step=5, warmup_steps=0, base_offset_bits=4)
+    install_attention(pipe, pcfg)
+    g = torch.Generator(device="cpu").manual_seed(1000 + rank)
+    latent_h = torch.randn(1, 16, 17, 68, 120, generator=g).to(torch.bfloat16).pin_memory()
+    text_h = torch.randn(1, 256, hcfg.text_dim, generator=g).to(torch.bfloat16).pin_memory()
+    pooled_h = torch.randn(1, hcfg.pooled_dim, generator=g).to(torch.bfloat16).pin_memory()
+    mask = torch.ones(1, 256, dtype=torch.bool, device=dev)
+    t = torch.tensor([500.0], device=dev)
+    latent, text, pooled = (x.to(dev) for x in (latent_h, text_h, pooled_h))
+    out_h = torch.empty(latent_h.shape, dtype=torch.bfloat16).pin_memory()
+    lib = _native.load()
+
+    def step():
+        with torch.no_grad():
+            return model(latent, t, text, mask, pooled)
+
+    def time_steps(n, fn):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+        for a, b in evs:
+            a.record()
+            fn()
+            b.record()
+        torch.cuda.synchronize()
+        return statistics.mean(a.elapsed_time(b) for a, b in evs)
+
+    for _ in range(max(1, args.warmup)):
+        step()  # the first step initialises every layer's centroids
+    torch.cuda.synchronize()
+    barrier(world)
+    sampler = ClockSampler(_smi_id(dev))
+    sampler.start()
+    launches0 = lib.peco_launch_count()
+    ms = time_steps(args.steps, step)
+    launches = lib.peco_launch_count() - launches0
+    clocks = sampler.stop()
+    ms_max = allreduce(ms, world, "max")
+
+    def e2e_step():
+        latent.copy_(latent_h, non_blocking=True)
+        text.copy_(text_h, non_blocking=True)
+        pooled.copy_(pooled_h, non_blocking=True)
+        out_h.copy_(step(), non_blocking=True)
+
+    e2e = allreduce(time_steps(max(1, min(args.steps, 3)), e2e_step), world, "max")
+    status = _native.device_status(clear=True)
+    # the same step with exact attention in every block (torch SDPA)
+    use_dense_attention(model, InferenceContext(step=1, text_length=256, valid_text_length=256))
+    step()
+    torch.cuda.synchronize()
+    dense = allreduce(time_steps(max(1, min(args.steps, 3)), step), world, "max")
+    tokens = 17 * 34 * 60
+    return {
+        "metric": STEP_METRIC,
+        "value": round(ms_max / world, 3),
+        "unit": "ms",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_max, 3),
+        "higher_is_better": False,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: random-init weights ~N(0, 0.02), latent and text embeddings ~N(0, 1)",
+        "config": {
+            "workload": f"hv-step: HunyuanVideo architecture (20 dual + 40 single blocks, hidden 3072, 24 heads x 128, "
+                        f"MLP x4, RMSNorm Q/K, 3D RoPE), latent 16x17x68x120 -> {tokens} video + 256 text tokens; "
+                        "PECO CQ=256, CK=512, 5 Lloyd iterations, top-32, 4-bit Base-Offset in every block",
+            "parallelism": f"replicas: {world} rank(s), one full step each (the step is not sharded)",
+            "l2": "inputs and weights far larger than L2",
+        },
+        "dense_attention_ms_per_step": round(dense, 3),
+        "e2e": {"value": round(e2e / world, 3), "unit": "ms",
+                "h2d_bytes_per_step": (latent.numel() + text.numel() + pooled.numel()) * 2 * world,
+                "d2h_bytes_per_step": latent.numel() * 2 * world,
+                "api": "peco_b200.hunyuan.HunyuanVideoTransformer.forward with PECO installed by "
+                       "peco_b200.model.install_attention; pinned host latent/text in, denoised latent out"},
+        "gpu_launches": int(allreduce(launches, world, "sum")),
+        "clocks": clocks,
+        "device_status": status,
+    }
+
+
 def attention_flops(emap, qs, ks, d):
     """4*D * sum over (query row, allowed key) pairs, from the extended map and sizes."""
     import torch
@@ -608,6 +715,11 @@ def main():
             if rank == 0:
                 print(json.dumps(result), flush=True)
             return
+        if args.config == "hv-step":
+            result = run_step(args, world, rank, local)
+            if rank == 0:
+                print(json.dumps(result), flush=True)
+            return
         result, (inputs_w) = run_ours(args, world, rank, local)
         if rank == 0 and world == 1 and args.baselines == "all":
             q_c, k_c, v_c, w = inputs_w
@@ -631,6 +743,10 @@ def main():
 def main_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
+        return 0
+    if args.config == "hv-step":
+        print(json.dumps({"impl": "reference", "unavailable": "config 5 runs the reference inside the diffusers "
+                          "HunyuanVideo pipeline, and diffusers is not installed here"}), flush=True)
         return 0
     import torch
     from peco_b200 import synthetic

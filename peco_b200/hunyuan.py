@@ -1,0 +1,247 @@
+"""A random-init HunyuanVideo-architecture transformer in plain PyTorch.
+
+Stands in for the diffusers ``HunyuanVideoTransformer3DModel`` (absent here)
+so that one full denoising step runs with PECO
+attention installed through ``peco_b200.model.install_attention``, exactly
+the way peco/model.py attaches it to the diffusers model.  Only the
+architecture matters (weights are random, N(0, 0.02)):
+
+* patch embedding: Conv3d, kernel = stride = (1, 2, 2), 16 latent channels;
+* text: a linear projection of 4096-dim embeddings (the reference's token
+  refiner is folded into it), pooled text and timestep form the modulation
+  vector;
+* ``transformer_blocks``: dual-stream blocks (separate video/text weights,
+  joint attention, adaLN-zero modulation, GELU-tanh MLP);
+* ``single_transformer_blocks``: single-stream blocks (one projection to
+  Q/K/V and the MLP, parallel attention + MLP, one output projection);
+* RMSNorm on Q and K per head, 3D rotary embedding on the video tokens
+  (head dim split 16 / 56 / 56 over time / height / width);
+* adaLN output norm and un-patchify back to the latent shape.
+
+The attention modules expose the attributes the PECO processor reads
+(``heads``, ``to_q``/``to_k``/``to_v``, ``norm_q``/``norm_k``,
+``add_q_proj``... for the text stream, ``to_out``, ``to_add_out``) and call
+their processor as ``processor(attn, hidden_states, encoder_hidden_states,
+attention_mask, image_rotary_emb)`` (peco/processor.py:159-197).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .processor import InferenceContext, PecoAttention, PecoConfig
+
+
+@dataclass(frozen=True)
+class HunyuanConfig:
+    in_channels: int = 16
+    hidden: int = 3072
+    heads: int = 24
+    head_dim: int = 128
+    mlp_ratio: int = 4
+    dual_blocks: int = 20
+    single_blocks: int = 40
+    text_dim: int = 4096
+    pooled_dim: int = 768
+    patch: tuple = (1, 2, 2)
+    rope_axes: tuple = (16, 56, 56)
+    rope_theta: float = 256.0
+
+
+class RMSNorm(nn.Module):
+    def __init__(self, dim, eps=1e-6):
+        super().__init__()
+        self.eps = eps
+        self.weight = nn.Parameter(torch.ones(dim))
+
+    def forward(self, x):
+        xf = x.float()
+        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps) * self.weight.float()).to(x.dtype)
+
+
+def _ln(x):
+    return F.layer_norm(x, x.shape[-1:], eps=1e-6)
+
+
+class SDPAProcessor(PecoAttention):
+    """Exact joint attention with torch SDPA (the dense baseline): the PECO
+    processor's projections, norms and rotary embedding, with the attention
+    itself replaced by full softmax attention over [0, valid) and [valid, S)."""
+
+    def __init__(self, context: InferenceContext):
+        super().__init__(0, PecoConfig(), context)
+
+    def attention(self, query, key, value):
+        s = query.shape[2]
+        valid = s - self.context.text_length + self.context.valid_text_length
+        out = torch.empty_like(query)
+        for a, b in ((0, valid), (valid, s)):
+            if a < b:
+                out[:, :, a:b] = F.scaled_dot_product_attention(query[:, :, a:b], key[:, :, a:b], value[:, :, a:b])
+        return out
+
+
+class Attention(nn.Module):
+    """Projections and norms of one attention layer; the math is the processor's."""
+
+    def __init__(self, dim, heads, head_dim, joint_text: bool, pre_only: bool):
+        super().__init__()
+        inner = heads * head_dim
+        self.heads = heads
+        self.to_q, self.to_k, self.to_v = (nn.Linear(dim, inner) for _ in range(3))
+        self.norm_q, self.norm_k = RMSNorm(head_dim), RMSNorm(head_dim)
+        if joint_text:
+            self.add_q_proj, self.add_k_proj, self.add_v_proj = (nn.Linear(dim, inner) for _ in range(3))
+            self.norm_added_q, self.norm_added_k = RMSNorm(head_dim), RMSNorm(head_dim)
+            self.to_add_out = nn.Linear(inner, dim)
+        else:
+            self.add_q_proj = self.add_k_proj = self.add_v_proj = None
+            self.norm_added_q = self.norm_added_k = None
+            self.to_add_out = None
+        self.to_out = None if pre_only else nn.ModuleList([nn.Linear(inner, dim), nn.Identity()])
+        self.processor = None
+
+    def set_processor(self, processor):
+        self.processor = processor
+
+    def forward(self, hidden_states, encoder_hidden_states=None, attention_mask=None, image_rotary_emb=None):
+        return self.processor(self, hidden_states, encoder_hidden_states, attention_mask, image_rotary_emb)
+
+
+def _mlp(dim, ratio):
+    return nn.Sequential(nn.Linear(dim, dim * ratio), nn.GELU(approximate="tanh"), nn.Linear(dim * ratio, dim))
+
+
+class DualStreamBlock(nn.Module):
+    def __init__(self, cfg: HunyuanConfig):
+        super().__init__()
+        d = cfg.hidden
+        self.img_mod = nn.Linear(d, 6 * d)
+        self.txt_mod = nn.Linear(d, 6 * d)
+        self.attn = Attention(d, cfg.heads, cfg.head_dim, joint_text=True, pre_only=False)
+        self.ff = _mlp(d, cfg.mlp_ratio)
+        self.ff_context = _mlp(d, cfg.mlp_ratio)
+
+    def forward(self, img, txt, temb, rope):
+        e = F.silu(temb)
+        i_shift, i_scale, i_gate, i_shift2, i_scale2, i_gate2 = self.img_mod(e)[:, None].chunk(6, dim=-1)
+        t_shift, t_scale, t_gate, t_shift2, t_scale2, t_gate2 = self.txt_mod(e)[:, None].chunk(6, dim=-1)
+        a_img, a_txt = self.attn(_ln(img) * (1 + i_scale) + i_shift, _ln(txt) * (1 + t_scale) + t_shift, None, rope)
+        img = img + i_gate * a_img
+        txt = txt + t_gate * a_txt
+        img = img + i_gate2 * self.ff(_ln(img) * (1 + i_scale2) + i_shift2)
+        txt = txt + t_gate2 * self.ff_context(_ln(txt) * (1 + t_scale2) + t_shift2)
+        return img, txt
+
+
+class SingleStreamBlock(nn.Module):
+    def __init__(self, cfg: HunyuanConfig):
+        super().__init__()
+        d = cfg.hidden
+        self.mod = nn.Linear(d, 3 * d)
+        self.attn = Attention(d, cfg.heads, cfg.head_dim, joint_text=False, pre_only=True)
+        self.proj_mlp = nn.Linear(d, cfg.mlp_ratio * d)
+        self.proj_out = nn.Linear(d + cfg.mlp_ratio * d, d)
+
+    def forward(self, img, txt, temb, rope):
+        n_txt = txt.shape[1]
+        x = torch.cat((img, txt), 1)
+        shift, scale, gate = self.mod(F.silu(temb))[:, None].chunk(3, dim=-1)
+        h = _ln(x) * (1 + scale) + shift
+        mlp = F.gelu(self.proj_mlp(h), approximate="tanh")
+        a_img, a_txt = self.attn(h[:, :-n_txt], h[:, -n_txt:], None, rope)
+        x = x + gate * self.proj_out(torch.cat((torch.cat((a_img, a_txt), 1), mlp), -1))
+        return x[:, :-n_txt], x[:, -n_txt:]
+
+
+def _timestep_embedding(t, dim=256, max_period=10000.0):
+    half = dim // 2
+    freqs = torch.exp(-math.log(max_period) * torch.arange(half, dtype=torch.float32, device=t.device) / half)
+    args = t.float()[:, None] * freqs[None]
+    return torch.cat((torch.cos(args), torch.sin(args)), -1)
+
+
+def rope_3d(grid, axes, theta, device):
+    """(cos, sin) tables [T*H*W, sum(axes)] for a (T, H, W) token grid, pairs
+    interleaved (the real form diffusers' apply_rotary_emb takes)."""
+    tables = []
+    coords = torch.meshgrid(*(torch.arange(n, dtype=torch.float32) for n in grid), indexing="ij")
+    for dim, pos in zip(axes, coords):
+        inv = 1.0 / (theta ** (torch.arange(0, dim, 2, dtype=torch.float32) / dim))
+        ang = pos.reshape(-1, 1) * inv[None]
+        tables.append(ang.repeat_interleave(2, dim=-1))
+    ang = torch.cat(tables, -1)
+    return ang.cos().to(device), ang.sin().to(device)
+
+
+class HunyuanVideoTransformer(nn.Module):
+    def __init__(self, cfg: HunyuanConfig = HunyuanConfig()):
+        super().__init__()
+        self.cfg = cfg
+        d = cfg.hidden
+        self.x_embedder = nn.Conv3d(cfg.in_channels, d, kernel_size=cfg.patch, stride=cfg.patch)
+        self.context_embedder = nn.Linear(cfg.text_dim, d)
+        self.time_in = nn.Sequential(nn.Linear(256, d), nn.SiLU(), nn.Linear(d, d))
+        self.vector_in = nn.Sequential(nn.Linear(cfg.pooled_dim, d), nn.SiLU(), nn.Linear(d, d))
+        self.transformer_blocks = nn.ModuleList(DualStreamBlock(cfg) for _ in range(cfg.dual_blocks))
+        self.single_transformer_blocks = nn.ModuleList(SingleStreamBlock(cfg) for _ in range(cfg.single_blocks))
+        self.norm_out = nn.Linear(d, 2 * d)
+        self.proj_out = nn.Linear(d, cfg.in_channels * math.prod(cfg.patch))
+
+    @torch.no_grad()
+    def init_random(self, std=0.02, seed=0):
+        """Weights ~N(0, std) drawn on the parameters' device, biases 0, RMSNorm gains 1."""
+        dev = next(self.parameters()).device
+        g = torch.Generator(device=dev).manual_seed(seed)
+        for name, p in self.named_parameters():
+            if p.ndim > 1:
+                p.copy_(torch.randn(p.shape, generator=g, device=dev, dtype=torch.float32).mul_(std))
+            elif name.endswith("norm_q.weight") or name.endswith("norm_k.weight") or "norm_added" in name:
+                p.fill_(1.0)
+            else:
+                p.zero_()
+        return self
+
+
+    def forward(self, hidden_states, timestep, encoder_hidden_states, encoder_attention_mask, pooled_projections):
+        b, c, t, h, w = hidden_states.shape
+        pt, ph, pw = self.cfg.patch
+        grid = (t // pt, h // ph, w // pw)
+        img = self.x_embedder(hidden_states).flatten(2).transpose(1, 2)
+        txt = self.context_embedder(encoder_hidden_states)
+        temb = self.time_in(_timestep_embedding(timestep).to(img.dtype)) + self.vector_in(pooled_projections)
+        rope = rope_3d(grid, self.cfg.rope_axes, self.cfg.rope_theta, img.device)
+        for block in self.transformer_blocks:
+            img, txt = block(img, txt, temb, rope)
+        for block in self.single_transformer_blocks:
+            img, txt = block(img, txt, temb, rope)
+        scale, shift = self.norm_out(F.silu(temb))[:, None].chunk(2, dim=-1)
+        out = self.proj_out(_ln(img) * (1 + scale) + shift)
+        out = out.reshape(b, *grid, c, pt, ph, pw).permute(0, 4, 1, 5, 2, 6, 3, 7)
+        return out.reshape(b, c, t, h, w)
+
+
+def build_transformer(cfg: HunyuanConfig = HunyuanConfig(), device="cuda", dtype=torch.bfloat16, seed=0):
+    """Random-init model built straight on ``device`` (no default initialisation pass)."""
+    with torch.device("meta"):
+        model = HunyuanVideoTransformer(cfg)
+    model = model.to_empty(device=device).to(dtype)
+    return model.init_random(seed=seed).eval()
+
+
+class Pipe:
+    """The part of a diffusers pipeline ``install_attention`` uses."""
+
+    def __init__(self, transformer):
+        self.transformer = transformer
+
+
+def use_dense_attention(transformer, context: InferenceContext):
+    """Give every attention layer the exact SDPA processor (the dense baseline)."""
+    for block in [*transformer.transformer_blocks, *transformer.single_transformer_blocks]:
+        block.attn.set_processor(SDPAProcessor(context))
