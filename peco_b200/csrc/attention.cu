@@ -5,7 +5,7 @@
 // with no allowed key -> 0.
 //
 // Three kernels:
-//  * planner (one CTA per head): clamped cluster prefixes, the work units,
+//  * planner (several CTAs per head): clamped cluster prefixes, the work units,
 //    the key-row -> key-block map, zeroed padding rows of the key blocks, and
 //    per unit the list of selected key clusters as block ranges.  A unit is
 //    up to 128 consecutive query rows made of up to four whole consecutive
@@ -57,7 +57,7 @@ constexpr int kSlots = 5;        // K/V ring: slot of K(t) = 2t mod 5, V(t) = 2t
 constexpr int kQBufs = 2;        // Q tiles: the next unit's loads while this one runs
 constexpr int kRing = 8;         // tile-info ring depth
 constexpr int kMaxGroups = 4;    // query groups per unit
-constexpr int kPlanParts = 4;    // planner CTAs per head
+constexpr int kPlanParts = 4;    // planner CTAs per head (at least)
 constexpr int kSoftmaxWarps = 8;
 constexpr int kThreads = 32 * (2 + kSoftmaxWarps);
 constexpr uint32_t kTmemCols = 512;  // S0 | S1 | O_0 | O_1, 128 columns each
@@ -149,13 +149,13 @@ __device__ long long block_exclusive_scan(long long v, long long* tmp) {
 // Group extents are clamped the way the reference's work map clamps them
 // (sparse_attention.cu:25-31): start_g = min(S, sum_{g'<g} max(0, size_g')).
 // Units of later query groups come first, so the text groups (which attend to
-// every key) start early.  kPlanParts CTAs share a head (grid (BH,
-// kPlanParts)): each recomputes the head's prefixes and unit list (cheap) and
-// takes its slice of the key-row map, the padding rows and the units' entry
-// lists; part 0 writes the per-head records.  Dynamic smem: 2 (gk + 1) + 2 gq
-// + 2 max_units ints, then (when ``map_in_smem``) the head's gq x gk map bytes,
-// staged once so the per-unit entry scans read shared rather than global
-// memory.
+// every key) start early.  Several CTAs share a head (grid (BH, parts), at
+// least kPlanParts, more when there are few heads): each recomputes the
+// head's prefixes and unit list (cheap) and takes its slice of the key-row
+// map, the padding rows and the units' entry lists; part 0 writes the per-head
+// records.  Dynamic smem: 2 (gk + 1) + 2 gq + 2 max_units ints, then (when
+// ``map_in_smem``) the head's gq x gk map bytes, staged once so the per-unit
+// entry scans read shared rather than global memory.
 __global__ void __launch_bounds__(1024) attn_plan_kernel(const uint8_t* __restrict__ map,
                                                          const int* __restrict__ q_sizes,
                                                          const int* __restrict__ k_sizes, int* __restrict__ ws,
@@ -348,12 +348,29 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(const uint8_t* __restri
     const uint8_t* mrow = head_map + static_cast<long long>(lo) * g.gk;
     int2* ent = ent_all + static_cast<long long>(u) * g.gk;
     int nent = 0, blocks = 0;
+    // the map bytes of kMapBatch chunks of 32 clusters are loaded together,
+    // so one memory round trip serves kMapBatch * 32 clusters
+    constexpr int kMapBatch = 8;
+    int gms[kMapBatch];
     for (int c0 = 0; c0 < g.gk; c0 += 32) {
       const int c = c0 + lane;
-      int n = 0, nb = 0, gm = 0;
+      const int bi = (c0 / 32) % kMapBatch;
+      if (bi == 0) {
+#pragma unroll
+        for (int b = 0; b < kMapBatch; ++b) {
+          const int cb = c + 32 * b;
+          int v = 0;
+          if (cb < g.gk)
+            for (int m = 0; m < ng; ++m) v |= (mrow[static_cast<long long>(m) * g.gk + cb] ? 1 : 0) << m;
+          gms[b] = v;
+        }
+      }
+      int gm = 0;
+#pragma unroll
+      for (int b = 0; b < kMapBatch; ++b) gm = b == bi ? gms[b] : gm;
+      int n = 0, nb = 0;
       if (c < g.gk) {
         n = skp[c + 1] - skp[c];
-        for (int m = 0; m < ng; ++m) gm |= (mrow[static_cast<long long>(m) * g.gk + c] ? 1 : 0) << m;
         if (n > 0 && gm) nb = sgp[c + 1] - sgp[c];
       }
       const unsigned bal = __ballot_sync(0xffffffffu, nb > 0);
@@ -996,7 +1013,10 @@ int launch_attention_plan(const uint8_t* map, const int* q_sizes, const int* k_s
     cudaError_t e = cudaFuncSetAttribute(attn_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return static_cast<int>(e);
   }
-  attn_plan_kernel<<<dim3(bh, kPlanParts), 1024, smem, stream>>>(map, q_sizes, k_sizes, ws, g, static_cast<unsigned char*>(k_blocks),
+  // at least kPlanParts CTAs per head, more when there are few heads, so the
+  // per-unit map scans fill the GPU
+  const int parts = max(kPlanParts, min(64, num_sms() / bh));
+  attn_plan_kernel<<<dim3(bh, parts), 1024, smem, stream>>>(map, q_sizes, k_sizes, ws, g, static_cast<unsigned char*>(k_blocks),
                                                static_cast<unsigned char*>(v_blocks), kKeyBlockRows * d * 2, map_in_smem);
   return launch_status();
 }
