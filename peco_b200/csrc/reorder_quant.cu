@@ -109,7 +109,8 @@ __global__ void __launch_bounds__(kSortThreads) stable_sort_labels_kernel(const 
   const int plen = (tokens + parts - 1) / parts;
   // The first kSortCache batches of each partition are loaded once, all in
   // flight together, and kept in registers for both passes (the labels of a
-  // 6750-token head fit); longer partitions load the rest as they go.
+  // 6750-token head fit); longer partitions load the rest the same way, a
+  // round trip per kSortCache batches.
   constexpr int kSortCache = 8;
   int cached[kSortCache];
   const int p0 = warp * plen, p1 = min(tokens, p0 + plen);
@@ -132,11 +133,18 @@ __global__ void __launch_bounds__(kSortThreads) stable_sort_labels_kernel(const 
       if (l >= 0 && (peers & lt_mask) == 0) hist[warp * clusters + l] += __popc(peers);
       __syncwarp();
     }
-    for (int base = p0 + 32 * kSortCache; base < p1; base += 32) {
-      const int l = label_at(base + lane, true);
-      const unsigned peers = __match_any_sync(0xffffffffu, l);
-      if (l >= 0 && (peers & lt_mask) == 0) hist[warp * clusters + l] += __popc(peers);
-      __syncwarp();
+    // longer partitions: the rest kSortCache batches per round trip
+    for (int base = p0 + 32 * kSortCache; base < p1; base += 32 * kSortCache) {
+      int lb[kSortCache];
+#pragma unroll
+      for (int i = 0; i < kSortCache; ++i) lb[i] = label_at(base + 32 * i + lane, true);
+#pragma unroll
+      for (int i = 0; i < kSortCache; ++i) {
+        const int l = lb[i];
+        const unsigned peers = __match_any_sync(0xffffffffu, l);
+        if (l >= 0 && (peers & lt_mask) == 0) hist[warp * clusters + l] += __popc(peers);
+        __syncwarp();
+      }
     }
   }
   __syncthreads();
@@ -201,7 +209,13 @@ __global__ void __launch_bounds__(kSortThreads) stable_sort_labels_kernel(const 
     };
 #pragma unroll
     for (int i = 0; i < kSortCache; ++i) place(p0 + 32 * i + lane, cached[i]);
-    for (int base = p0 + 32 * kSortCache; base < p1; base += 32) place(base + lane, label_at(base + lane, false));
+    for (int base = p0 + 32 * kSortCache; base < p1; base += 32 * kSortCache) {
+      int lb[kSortCache];
+#pragma unroll
+      for (int i = 0; i < kSortCache; ++i) lb[i] = label_at(base + 32 * i + lane, false);
+#pragma unroll
+      for (int i = 0; i < kSortCache; ++i) place(base + 32 * i + lane, lb[i]);
+    }
   }
 }
 
