@@ -111,8 +111,9 @@ int peco_sort_labels(const int32_t* labels, int32_t* indices, int32_t* counts, i
  * row b*head_rows (so the video prefix of a [BH,S,D] tensor needs no copy).
  * Per problem: init [BH,C,D] fp32 (read), centers (final means of the last
  * partition, may alias init), work (BH * peco_kmeans_work_floats(C, D, N)
- * floats: ping-pong centres, the centres' bf16 tensor-core image and the
- * token norms the first iteration records for the rest), norms [BH,C],
+ * floats: ping-pong centres, the centres' bf16 tensor-core image, the
+ * token norms the first iteration records for the rest and, for long
+ * sequences, the label sort's per-segment scratch), norms [BH,C],
  * labels [BH,N], counts [BH,C], offsets [BH,C+1], perm [BH,N] (stable
  * argsort of the final labels).  Pass k_x = NULL for a single problem.
  * Replaces fit_token_clusters' CUDA loop, peco/clustering.py:59-88 with tol=0. */

@@ -60,6 +60,7 @@ class KmeansBuffers:
             raise ValueError("centers must be a contiguous fp32 [BH, C, D] tensor")
         self.centers = centers
         # ping-pong centres, the centres' bf16 tensor-core image, token norms
+        # and, for long sequences, the label sort's per-segment scratch
         self.work = torch.empty((bh, int(_native.load().peco_kmeans_work_floats(clusters, dims, tokens))),
                                 dtype=f32, device=device)
         self.norms = torch.empty((bh, clusters), dtype=f32, device=device)

@@ -23,6 +23,7 @@ struct KmeansProblem {
   int32_t* perm;          // [B, tokens] stable argsort of the last labels
   unsigned char* image;   // [B, image bytes per head] bf16 hi/lo image of the centres being assigned against
   float* xnorm;           // [B, tokens] token norms |x| (written by the first assignment, read by the rest)
+  int32_t* sort_seg;      // [B, sort_segments(tokens), C] sort scratch, or null (one CTA per head)
 };
 
 int kmeans_fit_bf16(int njobs, const KmeansProblem* probs, int bh, int dims, int iters, cudaStream_t stream);
@@ -38,7 +39,18 @@ struct SortJobInput {
   int32_t* indices;   // [rows, tokens]
   int32_t* counts;    // [rows, clusters] or null
   int32_t* offsets;   // [rows, clusters + 1] or null
+  int32_t* seg;       // optional [rows, segs, clusters] scratch: split each row over segs CTAs
+  int segs;
 };
+
+// CTAs per row for the label sort of a k-means fit (0: one CTA per row).  Long
+// rows are split so that few heads still fill the GPU; their scratch is
+// segs * clusters ints per row.
+inline int sort_segments(int tokens) {
+  if (tokens < 32768) return 0;
+  const int s = (tokens + 8191) / 8192;
+  return s < 16 ? s : 16;
+}
 int launch_stable_sort_jobs(const SortJobInput* jobs, int njobs, cudaStream_t stream);
 
 int launch_select(const float* qc, const float* kc, const int32_t* qs, const int32_t* ks, uint8_t* map, int bh,

@@ -1115,7 +1115,8 @@ int kmeans_fit_bf16(int njobs, const KmeansProblem* probs, int bh, int dims, int
     SortJobInput sj[2];
     for (int j = 0; j < njobs; ++j) {
       const KmeansProblem& p = probs[j];
-      sj[j] = {p.labels, p.tokens, bh, p.tokens, p.clusters, p.perm, p.counts, p.offsets};
+      sj[j] = {p.labels, p.tokens, bh, p.tokens, p.clusters, p.perm, p.counts, p.offsets, p.sort_seg,
+               sort_segments(p.tokens)};
     }
     rc = launch_stable_sort_jobs(sj, njobs, stream);
     if (rc) return rc;
@@ -1127,7 +1128,8 @@ int kmeans_fit_bf16(int njobs, const KmeansProblem* probs, int bh, int dims, int
 
 long long kmeans_work_floats(int clusters, int dims, int tokens) {
   if (clusters < 1 || tokens < 1 || (dims != 64 && dims != 128)) return -1;
-  return static_cast<long long>(clusters) * dims + image_bytes_per_head(clusters, dims) / 4 + tokens;
+  return static_cast<long long>(clusters) * dims + image_bytes_per_head(clusters, dims) / 4 + tokens +
+         static_cast<long long>(sort_segments(tokens)) * clusters;
 }
 
 }  // namespace peco
@@ -1268,7 +1270,8 @@ extern "C" int peco_kmeans_fit(const void* q_x, long long q_head_rows, int q_tok
                                float* k_norms, int32_t* k_counts, int32_t* k_offsets, int32_t* k_perm, int bh, int dims,
                                int iters, void* stream) {
   // work per problem: [bh, C, D] ping-pong centres, the bh centroid images,
-  // then the [bh, tokens] token norms
+  // the [bh, tokens] token norms, then (long rows) the label sort's
+  // [bh, segments, C] scratch
   auto image_of = [&](float* work, int clusters) {
     return work ? reinterpret_cast<unsigned char*>(work + static_cast<long long>(bh) * clusters * dims) : nullptr;
   };
@@ -1276,11 +1279,16 @@ extern "C" int peco_kmeans_fit(const void* q_x, long long q_head_rows, int q_tok
     if (!work || clusters < 1 || (dims != 64 && dims != 128)) return static_cast<float*>(nullptr);
     return work + static_cast<long long>(bh) * clusters * dims + static_cast<long long>(bh) * (image_bytes_per_head(clusters, dims) / 4);
   };
+  auto sort_seg_of = [&](float* work, int clusters, int tokens) {
+    float* xn = xnorm_of(work, clusters);
+    return xn && tokens > 0 && sort_segments(tokens) > 0 ? reinterpret_cast<int32_t*>(xn + static_cast<long long>(bh) * tokens)
+                                                         : static_cast<int32_t*>(nullptr);
+  };
   KmeansProblem p[2];
   p[0] = {q_x, q_head_rows, q_tokens, q_clusters, q_init, q_work, q_centers, q_norms, q_labels, q_counts, q_offsets, q_perm,
-          image_of(q_work, q_clusters), xnorm_of(q_work, q_clusters)};
+          image_of(q_work, q_clusters), xnorm_of(q_work, q_clusters), sort_seg_of(q_work, q_clusters, q_tokens)};
   p[1] = {k_x, k_head_rows, k_tokens, k_clusters, k_init, k_work, k_centers, k_norms, k_labels, k_counts, k_offsets, k_perm,
-          image_of(k_work, k_clusters), xnorm_of(k_work, k_clusters)};
+          image_of(k_work, k_clusters), xnorm_of(k_work, k_clusters), sort_seg_of(k_work, k_clusters, k_tokens)};
   const int njobs = k_x ? 2 : 1;
   return kmeans_fit_bf16(njobs, p, bh, dims, iters, static_cast<cudaStream_t>(stream));
 }

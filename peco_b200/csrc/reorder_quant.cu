@@ -80,14 +80,24 @@ struct SortJob {
   int32_t* indices;
   int32_t* counts;
   int32_t* offsets;
+  int segs;         // CTAs per row (1: the whole row in one CTA)
+  int32_t* seg;     // segs > 1: [rows][segs][clusters] per-segment counts, then bases
 };
 struct SortJobs {
   SortJob job[2];   // blockIdx.y selects the job (the Q and K sorts of one k-means iteration)
 };
 
-__global__ void __launch_bounds__(kSortThreads) stable_sort_labels_kernel(const SortJobs jobs, unsigned* status) {
+// mode 0: the whole sort of a row in one CTA.  For long rows the sort is
+// split over J.segs CTAs per row, each owning a contiguous token range, in
+// three launches: mode 1 writes each segment's label counts, the scan kernel
+// turns them into per-(segment, label) bases (and the counts and offsets),
+// mode 2 recounts per warp and places the segment's tokens.
+__global__ void __launch_bounds__(kSortThreads) stable_sort_labels_kernel(const SortJobs jobs, int mode,
+                                                                         unsigned* status) {
   const SortJob J = blockIdx.y ? jobs.job[1] : jobs.job[0];  // no dynamic index into the parameters
-  if (static_cast<int>(blockIdx.x) >= J.rows) return;
+  const int segs = mode ? J.segs : 1;
+  const int row = static_cast<int>(blockIdx.x) / segs, seg = static_cast<int>(blockIdx.x) % segs;
+  if (row >= J.rows) return;
   const int32_t* __restrict__ labels = J.labels;
   const long long label_stride = J.label_stride;
   const int tokens = J.tokens, clusters = J.clusters, parts = J.parts;
@@ -98,7 +108,6 @@ __global__ void __launch_bounds__(kSortThreads) stable_sort_labels_kernel(const 
   int32_t* hist = sm;                         // [parts][clusters]
   int32_t* colsum = sm + parts * clusters;    // [clusters]
   __shared__ int32_t warp_tot[32];
-  const int row = blockIdx.x;
   const int32_t* lab = labels + row * label_stride;
   int32_t* out_idx = indices + static_cast<long long>(row) * tokens;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -106,14 +115,17 @@ __global__ void __launch_bounds__(kSortThreads) stable_sort_labels_kernel(const 
 
   for (int i = threadIdx.x; i < parts * clusters; i += blockDim.x) hist[i] = 0;
   __syncthreads();
-  const int plen = (tokens + parts - 1) / parts;
+  // this CTA's tokens [r0, r1) (a multiple of 32 per segment), one partition per warp
+  const int span = segs > 1 ? (((tokens + segs - 1) / segs + 31) & ~31) : tokens;
+  const int r0 = min(tokens, seg * span), r1 = min(tokens, r0 + span);
+  const int plen = (r1 - r0 + parts - 1) / parts;
   // The first kSortCache batches of each partition are loaded once, all in
   // flight together, and kept in registers for both passes (the labels of a
   // 6750-token head fit); longer partitions load the rest the same way, a
   // round trip per kSortCache batches.
   constexpr int kSortCache = 8;
   int cached[kSortCache];
-  const int p0 = warp * plen, p1 = min(tokens, p0 + plen);
+  const int p0 = r0 + warp * plen, p1 = min(r1, p0 + plen);
   auto label_at = [&](int t, bool report) {
     int l = (t < p1) ? lab[t] : -1;
     if (l >= clusters || (t < p1 && l < 0)) {
@@ -155,45 +167,62 @@ __global__ void __launch_bounds__(kSortThreads) stable_sort_labels_kernel(const 
     colsum[c] = s;
   }
   __syncthreads();
-  // block-wide exclusive scan of colsum (chunked: each thread owns a contiguous run)
-  const int per = (clusters + blockDim.x - 1) / blockDim.x;
-  const int c0 = threadIdx.x * per, c1 = min(clusters, c0 + per);
-  int local = 0;
-  for (int c = c0; c < c1; ++c) local += colsum[c];
-  int incl = local;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int v = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += v;
+  int32_t* segrow = mode ? J.seg + (static_cast<long long>(row) * segs + seg) * clusters : nullptr;
+  if (mode == 1) {  // this segment's label counts
+    for (int c = threadIdx.x; c < clusters; c += blockDim.x) segrow[c] = colsum[c];
+    return;
   }
-  if (lane == 31) warp_tot[warp] = incl;
-  __syncthreads();
-  if (warp == 0) {
-    int v = warp_tot[lane];
-    int inc = v;
+  if (mode == 2) {  // bases from the scan: hist becomes per-partition base offsets
+    for (int c = threadIdx.x; c < clusters; c += blockDim.x) {
+      int b = segrow[c];
+      for (int p = 0; p < parts; ++p) {
+        const int h = hist[p * clusters + c];
+        hist[p * clusters + c] = b;
+        b += h;
+      }
+    }
+    __syncthreads();
+  } else {
+    // block-wide exclusive scan of colsum (chunked: each thread owns a contiguous run)
+    const int per = (clusters + blockDim.x - 1) / blockDim.x;
+    const int c0 = threadIdx.x * per, c1 = min(clusters, c0 + per);
+    int local = 0;
+    for (int c = c0; c < c1; ++c) local += colsum[c];
+    int incl = local;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const int u = __shfl_up_sync(0xffffffffu, inc, o);
-      if (lane >= o) inc += u;
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
     }
-    warp_tot[lane] = inc - v;  // exclusive warp offsets
-  }
-  __syncthreads();
-  int run = warp_tot[warp] + incl - local;  // exclusive prefix for c0
-  for (int c = c0; c < c1; ++c) {
-    const int n = colsum[c];
-    if (counts) counts[static_cast<long long>(row) * clusters + c] = n;
-    if (offsets) offsets[static_cast<long long>(row) * (clusters + 1) + c] = run;
-    int b = run;
-    for (int p = 0; p < parts; ++p) {  // hist becomes per-partition base offsets
-      const int h = hist[p * clusters + c];
-      hist[p * clusters + c] = b;
-      b += h;
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      int v = warp_tot[lane];
+      int inc = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += u;
+      }
+      warp_tot[lane] = inc - v;  // exclusive warp offsets
     }
-    run += n;
-  }
-  if (offsets && threadIdx.x == blockDim.x - 1) offsets[static_cast<long long>(row) * (clusters + 1) + clusters] = run;
-  __syncthreads();
+    __syncthreads();
+    int run = warp_tot[warp] + incl - local;  // exclusive prefix for c0
+    for (int c = c0; c < c1; ++c) {
+      const int n = colsum[c];
+      if (counts) counts[static_cast<long long>(row) * clusters + c] = n;
+      if (offsets) offsets[static_cast<long long>(row) * (clusters + 1) + c] = run;
+      int b = run;
+      for (int p = 0; p < parts; ++p) {  // hist becomes per-partition base offsets
+        const int h = hist[p * clusters + c];
+        hist[p * clusters + c] = b;
+        b += h;
+      }
+      run += n;
+    }
+    if (offsets && threadIdx.x == blockDim.x - 1) offsets[static_cast<long long>(row) * (clusters + 1) + clusters] = run;
+    __syncthreads();
+  }  // mode 0
   // phase 3: stable placement
   if (warp < parts) {
     auto place = [&](int t, int l) {
@@ -217,6 +246,64 @@ __global__ void __launch_bounds__(kSortThreads) stable_sort_labels_kernel(const 
       for (int i = 0; i < kSortCache; ++i) place(base + 32 * i + lane, lb[i]);
     }
   }
+}
+
+// Segmented sort, middle launch (one CTA per row): label totals over the
+// segments -> counts and offsets, and each (segment, label) count replaced by
+// its base position (label-major, then segment order, which keeps the sort
+// stable).
+__global__ void __launch_bounds__(kSortThreads) sort_segments_scan_kernel(const SortJobs jobs) {
+  const SortJob J = blockIdx.y ? jobs.job[1] : jobs.job[0];
+  const int row = blockIdx.x;
+  if (row >= J.rows) return;
+  const int clusters = J.clusters, segs = J.segs;
+  extern __shared__ int32_t tot[];  // [clusters]
+  __shared__ int32_t warp_tot[32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int32_t* sg = J.seg + static_cast<long long>(row) * segs * clusters;
+  for (int c = threadIdx.x; c < clusters; c += blockDim.x) {
+    int t = 0;
+    for (int g = 0; g < segs; ++g) t += sg[static_cast<long long>(g) * clusters + c];
+    tot[c] = t;
+  }
+  __syncthreads();
+  const int per = (clusters + blockDim.x - 1) / blockDim.x;
+  const int c0 = threadIdx.x * per, c1 = min(clusters, c0 + per);
+  int local = 0;
+  for (int c = c0; c < c1; ++c) local += tot[c];
+  int incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int v = warp_tot[lane];
+    int inc = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += u;
+    }
+    warp_tot[lane] = inc - v;  // exclusive warp offsets (the block has 32 warps)
+  }
+  __syncthreads();
+  int run = warp_tot[warp] + incl - local;
+  for (int c = c0; c < c1; ++c) {
+    if (J.counts) J.counts[static_cast<long long>(row) * clusters + c] = tot[c];
+    if (J.offsets) J.offsets[static_cast<long long>(row) * (clusters + 1) + c] = run;
+    int b = run;
+    for (int g = 0; g < segs; ++g) {
+      const long long i = static_cast<long long>(g) * clusters + c;
+      const int n = sg[i];
+      sg[i] = b;
+      b += n;
+    }
+    run += tot[c];
+  }
+  if (J.offsets && threadIdx.x == blockDim.x - 1) J.offsets[static_cast<long long>(row) * (clusters + 1) + clusters] = run;
 }
 
 // ---------------------------------------------------------------------------
@@ -557,7 +644,8 @@ int launch_stable_sort_jobs(const SortJobInput* in, int njobs, cudaStream_t stre
   if (njobs < 1 || njobs > 2) return kErrInvalidValue;
   SortJobs jobs{};
   size_t smem = 0;
-  int rows = 0;
+  int rows = 0, max_segs = 1, max_clusters = 1;
+  bool segmented = true;
   for (int j = 0; j < njobs; ++j) {
     const SortJobInput& a = in[j];
     if (a.rows < 1 || a.tokens < 1 || a.clusters < 1) return kErrInvalidValue;
@@ -567,14 +655,32 @@ int launch_stable_sort_jobs(const SortJobInput* in, int njobs, cudaStream_t stre
     if (need > 200 * 1024) return kErrUnsupported;
     smem = need > smem ? need : smem;
     rows = a.rows > rows ? a.rows : rows;
-    jobs.job[j] = {a.labels, a.label_stride, a.rows, a.tokens, a.clusters, parts, a.indices, a.counts, a.offsets};
+    jobs.job[j] = {a.labels, a.label_stride, a.rows, a.tokens, a.clusters, parts, a.indices, a.counts, a.offsets,
+                   a.seg && a.segs > 1 ? a.segs : 1, a.seg};
+    segmented = segmented && a.seg && a.segs > 1;
+    max_segs = a.segs > max_segs ? a.segs : max_segs;
+    max_clusters = a.clusters > max_clusters ? a.clusters : max_clusters;
   }
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(stable_sort_labels_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return static_cast<int>(e);
   }
-  stable_sort_labels_kernel<<<dim3(rows, njobs), kSortThreads, smem, stream>>>(jobs, device_status_ptr());
+  if (!segmented) {
+    stable_sort_labels_kernel<<<dim3(rows, njobs), kSortThreads, smem, stream>>>(jobs, 0, device_status_ptr());
+    return launch_status();
+  }
+  // long rows: segs CTAs per row (count, scan, place)
+  const size_t scan_smem = static_cast<size_t>(max_clusters) * sizeof(int32_t);
+  if (scan_smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(sort_segments_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(scan_smem));
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
+  const dim3 grid(static_cast<unsigned>(rows) * max_segs, njobs);
+  stable_sort_labels_kernel<<<grid, kSortThreads, smem, stream>>>(jobs, 1, device_status_ptr());
+  sort_segments_scan_kernel<<<dim3(rows, njobs), kSortThreads, scan_smem, stream>>>(jobs);
+  stable_sort_labels_kernel<<<grid, kSortThreads, smem, stream>>>(jobs, 2, device_status_ptr());
   return launch_status();
 }
 

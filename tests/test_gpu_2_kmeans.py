@@ -207,3 +207,35 @@ def test_full_headline_pair_reuses_tile_slots():
             if mism == 0:
                 assert torch.equal(b.centers[head:head + 1].cpu(), rc)
                 assert torch.equal(b.counts[head:head + 1].cpu(), rn)
+
+
+def test_long_sequence_fit_sorts_over_segments():
+    """A head of 36000 tokens is sorted by several CTAs (count, scan, place):
+    the permutation must still be the stable argsort of the final labels, the
+    counts and offsets must match it, and the fit must agree with the oracle
+    (the centre update sums each cluster in permutation order, so a wrong
+    order shows up as non-identical centres)."""
+    from peco_b200.clustering import kmeans_fit_pair
+    w = synthetic.workload("hv-long", heads=2, grid=(10, 45, 80), q_clusters=256, k_clusters=512)
+    q, k, _ = synthetic.make_inputs(w, seed=5)
+    nv, d, h, iters = w.video_tokens, w.dims, w.heads, 2
+    assert nv >= 32768  # the segmented sort's threshold
+    qv, kv = video(q, nv).contiguous(), video(k, nv).contiguous()
+    qi = synthetic.init_centroids(qv, w.q_clusters, w.init)
+    ki = synthetic.init_centroids(kv, w.k_clusters, w.init)
+    qb, kb = kmeans_fit_pair(q.to(DEV).contiguous(), w.seq, nv, qi.to(DEV), k.to(DEV).contiguous(), w.seq, nv,
+                             ki.to(DEV), h, d, iters)
+    for xv, init, b, c in ((qv, qi, qb, w.q_clusters), (kv, ki, kb, w.k_clusters)):
+        labels = b.labels.cpu()
+        assert torch.equal(b.perm.cpu(), torch.argsort(labels, dim=-1, stable=True).to(torch.int32))
+        counts = torch.stack([torch.bincount(labels[i].long(), minlength=c) for i in range(h)]).to(torch.int32)
+        assert torch.equal(b.counts.cpu(), counts)
+        offsets = torch.zeros((h, c + 1), dtype=torch.int32)
+        offsets[:, 1:] = torch.cumsum(counts, dim=-1)
+        assert torch.equal(b.offsets.cpu(), offsets)
+        for head in range(h):
+            rl, rc, rn = O.fit_token_clusters(xv[head:head + 1], c, iters, init[head:head + 1])
+            mism = (labels[head:head + 1] != rl).float().mean().item()
+            assert mism <= 1e-3, mism
+            if mism == 0:
+                assert torch.equal(b.centers[head:head + 1].cpu(), rc)
