@@ -31,6 +31,7 @@
 // their previous centre.  No atomics: the result is deterministic and, for
 // identical labels, bit-identical to the reference's CPU centroids.
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 #include "../../include/peco_b200.h"
@@ -837,6 +838,7 @@ struct UpdateJob {
   float* sums;              // optional [B, C, D]
   float* norms;             // optional [B, C]
   unsigned char* image;     // optional [B, nchunks * b_bytes]: bf16 hi/lo image of the means
+  int big_rows;             // > 0: clusters above this many rows are left to kmeans_update_big_kernel
 };
 struct UpdateJobs {
   UpdateJob job[2];
@@ -907,6 +909,7 @@ __global__ void __launch_bounds__(kUpdateThreads, 8) kmeans_update_kernel(const 
   float acc[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) acc[e] = 0.0f;
+  if (J.big_rows > 0 && end - start > J.big_rows) return;  // a large cluster: the block kernel sums it
   bool bad = start < 0 || end > J.tokens || start > end;
   if (bad) end = start;
   auto token_id = [&](int pos) {
@@ -959,6 +962,91 @@ __global__ void __launch_bounds__(kUpdateThreads, 8) kmeans_update_kernel(const 
   if (J.norms) {
     nsq = warp_sum(nsq);
     if (lane == 0) J.norms[static_cast<long long>(head) * J.clusters + c] = nsq;
+  }
+}
+
+// The clusters above J.big_rows rows (long sequences, bf16 tokens): one block
+// of D threads per cluster, thread e owning element e.  The whole block loads
+// kBigChunk rows per round trip into shared memory (the next chunk loads while
+// the current one is summed), then every thread adds its element over those
+// rows in token order -- the same sequence of fp32 additions, per element, as
+// the warp kernel, so the result is identical.  The norm is reduced in the
+// warp kernel's order (per lane its E elements, then the lanes by xor).
+constexpr int kBigChunk = 64;
+template <int D>
+__global__ void __launch_bounds__(D) kmeans_update_big_kernel(const UpdateJobs jobs, int bh, unsigned* status) {
+  using T = __nv_bfloat16;
+  constexpr int E = D / 32;                        // the warp kernel's elements per lane
+  constexpr int kRowVecs = D * 2 / 16;             // uint4 per row
+  constexpr int kPer = kBigChunk * kRowVecs / D;   // uint4 per thread per chunk
+  const UpdateJob J = blockIdx.y ? jobs.job[1] : jobs.job[0];  // no dynamic index into the parameters
+  const long long w = blockIdx.x;
+  if (J.big_rows <= 0 || w >= static_cast<long long>(bh) * J.clusters) return;
+  const int head = static_cast<int>(w / J.clusters);
+  const int c = static_cast<int>(w - static_cast<long long>(head) * J.clusters);
+  const int start = J.offsets[static_cast<long long>(head) * (J.clusters + 1) + c];
+  const int end = J.offsets[static_cast<long long>(head) * (J.clusters + 1) + c + 1];
+  if (end - start <= J.big_rows || start < 0 || end > J.tokens) return;
+  __shared__ __align__(16) T buf[kBigChunk * D];
+  __shared__ float part[32];
+  const int e = threadIdx.x;
+  const int32_t* perm = J.perm + static_cast<long long>(head) * J.tokens;
+  const T* xb = static_cast<const T*>(J.x) + static_cast<long long>(head) * J.head_rows * D;
+  bool bad = false;
+  uint4 nxt[kPer];
+  auto load_chunk = [&](int base) {
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int q = e + i * D, r = q / kRowVecs;
+      nxt[i] = make_uint4(0, 0, 0, 0);
+      if (base + r < end) {
+        int t = perm[base + r];
+        if (t < 0 || t >= J.tokens) {
+          bad = true;
+          t = 0;
+        }
+        nxt[i] = reinterpret_cast<const uint4*>(xb + static_cast<long long>(t) * D)[q % kRowVecs];
+      }
+    }
+  };
+  float acc = 0.0f;
+  load_chunk(start);
+  for (int base = start; base < end; base += kBigChunk) {
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) reinterpret_cast<uint4*>(buf)[e + i * D] = nxt[i];
+    __syncthreads();
+    if (base + kBigChunk < end) load_chunk(base + kBigChunk);  // in flight while this chunk is summed
+    const int rows = min(kBigChunk, end - base);
+    for (int r = 0; r < rows; ++r) acc = __fadd_rn(acc, to_f32<T>(buf[r * D + e]));
+    __syncthreads();
+  }
+  if (bad) record_status(status, kDevBadIndex);
+  const int n = end - start;
+  const long long o = (static_cast<long long>(head) * J.clusters + c) * D + e;
+  const float m = __fdiv_rn(acc, static_cast<float>(n));
+  J.means[o] = m;
+  if (J.sums) J.sums[o] = acc;
+  if (J.image) {
+    const CenterGeom g = center_geom(J.clusters, D);
+    const float mv[1] = {m};
+    write_image<1>(J.image + static_cast<long long>(head) * g.nchunks * g.b_bytes, g, c, e, mv);
+  }
+  if (J.norms) {
+    // lane l of the warp kernel held elements [l E, (l + 1) E): its partial,
+    // then the xor reduction over the 32 partials
+    const unsigned grp = 0xffffffffu;
+    float nsq = 0.0f;
+#pragma unroll
+    for (int k2 = 0; k2 < E; ++k2) {
+      const float mk = __shfl_sync(grp, m, (threadIdx.x & 31 & ~(E - 1)) + k2);
+      nsq = fmaf(mk, mk, nsq);
+    }
+    if ((e % E) == 0) part[e / E] = nsq;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      const float v = warp_sum(part[threadIdx.x]);
+      if (threadIdx.x == 0) J.norms[static_cast<long long>(head) * J.clusters + c] = v;
+    }
   }
 }
 
@@ -1063,6 +1151,15 @@ int launch_update_t(const UpdateJobs& jobs, int njobs, int bh, int dims, int max
   if (dims == 128) kmeans_update_kernel<128, T><<<grid, kUpdateThreads, 0, stream>>>(jobs, bh, device_status_ptr());
   else if (dims == 64) kmeans_update_kernel<64, T><<<grid, kUpdateThreads, 0, stream>>>(jobs, bh, device_status_ptr());
   else return kErrUnsupported;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    bool big = false;
+    for (int j = 0; j < njobs; ++j) big = big || jobs.job[j].big_rows > 0;
+    if (big) {
+      const dim3 bgrid(static_cast<unsigned>(warps), njobs);  // a block per (head, cluster)
+      if (dims == 128) kmeans_update_big_kernel<128><<<bgrid, 128, 0, stream>>>(jobs, bh, device_status_ptr());
+      else kmeans_update_big_kernel<64><<<bgrid, 64, 0, stream>>>(jobs, bh, device_status_ptr());
+    }
+  }
   return launch_status();
 }
 
@@ -1106,8 +1203,9 @@ int kmeans_fit_bf16(int njobs, const KmeansProblem* probs, int bh, int dims, int
       aj.job[j] = {p.tokens, p.clusters, p.head_rows, nullptr, static_cast<const __nv_bfloat16*>(p.x), cur, p.norms,
                    p.image, p.labels, it > 0 ? p.xnorm : nullptr, it == 0 ? p.xnorm : nullptr};
       // the last update needs no image: nothing assigns against it
+      // long sequences: clusters above 512 rows go to the block kernel
       uj.job[j] = {p.x, p.head_rows, p.tokens, p.clusters, p.perm, p.offsets, cur, nxt, nullptr, p.norms,
-                   it + 1 < iters ? p.image : nullptr};
+                   it + 1 < iters ? p.image : nullptr, p.tokens >= 32768 ? 512 : 0};
     }
     rc = dims == 128 ? launch_assign_t<128, false>(aj, xs, none, rows, stream)
                      : launch_assign_t<64, false>(aj, xs, none, rows, stream);

@@ -210,11 +210,13 @@ def test_full_headline_pair_reuses_tile_slots():
 
 
 def test_long_sequence_fit_sorts_over_segments():
-    """A head of 36000 tokens is sorted by several CTAs (count, scan, place):
-    the permutation must still be the stable argsort of the final labels, the
-    counts and offsets must match it, and the fit must agree with the oracle
-    (the centre update sums each cluster in permutation order, so a wrong
-    order shows up as non-identical centres)."""
+    """A head of 36000 tokens is sorted by several CTAs (count, scan, place)
+    and its clusters above 512 rows are summed by the block kernel: the
+    permutation must still be the stable argsort of the final labels, the
+    counts and offsets must match it, the centres must be bit-identical to the
+    means of the final labels (the update sums each cluster in permutation
+    order, so a wrong order shows up as non-identical centres), and the fit
+    must agree with the oracle."""
     from peco_b200.clustering import kmeans_fit_pair
     w = synthetic.workload("hv-long", heads=2, grid=(10, 45, 80), q_clusters=256, k_clusters=512)
     q, k, _ = synthetic.make_inputs(w, seed=5)
@@ -233,6 +235,9 @@ def test_long_sequence_fit_sorts_over_segments():
         offsets = torch.zeros((h, c + 1), dtype=torch.int32)
         offsets[:, 1:] = torch.cumsum(counts, dim=-1)
         assert torch.equal(b.offsets.cpu(), offsets)
+        assert int(counts.max()) > 512  # the block kernel ran
+        means, _, _ = O.update_centers(xv.float(), labels, b.centers.cpu())  # empty clusters keep theirs
+        assert torch.equal(b.centers.cpu(), means)
         for head in range(h):
             rl, rc, rn = O.fit_token_clusters(xv[head:head + 1], c, iters, init[head:head + 1])
             mism = (labels[head:head + 1] != rl).float().mean().item()
