@@ -178,7 +178,14 @@ class PecoAttention:
         return qb, kb
 
     # -- one call -----------------------------------------------------------
-    def attention(self, query, key, value):
+    def attention(self, query, key, value, value_ready=None):
+        """PECO attention of [1, H, S, D] Q/K/V (peco/processor.py:115-157).
+
+        ``value_ready``, if given, is called on the current stream before the
+        first read of ``value``: a caller still delivering V (an all-to-all
+        in flight) can hand over its buffer early and let the transfer
+        overlap the clustering, which does not need V.
+        """
         batch, heads, length, dim = query.shape
         if batch != 1:
             raise ValueError("This minimal HunyuanVideo entry supports one prompt per call")
@@ -191,13 +198,15 @@ class PecoAttention:
         if warmup:
             if self.config.zero_step_kmeans_init and self.layer_idx >= self.config.warmup_layers:
                 self._update_cluster_state(query[:, :, :video_length], key[:, :, :video_length])
+            if value_ready is not None:
+                value_ready()
             return dense_attention(query, key, value, video_length + valid_text)
         if query.dtype != torch.bfloat16 or key.dtype != torch.bfloat16 or value.dtype != torch.bfloat16:
             raise TypeError("the fused PECO call takes bfloat16 Q/K/V (HunyuanVideo's attention dtype)")
         return self._sparse_call(query.contiguous(), key.contiguous(), value.contiguous(), video_length,
-                                 text_length, valid_text)
+                                 text_length, valid_text, value_ready)
 
-    def _sparse_call(self, q, k, v, video, text_length, valid_text):
+    def _sparse_call(self, q, k, v, video, text_length, valid_text, value_ready=None):
         _native.require_cuda(q, k, v)
         lib = _native.load()
         _, h, s, d = q.shape
@@ -244,6 +253,8 @@ class PecoAttention:
             if ev:
                 ev["plan"].record()
             qp = torch.empty_like(q)
+            if value_ready is not None:  # V is first read here
+                value_ready()
             stream = _native.stream_of(dev, q, k, v, qp)
             st = lib.peco_quantize_gather(
                 _native.ptr(q), _native.ptr(k), _native.ptr(v), _native.ptr(qp), _native.ptr(kblocks),

@@ -50,12 +50,14 @@ def _worker(rank, world, port, kind, out_q):
             dmap = torch.ones((1, h, 2, 2), dtype=torch.bool)
             dmap[0, :, 1, 0] = False
 
-            def attend(q, k, v):
+            def attend(q, k, v, value_ready=None):
+                if kind == "overlap":  # V's all-to-all is still in flight until value_ready()
+                    value_ready()
                 lo = rank * hl
                 return O.sparse_attention(q, k, v, dmap[:, lo:lo + hl], qs[:, lo:lo + hl], qs[:, lo:lo + hl])
 
             ks, vs = (t[:, :, rank * sl:(rank + 1) * sl].contiguous() for t in (k_full, v_full))
-            got = pd.sequence_parallel_attention(attend, shard, ks, vs)
+            got = pd.sequence_parallel_attention(attend, shard, ks, vs, overlap_value=kind == "overlap")
             ref = O.sparse_attention(x, k_full, v_full, dmap, qs, qs)[:, :, rank * sl:(rank + 1) * sl]
             ok = torch.allclose(got, ref, atol=1e-6, rtol=1e-5)
         out_q.put((rank, bool(ok)))
@@ -64,7 +66,7 @@ def _worker(rank, world, port, kind, out_q):
 
 
 @pytest.mark.parametrize("world", [2, 4])
-@pytest.mark.parametrize("kind", ["reshard", "attention"])
+@pytest.mark.parametrize("kind", ["reshard", "attention", "overlap"])
 def test_ulysses_reshard_multi_process(world, kind):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
