@@ -13,9 +13,12 @@ synthetic tensors with that shape and distribution (no dataset is involved).
 Timing: W untimed warm-up calls, then exactly K calls timed with CUDA events
 on the launching stream, bracketed by a barrier and a device synchronise;
 L2 is flushed (256 MB write) before every step, outside the step's events.
-With N GPUs (torchrun) every rank processes its own 24 heads -- heads are
-independent, so there is no collective -- and the job completes N calls per
-step (weak scaling); ``value`` = max-over-ranks step time / N.
+With N GPUs (torchrun) the one call's 24 heads are split 24/N per rank --
+heads are independent, so there is no collective -- and ``value`` is the
+max-over-ranks time of the call (strong scaling).  The same line carries the
+long-video configuration (119k tokens, sequence-sharded over the same N
+ranks and resharded to heads by point-to-point NCCL exchanges) as
+``long_config``, with its own clock record and exchange timings.
 
 ``--impl reference`` times the reference's algorithm on the host CPU cores
 (the CPU restatement in oracle/, all threads) on a bounded sample of heads
@@ -55,6 +58,8 @@ def parse_args():
                     help="heads: every rank runs all heads of its own call (weak scaling); ulysses: one call, "
                          "tokens sequence-sharded over the ranks and resharded to heads by NCCL all-to-all "
                          "(strong scaling, the long-video config)")
+    ap.add_argument("--long-steps", type=int, default=10,
+                    help="timed steps of the long-video sub-record (0 skips it)")
     ap.add_argument("--e2e-steps", type=int, default=100)
     ap.add_argument("--cpu-sample-heads", type=int, default=2)
     ap.add_argument("--baselines", choices=("all", "none"), default="all",
@@ -176,16 +181,19 @@ def make_processor(w, q, k):
     return proc, q_init, k_init
 
 
-def run_ulysses(args, world, rank, local):
-    """One PECO call per step on sequence-sharded Q/K/V [1, H, S/P, D]: NCCL
-    all-to-all to [1, H/P, S, D] (V's stays in flight while the call clusters
-    Q and K), the call on this rank's heads, all-to-all back.  Device time per
-    step (max over ranks) is the whole job's time."""
+def run_ulysses(args, world, rank, local, steps=None, warmup=None, config=None):
+    """One PECO call per step on sequence-sharded Q/K/V [1, H, S/P, D]: Q is
+    resharded to [1, H/P, S, D] first, K's and V's exchanges stay in flight
+    while the call clusters Q (K) and Q and K (V), the call runs on this
+    rank's heads, and the output returns to the sequence sharding.  Device
+    time per step (max over ranks) is the whole job's time."""
     import torch
     from peco_b200 import _native, synthetic
     from peco_b200.distributed import heads_to_seq, seq_to_heads, seq_to_heads_async
 
-    w = synthetic.workload(args.config, **({"top_k": args.top_k} if args.top_k else {}))
+    steps = args.steps if steps is None else steps
+    warmup = args.warmup if warmup is None else warmup
+    w = synthetic.workload(config or args.config, **({"top_k": args.top_k} if args.top_k and not config else {}))
     h, s, d, nv = w.heads, w.seq, w.dims, w.video_tokens
     if h % world or s % world:
         raise SystemExit(f"{h} heads / {s} tokens do not split over {world} ranks")
@@ -197,28 +205,41 @@ def run_ulysses(args, world, rank, local):
     del q_f, k_f, v_f
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
     lib = _native.load()
-    ev_names = ("start", "resharded", "attended", "end")
+    ev_names = ("start", "q_in", "k0", "k1", "v0", "v1", "attended", "end")
 
     def call(evs=None):
         proc.q_centroids, proc.k_centroids = q_init, k_init
-        if evs:
-            evs["start"].record()
-        q, k = (seq_to_heads(t) for t in (q_sh, k_sh))
-        v, v_ready = seq_to_heads_async(v_sh)
-        if evs:
-            evs["resharded"].record()
-        o = proc.attention(q, k, v, value_ready=v_ready)
-        if evs:
-            evs["attended"].record()
+        rec = (lambda n: evs[n].record()) if evs else (lambda n: None)
+        rec("start")
+        q = seq_to_heads(q_sh)
+        rec("q_in")
+        k, k_wait = seq_to_heads_async(k_sh)
+        v, v_wait = seq_to_heads_async(v_sh)
+
+        def k_ready():
+            rec("k0")
+            k_wait()
+            rec("k1")
+
+        def v_ready():
+            rec("v0")
+            v_wait()
+            rec("v1")
+
+        # one rank has nothing in flight: the paired Q/K fit is then the faster form
+        hooks = dict(key_ready=k_ready, value_ready=v_ready) if world > 1 else {}
+        if not hooks:
+            k_ready()
+            v_ready()
+        o = proc.attention(q, k, v, **hooks)
+        rec("attended")
         out = heads_to_seq(o)
-        if evs:
-            evs["end"].record()
+        rec("end")
         return out
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         call()
     torch.cuda.synchronize()
-    steps = args.steps
     evs = [{n: torch.cuda.Event(enable_timing=True) for n in ev_names} for _ in range(steps)]
     sampler = ClockSampler(_smi_id(dev))
     barrier(world)
@@ -233,20 +254,26 @@ def run_ulysses(args, world, rank, local):
     clocks = sampler.stop()
     launches = lib.peco_launch_count() - launches0
     status = _native.device_status(clear=True)
-    step = statistics.mean(e["start"].elapsed_time(e["end"]) for e in evs)
-    a2a = statistics.mean(e["start"].elapsed_time(e["resharded"]) + e["attended"].elapsed_time(e["end"]) for e in evs)
-    att = statistics.mean(e["resharded"].elapsed_time(e["attended"]) for e in evs)
-    step_max = allreduce(step, world, "max")
-    a2a_max, att_max = allreduce(a2a, world, "max"), allreduce(att, world, "max")
+
+    def mean(a, b):
+        return statistics.mean(e[a].elapsed_time(e[b]) for e in evs)
+
+    step = allreduce(mean("start", "end"), world, "max")
+    q_ms, o_ms = allreduce(mean("start", "q_in"), world, "max"), allreduce(mean("attended", "end"), world, "max")
+    k_wait, v_wait = allreduce(mean("k0", "k1"), world, "max"), allreduce(mean("v0", "v1"), world, "max")
+    call_ms = allreduce(mean("q_in", "attended"), world, "max")
     launches_job = int(allreduce(launches, world, "sum"))
+    # bytes one rank sends (and receives) per exchanged tensor: all but its own piece
+    piece_bytes = h * sl * d * 2 * (world - 1) // world
+    gbs = (lambda ms: round(piece_bytes / (ms * 1e-3) / 1e9, 1) if ms > 0 and world > 1 else None)
     return {
         "metric": METRIC.replace("7006", str(s)),
-        "value": round(step_max, 5),
+        "value": round(step, 5),
         "unit": "ms",
         "n_gpus": world,
         "steps": steps,
-        "warmup": args.warmup,
-        "ms_per_step": round(step_max, 5),
+        "warmup": warmup,
+        "ms_per_step": round(step, 5),
         "higher_is_better": False,
         "scaling": "strong",
         "vs_baseline": None,
@@ -257,12 +284,18 @@ def run_ulysses(args, world, rank, local):
             "workload": f"{w.name}: {h} heads x {s} tokens ({nv} video + {w.text_length} text), d={d}, "
                         f"CQ={w.q_clusters}, CK={w.k_clusters}, {w.iters} Lloyd iterations, top-{w.top_k}, "
                         f"{w.bits}-bit Base-Offset",
-            "parallelism": f"ulysses: tokens sequence-sharded over {world} rank(s), NCCL all-to-all to {hl} heads "
-                           "per rank and back; V's all-to-all overlaps the k-means",
+            "parallelism": f"ulysses: tokens sequence-sharded over {world} rank(s), point-to-point NCCL exchanges to "
+                           f"{hl} heads per rank and back; K's exchange overlaps Q's k-means, V's both",
             "l2": "flushed before every step (256 MB write), outside the step events",
         },
-        # all_to_all_ms: Q and K in, O out; V's all-to-all runs inside peco_call_ms
-        "stages": {"all_to_all_ms": round(a2a_max, 5), "peco_call_ms": round(att_max, 5)},
+        "stages": {
+            "q_exchange_ms": round(q_ms, 5), "o_exchange_ms": round(o_ms, 5),
+            "k_exposed_wait_ms": round(k_wait, 5), "v_exposed_wait_ms": round(v_wait, 5),
+            "peco_call_ms": round(call_ms, 5),
+            "exchange_bytes_per_rank_per_tensor": piece_bytes,
+            "q_exchange_gbs_per_rank": gbs(q_ms), "o_exchange_gbs_per_rank": gbs(o_ms),
+            "note": "peco_call_ms includes the exposed waits for K and V; max over ranks per entry",
+        },
         "gpu_launches": launches_job,
         "clocks": clocks,
         "device_status": status,
@@ -388,9 +421,14 @@ def run_ours(args, world, rank, local):
     from peco_b200 import _native, synthetic
 
     w = synthetic.workload(args.config, **({"top_k": args.top_k} if args.top_k else {}))
-    h, s, d, nv = w.heads, w.seq, w.dims, w.video_tokens
+    s, d, nv = w.seq, w.dims, w.video_tokens
+    if w.heads % world:
+        raise SystemExit(f"{w.heads} heads do not split over {world} ranks")
+    h = w.heads // world  # this rank's heads of the one call
     dev = torch.device("cuda", local if world > 1 else 0)
-    q_c, k_c, v_c = synthetic.make_inputs(w, seed=1000 + rank)
+    full = synthetic.make_inputs(w, seed=1000)
+    q_c, k_c, v_c = (t[:, rank * h:(rank + 1) * h].contiguous() for t in full)
+    del full
     q, k, v = (t.to(dev).contiguous() for t in (q_c, k_c, v_c))
     proc, q_init, k_init = make_processor(w, q_c, k_c)
     q_init, k_init = q_init.to(dev), k_init.to(dev)
@@ -412,7 +450,7 @@ def run_ours(args, world, rank, local):
     proc.keep_partition = True
     out = call()
     emap, eqs, eks = proc.last_partition
-    attn_flops = attention_flops(emap, eqs, eks, d)
+    attn_flops = attention_flops(emap, eqs, eks, d)  # this rank's heads
     dense_flops = 4.0 * d * s * s * h
     kmeans_flops = 2.0 * nv * (w.q_clusters + w.k_clusters) * d * h * w.iters
     qg_bytes = (3 * h * s * d * 2) * 2 + 2 * h * nv * 4 * 2 + h * (w.q_clusters + w.k_clusters) * d * 4
@@ -449,9 +487,8 @@ def run_ours(args, world, rank, local):
             stage[name].append(ev[prev[name]].elapsed_time(ev[name]))
     proc.stage_events = None
     mean_rank = sum(step_ms) / steps
-    mean_max = allreduce(mean_rank, world, "max")
+    mean_max = allreduce(mean_rank, world, "max")  # the call ends when its slowest rank does
     launches_job = int(allreduce(launches, world, "sum"))
-    value = mean_max / world  # N calls per step across the job
 
     # end to end through the public API with host buffers, pipelined the way a
     # serving loop runs it: the inputs of step i+1 cross PCIe (copy stream)
@@ -535,9 +572,9 @@ def run_ours(args, world, rank, local):
             "n_gpus": world,
             "steps": steps,
             "warmup": args.warmup,
-            "ms_per_step": round(graph["ms_per_call"] * world, 5),
+            "ms_per_step": round(graph["ms_per_call"], 5),
             "higher_is_better": False,
-            "scaling": "weak",
+            "scaling": "strong",
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic: seeded Gaussian-mixture video Q/K (block-map centres, noise 0.3), N(0,1) text Q/K and V",
@@ -545,16 +582,17 @@ def run_ours(args, world, rank, local):
                 "workload": f"{w.name}: {h} heads x {s} tokens ({nv} video + {w.text_length} text), d={d}, "
                             f"CQ={w.q_clusters}, CK={w.k_clusters}, {w.iters} Lloyd iterations, top-{w.top_k}, "
                             f"{w.bits}-bit Base-Offset",
-                "parallelism": f"heads independent, {world} rank(s) x {h} heads, no collective",
+                "parallelism": f"heads sharded: one {w.heads}-head call split over {world} rank(s), {h} heads "
+                               "each, no collective (per-head stages are independent)",
                 "l2": "flushed before every step (256 MB write), outside the step events",
                 "init": f"{w.init} tokens as initial centroids, the same every step",
                 "timing": "value: the steady-state call replayed as one CUDA graph (peco_b200.graph.PecoCallGraph, "
                           "same kernels and results); eager.ms_per_call: the same call issued eagerly through "
                           "PecoAttention.attention, whose stage events give stages",
             },
-            "eager": {"ms_per_call": round(value, 5), "ms_per_step": round(mean_max, 5)},
+            "eager": {"ms_per_call": round(mean_max, 5)},
             "roofline": {
-                "kernel": "sparse_attention_tc, attention stage of the call",
+                "kernel": f"sparse_attention_tc, attention stage of the call (rank 0: {h} heads)",
                 "bound": "tensor",
                 "achieved": round(attn_tflops, 2),
                 "peak": tf_burst,
@@ -563,7 +601,9 @@ def run_ours(args, world, rank, local):
                 "peak_source": f"{peak_kind} bf16 burst (MEASURED_PEAKS.json)",
                 "algorithmic_flops_per_launch": attn_flops,
                 "dense_equivalent_flops": dense_flops,
-                "traffic": _profile_traffic(),
+                "traffic": None,
+                "traffic_note": "not measured by this run: ncu DRAM bytes per launch of the same kernel build are "
+                                "in profiles/sparse_attention_tc_hv480.md",
             },
             "stages": {
                 "kmeans": {"ms": round(km_ms, 5), "algorithmic_tflops": round(kmeans_flops / (km_ms * 1e-3) / 1e12, 2),
@@ -577,7 +617,7 @@ def run_ours(args, world, rank, local):
                               "dense_equivalent_tflops": round(dense_flops / (attn_ms * 1e-3) / 1e12, 2),
                               "density": round(attn_flops / dense_flops, 4)},
             },
-            "e2e": {"value": round(e2e_max / world, 5), "unit": "ms", "h2d_bytes_per_step": 3 * q.numel() * 2 * world,
+            "e2e": {"value": round(e2e_max, 5), "unit": "ms", "h2d_bytes_per_step": 3 * q.numel() * 2 * world,
                     "d2h_bytes_per_step": q.numel() * 2 * world,
                     "api": "peco_b200.processor.PecoAttention.attention with pinned host Q/K/V and output; "
                            "step i+1's inputs upload while step i computes (copy streams)"},
@@ -625,7 +665,7 @@ def _graph_leg(proc, q_init, k_init, q, k, v, flush, steps, world):
     mean = allreduce(sum(a.elapsed_time(b) for a, b in zip(starts, ends)) / steps, world, "max")
     proc.update_centroids_in_place = False
     del g
-    return {"ms_per_call": round(mean / world, 5), "host_enqueue_us_graph": round(host_us, 1),
+    return {"ms_per_call": round(mean, 5), "host_enqueue_us_graph": round(host_us, 1),
             "api": "peco_b200.graph.PecoCallGraph (one graph launch per call)"}
 
 
@@ -637,20 +677,6 @@ def _smi_id(dev):
         return u if u.startswith("GPU-") else "GPU-" + u
     except Exception:
         return str(dev.index or 0)
-
-
-def _profile_traffic():
-    """DRAM bytes per attention launch from the committed ncu summary, if any."""
-    p = ROOT / "profiles" / "sparse_attention_tc_hv480.md"
-    if not p.exists():
-        return None
-    for line in p.read_text().splitlines():
-        if line.startswith("traffic_bytes_per_launch:"):
-            try:
-                return float(line.split(":", 1)[1].strip())
-            except ValueError:
-                return None
-    return None
 
 
 def cpu_baseline(w, inputs, heads_sample, steps=1):
@@ -724,6 +750,12 @@ def main():
                 print(json.dumps(result), flush=True)
             return
         result, (inputs_w) = run_ours(args, world, rank, local)
+        if args.long_steps > 0 and args.config in ("hv480", "hv480-nopq"):
+            import torch
+            torch.cuda.empty_cache()
+            long = run_ulysses(args, world, rank, local, steps=args.long_steps, warmup=3, config="hv-long")
+            if rank == 0:
+                result["long_config"] = long
         if rank == 0 and world == 1 and args.baselines == "all":
             q_c, k_c, v_c, w = inputs_w
             ms, cores, sample = cpu_baseline(w, (q_c, k_c, v_c), args.cpu_sample_heads)
@@ -781,7 +813,7 @@ def main_reference(args):
         "warmup": args.warmup,
         "ms_per_step": round(value, 1),
         "higher_is_better": False,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic: seeded Gaussian-mixture video Q/K (block-map centres, noise 0.3), N(0,1) text Q/K and V",

@@ -72,7 +72,10 @@ int peco_reorder_token_features(const void* input, const int32_t* indices, void*
  * (an allocation can fail or stall under fragmentation there), or a process
  * whose stream-ordered pool is unavailable or capped.  The first call on a
  * device looks up the array's address (cudaGetSymbolAddress) and should come
- * before any stream capture.  Nothing in the scratch must start at zero.
+ * before any stream capture; the address is kept for the process's lifetime,
+ * so do not call it on a device after cudaDeviceReset there (the array, and
+ * the address, are gone with the context).  Nothing in the scratch must
+ * start at zero.
  * Calls that overlap on one device share the scratch and race; serialise
  * them. */
 int peco_recompute_cluster_centers_static(const float* x, const int32_t* labels, const float* previous,

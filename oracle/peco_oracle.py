@@ -288,6 +288,38 @@ def sparse_attention(q, k, v, dmap, q_sizes, k_sizes) -> torch.Tensor:
     return out
 
 
+def sparse_attention_rows(q, k, v, dmap, q_sizes, k_sizes, rows) -> torch.Tensor:
+    """:func:`sparse_attention` of one head evaluated only at packed query ``rows``.
+
+    q [SQ,D], k/v [SK,D] in group-packed order, dmap [GQ,GK], sizes [GQ]/[GK],
+    rows a 1-D index tensor.  Each row attends to the key runs of the groups
+    its own group selects (sparse_attention.cu:55-190); rows of no group or
+    with no allowed key are zero.  Cost is proportional to the sampled rows,
+    which is what makes the 119k-token configuration checkable on a CPU.
+    Returns fp32 [len(rows), D].
+    """
+    sq, d = q.shape
+    sk = k.shape[0]
+    qp = group_prefix(q_sizes, sq)
+    kp = group_prefix(k_sizes, sk)
+    group = torch.searchsorted(qp[1:], rows.long(), right=True)
+    out = torch.zeros((rows.numel(), d), dtype=torch.float32)
+    scale = 1.0 / math.sqrt(d)
+    kf, vf = k.float(), v.float()
+    for g in torch.unique(group).tolist():
+        if g >= dmap.shape[0]:
+            continue
+        sel = (group == g).nonzero().flatten()
+        cols = [torch.arange(int(kp[c]), int(kp[c + 1])) for c in torch.nonzero(dmap[g]).flatten().tolist()
+                if kp[c + 1] > kp[c]]
+        if not cols:
+            continue
+        idx = torch.cat(cols)
+        s = (q[rows[sel].long()].float() @ kf[idx].T) * scale
+        out[sel] = torch.softmax(s, dim=-1) @ vf[idx]
+    return out
+
+
 # --------------------------------------------------------------------------
 # one PECO attention call (peco/processor.py:115-157, non-warmup branch)
 # --------------------------------------------------------------------------

@@ -986,7 +986,11 @@ __global__ void __launch_bounds__(D) kmeans_update_big_kernel(const UpdateJobs j
   const int c = static_cast<int>(w - static_cast<long long>(head) * J.clusters);
   const int start = J.offsets[static_cast<long long>(head) * (J.clusters + 1) + c];
   const int end = J.offsets[static_cast<long long>(head) * (J.clusters + 1) + c + 1];
-  if (end - start <= J.big_rows || start < 0 || end > J.tokens) return;
+  if (end - start <= J.big_rows) return;  // the warp kernel sums it
+  if (start < 0 || end > J.tokens) {       // the warp kernel skipped it as large: report it here
+    if (threadIdx.x == 0) record_status(status, kDevBadIndex);
+    return;
+  }
   __shared__ __align__(16) T buf[kBigChunk * D];
   __shared__ float part[32];
   const int e = threadIdx.x;

@@ -147,12 +147,14 @@ class PecoAttention:
         self.q_centroids = self.k_centroids = None
 
     # -- clustering state ---------------------------------------------------
-    def _update_cluster_state(self, query, key):
+    def _update_cluster_state(self, query, key, key_ready=None):
         """Fit Q/K partitions, reusing this layer's centres after initialization.
 
         ``query``/``key`` are [1,H,N,D] views (possibly of a longer sequence).
         Returns the two KmeansBuffers (labels, counts, perm, ...) and updates
-        the cached fp32 centroids [H,C,D].
+        the cached fp32 centroids [H,C,D].  With ``key_ready`` (K still
+        arriving) Q is clustered first, then ``key_ready()`` runs, then K is
+        clustered; otherwise both run in the same launches.
         """
         b, h, n, d = query.shape
         initializing = self.q_centroids is None
@@ -161,30 +163,44 @@ class PecoAttention:
             # fp16/fp32 inputs: the reference's fp32 iteration on the drop-in entry points
             ql, qc, qn, _ = fit_token_clusters(query.reshape(b * h, n, d).contiguous(), self.config.num_q_centroids,
                                                max_iters=iters, tol=0, init_centroids=self.q_centroids)
+            if key_ready is not None:
+                key_ready()
             kl, kc, kn, _ = fit_token_clusters(key.reshape(b * h, n, d).contiguous(), self.config.num_k_centroids,
                                                max_iters=iters, tol=0, init_centroids=self.k_centroids)
             self.q_centroids, self.k_centroids = qc, kc
             return (ql, qn), (kl, kn)
-        q_rows, q_stride = _rows_view(query)
-        k_rows, k_stride = _rows_view(key)
-        q_init = self.q_centroids if not initializing else _first_tokens_init(query.reshape(b * h, n, d),
-                                                                             self.config.num_q_centroids)
-        k_init = self.k_centroids if not initializing else _first_tokens_init(key.reshape(b * h, n, d),
-                                                                             self.config.num_k_centroids)
         in_place = self.update_centroids_in_place and not initializing
-        qb, kb = kmeans_fit_pair(q_rows, q_stride, n, q_init, k_rows, k_stride, n, k_init, b * h, d, iters,
-                                 q_centers=q_init if in_place else None, k_centers=k_init if in_place else None)
+
+        def rows_and_init(x, cached, clusters):
+            rows, stride = _rows_view(x)
+            init = cached if not initializing else _first_tokens_init(x.reshape(b * h, n, d), clusters)
+            return rows, stride, init
+
+        q_rows, q_stride, q_init = rows_and_init(query, self.q_centroids, self.config.num_q_centroids)
+        if key_ready is None:
+            k_rows, k_stride, k_init = rows_and_init(key, self.k_centroids, self.config.num_k_centroids)
+            qb, kb = kmeans_fit_pair(q_rows, q_stride, n, q_init, k_rows, k_stride, n, k_init, b * h, d, iters,
+                                     q_centers=q_init if in_place else None, k_centers=k_init if in_place else None)
+        else:
+            qb, _ = kmeans_fit_pair(q_rows, q_stride, n, q_init, None, 0, 0, q_init, b * h, d, iters,
+                                    q_centers=q_init if in_place else None)
+            key_ready()
+            k_rows, k_stride, k_init = rows_and_init(key, self.k_centroids, self.config.num_k_centroids)
+            kb, _ = kmeans_fit_pair(k_rows, k_stride, n, k_init, None, 0, 0, k_init, b * h, d, iters,
+                                    q_centers=k_init if in_place else None)
         self.q_centroids, self.k_centroids = qb.centers, kb.centers
         return qb, kb
 
     # -- one call -----------------------------------------------------------
-    def attention(self, query, key, value, value_ready=None):
+    def attention(self, query, key, value, value_ready=None, key_ready=None):
         """PECO attention of [1, H, S, D] Q/K/V (peco/processor.py:115-157).
 
-        ``value_ready``, if given, is called on the current stream before the
-        first read of ``value``: a caller still delivering V (an all-to-all
-        in flight) can hand over its buffer early and let the transfer
-        overlap the clustering, which does not need V.
+        ``key_ready`` / ``value_ready``, if given, are called on the current
+        stream before the first read of ``key`` / ``value``: a caller still
+        delivering K or V (a reshard in flight) can hand over the buffers
+        early and let the transfers overlap the clustering of Q (K) and of
+        Q and K (V).  The caller stays responsible for waiting on a transfer
+        when this method raises before calling its hook.
         """
         batch, heads, length, dim = query.shape
         if batch != 1:
@@ -197,16 +213,18 @@ class PecoAttention:
         warmup = self.context.step < self.config.warmup_steps or self.layer_idx < self.config.warmup_layers
         if warmup:
             if self.config.zero_step_kmeans_init and self.layer_idx >= self.config.warmup_layers:
-                self._update_cluster_state(query[:, :, :video_length], key[:, :, :video_length])
+                self._update_cluster_state(query[:, :, :video_length], key[:, :, :video_length], key_ready)
+            elif key_ready is not None:
+                key_ready()
             if value_ready is not None:
                 value_ready()
             return dense_attention(query, key, value, video_length + valid_text)
         if query.dtype != torch.bfloat16 or key.dtype != torch.bfloat16 or value.dtype != torch.bfloat16:
             raise TypeError("the fused PECO call takes bfloat16 Q/K/V (HunyuanVideo's attention dtype)")
         return self._sparse_call(query.contiguous(), key.contiguous(), value.contiguous(), video_length,
-                                 text_length, valid_text, value_ready)
+                                 text_length, valid_text, value_ready, key_ready)
 
-    def _sparse_call(self, q, k, v, video, text_length, valid_text, value_ready=None):
+    def _sparse_call(self, q, k, v, video, text_length, valid_text, value_ready=None, key_ready=None):
         _native.require_cuda(q, k, v)
         lib = _native.load()
         _, h, s, d = q.shape
@@ -219,7 +237,7 @@ class PecoAttention:
                   for n in ("start", "kmeans", "select", "plan", "gather", "attention")}
             self.stage_events.append(ev)
             ev["start"].record()
-        qb, kb = self._update_cluster_state(q[:, :, :video], k[:, :, :video])
+        qb, kb = self._update_cluster_state(q[:, :, :video], k[:, :, :video], key_ready)
         if ev:
             ev["kmeans"].record()
         dev = q.device
@@ -237,7 +255,8 @@ class PecoAttention:
             _native.check(st, "peco_select_text_partition")
             if ev:
                 ev["select"].record()
-            if getattr(self, "keep_partition", False):
+            keep = getattr(self, "keep_partition", False)
+            if keep:
                 self.last_partition = (emap, qs_ext, ks_ext)
             # plan first: it zeroes the padding rows of the key blocks and maps
             # every packed key row to its block row for the gather
@@ -264,6 +283,10 @@ class PecoAttention:
             _native.check(st, "peco_quantize_gather")
             if ev:
                 ev["gather"].record()
+            if keep:
+                # the call's intermediate state, for inspection by tests and tools
+                self.last_state = dict(q_labels=qb.labels, k_labels=kb.labels, q_perm=qb.perm, k_perm=kb.perm,
+                                       q_counts=qb.counts, k_counts=kb.counts, q_packed=qp)
             out = torch.empty_like(q)
             stream = _native.stream_of(dev, out, qb.perm)
             st = lib.peco_sparse_attention_restore(

@@ -34,7 +34,7 @@ def _worker(rank, world, port, kind, out_q):
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        b, h, s, d = 1, 4 * world, 24 * world, 16
+        b, h, s, d = (2 if kind == "reshard" else 1), 4 * world, 24 * world, 16
         sl, hl = s // world, h // world
         x = _full(1, b, h, s, d)
         shard = x[:, :, rank * sl:(rank + 1) * sl].contiguous()
@@ -50,16 +50,29 @@ def _worker(rank, world, port, kind, out_q):
             dmap = torch.ones((1, h, 2, 2), dtype=torch.bool)
             dmap[0, :, 1, 0] = False
 
-            def attend(q, k, v, value_ready=None):
-                if kind == "overlap":  # V's all-to-all is still in flight until value_ready()
+            def attend(q, k, v, key_ready=None, value_ready=None):
+                if kind == "overlap":  # K's and V's transfers are in flight until their hooks run
+                    key_ready()
                     value_ready()
                 lo = rank * hl
                 return O.sparse_attention(q, k, v, dmap[:, lo:lo + hl], qs[:, lo:lo + hl], qs[:, lo:lo + hl])
 
+            def failing(q, k, v, key_ready=None, value_ready=None):
+                raise RuntimeError("attention failed before reading K and V")
+
             ks, vs = (t[:, :, rank * sl:(rank + 1) * sl].contiguous() for t in (k_full, v_full))
-            got = pd.sequence_parallel_attention(attend, shard, ks, vs, overlap_value=kind == "overlap")
+            ok = True
+            if kind == "overlap":
+                # a callable that raises before its hooks: the transfers are still
+                # waited for, and the next exchange on the group works
+                try:
+                    pd.sequence_parallel_attention(failing, shard, ks, vs, overlap=True)
+                    ok = False
+                except RuntimeError:
+                    pass
+            got = pd.sequence_parallel_attention(attend, shard, ks, vs, overlap=kind == "overlap")
             ref = O.sparse_attention(x, k_full, v_full, dmap, qs, qs)[:, :, rank * sl:(rank + 1) * sl]
-            ok = torch.allclose(got, ref, atol=1e-6, rtol=1e-5)
+            ok = ok and torch.allclose(got, ref, atol=1e-6, rtol=1e-5)
         out_q.put((rank, bool(ok)))
     finally:
         dist.destroy_process_group()

@@ -147,3 +147,20 @@ def test_sparse_attention_oracle_matches_dense_mask():
         sc = sc.masked_fill(~mask, float("-inf"))
         p = torch.softmax(sc, -1).nan_to_num(0.0)
         torch.testing.assert_close(out[0, hi], p @ v[0, hi], rtol=1e-5, atol=1e-5)
+
+
+def test_sparse_attention_rows_equals_full_oracle():
+    """The row-sampled form (used where the full oracle is too slow) returns the
+    full oracle's rows, including rows of a group with no key and rows past
+    the last group."""
+    g = torch.Generator().manual_seed(4)
+    s, d = 60, 64
+    q, k, v = (torch.randn((1, 1, s, d), generator=g) for _ in range(3))
+    qs = torch.tensor([[[10, 0, 12, 30]]], dtype=torch.int32)  # 52 rows in groups, 8 past the end
+    ks = torch.tensor([[[7, 13, 0, 40]]], dtype=torch.int32)
+    dmap = torch.rand((1, 1, 4, 4), generator=g) > 0.4
+    dmap[0, 0, 2] = False
+    full = O.sparse_attention(q, k, v, dmap, qs, ks)[0, 0]
+    rows = torch.tensor([0, 3, 9, 10, 11, 21, 22, 40, 51, 52, 59])
+    got = O.sparse_attention_rows(q[0, 0], k[0, 0], v[0, 0], dmap[0, 0], qs[0, 0], ks[0, 0], rows)
+    torch.testing.assert_close(got, full[rows], rtol=1e-6, atol=1e-6)

@@ -4,14 +4,16 @@ that allocates nothing (its sort scratch is a fixed per-device array).
 Called through the C ABI and compared with the allocating entry point
 peco_recompute_cluster_centers on the same inputs, twice in a row (the
 second call reuses the scratch the first one left behind).  Tolerance:
-bit-exact -- both run the same sort and update kernels.
+bit-exact -- both run the same sort and update kernels.  Because a bug in
+those shared kernels would pass that comparison, one case is also checked
+against the CPU oracle's centroid update, and a problem that fills the fixed
+scratch exactly is accepted and correct.
 """
-
-import ctypes
 
 import pytest
 import torch
 
+from oracle import peco_oracle as O
 from peco_b200 import _native
 
 pytestmark = pytest.mark.gpu
@@ -55,6 +57,33 @@ def test_static_update_matches_allocating_update(batch, tokens, dims, clusters):
         torch.cuda.synchronize()
         for a, b in zip(got, ref):
             assert torch.equal(a, b)
+    assert _native.device_status(clear=True) == 0
+    if batch == 3:
+        # independent of the shared kernels: the CPU restatement of the update
+        means, counts, sums = O.update_centers(x.cpu(), labels.cpu(), previous.cpu())
+        assert torch.equal(got[2].cpu(), means)
+        assert torch.equal(got[1].cpu(), counts)
+        assert torch.equal(got[0].cpu(), sums)
+
+
+def test_static_update_accepts_a_problem_that_fills_its_scratch():
+    lib = _native.load()
+    cap = int(lib.peco_recompute_cluster_centers_static_capacity())
+    batch, dims, clusters = 1, 64, 7
+    tokens = cap - batch * (clusters + 1)  # batch*tokens + batch*(clusters+1) == cap
+    g = torch.Generator(device=DEV).manual_seed(9)
+    x = torch.randn((batch, tokens, dims), generator=g, device=DEV)
+    labels = torch.randint(0, clusters, (batch, tokens), generator=g, device=DEV, dtype=torch.int32)
+    previous = torch.randn((batch, clusters, dims), generator=g, device=DEV)
+    ref, got = _outputs(batch, clusters, dims), _outputs(batch, clusters, dims)
+    _native.check(_call(lib.peco_recompute_cluster_centers, x, labels, previous, ref, batch, tokens, dims, clusters),
+                  "peco_recompute_cluster_centers")
+    status = _call(lib.peco_recompute_cluster_centers_static, x, labels, previous, got, batch, tokens, dims, clusters)
+    assert status == 0
+    torch.cuda.synchronize()
+    for a, b in zip(got, ref):
+        assert torch.equal(a, b)
+    assert int(got[1].sum()) == tokens
     assert _native.device_status(clear=True) == 0
 
 
