@@ -200,6 +200,22 @@ int peco_sparse_attention_restore(const void* q, const void* k_blocks, const voi
                                   const int* workspace, void* output, int bh, int sq, int sk, int d, int gq,
                                   int gk, const int32_t* q_indices, int video, void* stream);
 
+/* Input stage of the attention processor: from the bf16 projection outputs
+ * of the video rows (vq/vk/vv) and the text rows (tq/tk/tv), each a
+ * row-major [rows, H*D] view with ``*_stride`` elements between rows, write
+ * bf16 Q/K/V [H, video_rows + text_rows, D] (video rows first).  Per (row,
+ * head): Q and K are RMS-normalised with the stream's gains (w*_v / w*_t,
+ * fp32 [D]; null: no norm), rounded to bf16, and video rows are rotated with
+ * the (cos, sin) tables [video_rows, D] fp32, pairs interleaved (null: no
+ * rotation); V is copied.  Replaces the head split, norm_q/norm_k,
+ * apply_rotary_emb, concatenations and contiguous copies of
+ * peco/processor.py:163-188. */
+int peco_prepare_qkv(const void* vq, const void* vk, const void* vv, long long v_stride, int video_rows,
+                     const void* tq, const void* tk, const void* tv, long long t_stride, int text_rows,
+                     const float* wq_v, const float* wk_v, float eps_v, const float* wq_t, const float* wk_t,
+                     float eps_t, const float* cos, const float* sin, void* q, void* k, void* v, int heads,
+                     int dims, void* stream);
+
 /* ---- diagnostics --------------------------------------------------------- */
 
 /* Copies the device status word of the current device to *out (synchronising

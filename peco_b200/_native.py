@@ -38,6 +38,7 @@ _SIGNATURES = {
     "peco_attention_plan": [P] * 6 + [I] * 6 + [P],
     "peco_pack_key_blocks": [P] * 5 + [I] * 6 + [P],
     "peco_sparse_attention_restore": [P] * 5 + [I] * 6 + [P, I, P],
+    "peco_prepare_qkv": [P, P, P, LL, I, P, P, P, LL, I, P, P, F, P, P, F, P, P, P, P, P, I, I, P],
     "peco_attention_workspace_stride": [I, I, I, I],
     "peco_key_block_rows": [I, I],
     "peco_kmeans_work_floats": [I, I, I],

@@ -125,25 +125,28 @@ def fit_token_clusters(x, n_clusters, max_iters=100, tol=1e-4, init_centroids=No
         xb = x.contiguous()
         qb, _ = kmeans_fit_pair(xb, tokens, tokens, centers, None, 0, 0, centers, batch, dims, max_iters)
         return qb.labels, qb.centers, qb.counts, max_iters
-    x = x.float().contiguous()
-    labels = torch.empty((batch, tokens), dtype=torch.int32, device=x.device)
-    counts = torch.empty((batch, n_clusters), dtype=torch.int32, device=x.device)
+    # other dtypes, or early stopping: one assignment and one update per
+    # iteration on the drop-in entry points, in fp32
+    x32 = x.float().contiguous()
+    dev = x32.device
+    labels = torch.empty((batch, tokens), dtype=torch.int32, device=dev)
+    counts = torch.empty((batch, n_clusters), dtype=torch.int32, device=dev)
     sums = torch.empty_like(centers)
-    means = torch.empty_like(centers)
-    chunk_size = min(chunk_size, tokens)
-    scratch = torch.empty((chunk_size, n_clusters), dtype=torch.float32, device=x.device)
-    center_norms = torch.empty((batch, n_clusters), dtype=torch.float32, device=x.device)
-    iteration = 0
-    for iteration in range(1, max_iters + 1):
-        clustering_cuda.assign_tokens_to_centers(x, centers, labels, scratch, center_norms, chunk_size)
-        clustering_cuda.recompute_cluster_centers(x, labels, centers, sums, counts, means)
-        shift = None
-        if tol > 0:
-            shift = torch.linalg.vector_norm(means - centers, dim=-1).max().item()
-        centers, means = means, centers
-        if tol > 0 and shift <= tol:
+    norms = torch.empty((batch, n_clusters), dtype=torch.float32, device=dev)
+    rows = min(chunk_size, tokens)
+    scratch = torch.empty((rows, n_clusters), dtype=torch.float32, device=dev)
+    current, following = centers, torch.empty_like(centers)
+    done = 0
+    while done < max_iters:
+        done += 1
+        clustering_cuda.assign_tokens_to_centers(x32, current, labels, scratch, norms, rows)
+        clustering_cuda.recompute_cluster_centers(x32, labels, current, sums, counts, following)
+        # the largest centre displacement, checked on the host only when asked for
+        settled = tol > 0 and float((following - current).norm(dim=-1).max()) <= tol
+        current, following = following, current
+        if settled:
             break
-    return labels, centers, counts, iteration
+    return labels, current, counts, done
 
 
 def _prepare_sequence_indices(tensor, labels, dim, sorted_indices):
@@ -186,22 +189,6 @@ def restore_sequence_order(tensor, sorted_indices, dim=2):
     _native.require_cuda(tensor)
     indices = _prepare_sequence_indices(tensor, None, dim, sorted_indices)
     return clustering_cuda.reorder_token_features(tensor, indices, inverse=True)
-
-
-@torch.no_grad()
-def compute_cluster_weights(scores, weights):
-    """softmax(scores + log(counts)) over the key-cluster axis in FP32.
-
-    Empty clusters get zero mass; an entirely empty row returns zeros
-    (peco/clustering.py:139-151).  The fused selection kernel computes the
-    same quantity internally; this function exposes it for callers.
-    """
-    scores, weights = scores.float(), weights.float()
-    logits = scores + torch.where(weights > 0, weights.log(), -torch.inf)
-    row_max = logits.max(dim=-1, keepdim=True).values
-    row_max = torch.where(torch.isfinite(row_max), row_max, torch.zeros_like(row_max))
-    mass = torch.exp(logits - row_max)
-    return mass / mass.sum(dim=-1, keepdim=True).clamp_min(torch.finfo(torch.float32).tiny)
 
 
 @torch.no_grad()

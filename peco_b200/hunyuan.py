@@ -69,14 +69,18 @@ def _ln(x):
 
 
 class SDPAProcessor(PecoAttention):
-    """Exact joint attention with torch SDPA (the dense baseline): the PECO
-    processor's projections, norms and rotary embedding, with the attention
-    itself replaced by full softmax attention over [0, valid) and [valid, S)."""
+    """Exact joint attention with torch SDPA (the dense baseline).
+
+    On CUDA bf16 it is the PECO processor's entry (the fused projection-side
+    kernel) with the attention itself replaced by full softmax attention over
+    [0, valid) and [valid, S).  Elsewhere (CPU, fp32) the same math runs as
+    plain torch: projections, the modules' norms, the rotation of the video
+    rows, SDPA and the output projections."""
 
     def __init__(self, context: InferenceContext):
         super().__init__(0, PecoConfig(), context)
 
-    def attention(self, query, key, value):
+    def attention(self, query, key, value, value_ready=None, key_ready=None):
         s = query.shape[2]
         valid = s - self.context.text_length + self.context.valid_text_length
         out = torch.empty_like(query)
@@ -84,6 +88,47 @@ class SDPAProcessor(PecoAttention):
             if a < b:
                 out[:, :, a:b] = F.scaled_dot_product_attention(query[:, :, a:b], key[:, :, a:b], value[:, :, a:b])
         return out
+
+    def __call__(self, attn, hidden_states, encoder_hidden_states=None, attention_mask=None, image_rotary_emb=None):
+        if hidden_states.is_cuda and hidden_states.dtype == torch.bfloat16:
+            return super().__call__(attn, hidden_states, encoder_hidden_states, attention_mask, image_rotary_emb)
+        return self._torch_call(attn, hidden_states, encoder_hidden_states, image_rotary_emb)
+
+    def _torch_call(self, attn, video, text, rope):
+        separate = attn.add_q_proj is not None
+        n_text = 0 if text is None else text.shape[1]
+
+        def heads_of(x, layers, norms):
+            q, k, v = (layer(x).unflatten(-1, (attn.heads, -1)).transpose(1, 2) for layer in layers)
+            return norms[0](q), norms[1](k), v
+
+        q, k, v = heads_of(video, (attn.to_q, attn.to_k, attn.to_v), (attn.norm_q, attn.norm_k))
+        if rope is not None:
+            q, k = rotate_pairs(q, *rope), rotate_pairs(k, *rope)
+        if n_text:
+            layers = (attn.add_q_proj, attn.add_k_proj, attn.add_v_proj) if separate else (attn.to_q, attn.to_k, attn.to_v)
+            norms = (attn.norm_added_q, attn.norm_added_k) if separate else (attn.norm_q, attn.norm_k)
+            tq, tk, tv = heads_of(text, layers, norms)
+            q, k, v = torch.cat((q, tq), 2), torch.cat((k, tk), 2), torch.cat((v, tv), 2)
+        rows = self.attention(q, k, v).transpose(1, 2).flatten(2)
+        video_out, text_out = rows[:, : video.shape[1]], rows[:, video.shape[1]:]
+        if not n_text:
+            return video_out, text
+        if attn.to_out is not None:
+            for layer in attn.to_out:
+                video_out = layer(video_out)
+        if attn.to_add_out is not None:
+            text_out = attn.to_add_out(text_out)
+        return video_out, text_out
+
+
+def rotate_pairs(x, cos, sin):
+    """Rotary embedding of [.., N, D] rows with (cos, sin) tables [N, D], pairs
+    (2i, 2i+1) interleaved: (a, b) -> (a cos - b sin, b cos + a sin), each
+    product and the sum in fp32, rounded once to x's dtype."""
+    a, b = x.float().unflatten(-1, (-1, 2)).unbind(-1)
+    turned = torch.stack((-b, a), -1).flatten(-2)
+    return (x.float() * cos.to(x.device) + turned * sin.to(x.device)).to(x.dtype)
 
 
 class Attention(nn.Module):

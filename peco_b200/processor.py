@@ -27,8 +27,6 @@ import math
 from dataclasses import dataclass
 
 import torch
-import torch.nn.functional as F
-from torch.nn.attention import SDPBackend, sdpa_kernel
 
 from . import _native
 from .clustering import kmeans_fit_pair, fit_token_clusters
@@ -68,56 +66,52 @@ class InferenceContext:
 
 
 def dense_attention(query, key, value, valid_length):
-    """Warmup path: full attention over [0, valid) and [valid, S) separately
+    """Warmup path: exact attention within [0, valid) and within [valid, S)
     (peco/processor.py:52-65).
 
-    CUDA fp16/bf16 inputs with D in {64, 128} run on the tcgen05 attention
-    kernel as a two-group partition -- groups [0, valid) and [valid, S), each
-    attending only to itself -- which is exactly the reference's pair of
-    varlen SDPA calls.  Other inputs take the reference's SDPA route."""
-    if (query.is_cuda and query.dtype in (torch.float16, torch.bfloat16) and query.shape[-1] in (64, 128)
-            and key.dtype == query.dtype and value.dtype == query.dtype and key.shape == query.shape
-            and value.shape == query.shape):
-        return _dense_attention_tc(query.contiguous(), key.contiguous(), value.contiguous(), valid_length)
-    output = torch.empty_like(query)
-    backend = SDPBackend.FLASH_ATTENTION if query.is_cuda else SDPBackend.MATH
-    with sdpa_kernel(backend):
-        for start, end in ((0, valid_length), (valid_length, query.shape[2])):
-            if start < end:
-                output[:, :, start:end] = F.scaled_dot_product_attention(
-                    query[:, :, start:end].contiguous(), key[:, :, start:end].contiguous(),
-                    value[:, :, start:end].contiguous(), dropout_p=0.0)
-    return output
-
-
-def _dense_attention_tc(query, key, value, valid_length):
-    """Block-diagonal partition of the sequence into [0, valid) and [valid, S)
-    on the sparse kernel (built on the device, so the call never synchronises
-    and can be captured in a CUDA graph)."""
+    Runs on the tcgen05 attention kernel as a two-group partition whose map
+    is the 2x2 identity -- each group attends only to itself -- built on the
+    device, so the call never synchronises and can be captured in a CUDA
+    graph.  Takes CUDA fp16/bf16 Q/K/V of one shape with D in {64, 128}; there
+    is no CPU path."""
     from .attention_cuda import sparse_attention
+    _native.require_cuda(query, key, value)
+    if query.dtype not in (torch.float16, torch.bfloat16) or key.dtype != query.dtype or value.dtype != query.dtype:
+        raise TypeError("dense_attention takes float16 or bfloat16 Q/K/V of one dtype")
+    if key.shape != query.shape or value.shape != query.shape or query.shape[-1] not in (64, 128):
+        raise ValueError("dense_attention takes Q/K/V of one shape [B, H, S, D] with D in {64, 128}")
     b, h, s, _ = query.shape
     if not 0 <= valid_length <= s:
         raise ValueError("valid_length must lie in [0, S]")
-    sizes = torch.empty((b, h, 2), dtype=torch.int32, device=query.device)
-    sizes[..., 0] = valid_length
-    sizes[..., 1] = s - valid_length
+    sizes = torch.tensor([valid_length, s - valid_length], dtype=torch.int32).to(query.device, non_blocking=True)
+    sizes = sizes.expand(b, h, 2).contiguous()
     groups = torch.eye(2, dtype=torch.bool, device=query.device).expand(b, h, 2, 2).contiguous()
-    return sparse_attention(query, key, value, groups, sizes, sizes, validate_sizes=False)
+    return sparse_attention(query.contiguous(), key.contiguous(), value.contiguous(), groups, sizes, sizes,
+                            validate_sizes=False)
 
 
 def extend_text_partition(dynamic_map, q_sizes, k_sizes, valid_text, text_length):
-    """Append valid-text and padding groups to the video-cluster partition
-    (peco/processor.py:68-84): valid text and video see each other, padding
-    forms its own sequence."""
-    dynamic_map = F.pad(dynamic_map, (0, 2, 0, 2), value=False)
-    dynamic_map[..., -2, :-1] = True
-    dynamic_map[..., :-1, -2] = True
-    dynamic_map[..., -1, -1] = True
-    extra = torch.tensor([valid_text, text_length - valid_text], dtype=torch.int32).to(q_sizes.device,
-                                                                                          non_blocking=True)
-    extra = extra.expand(*q_sizes.shape[:-1], 2)
-    return (dynamic_map.contiguous(), torch.cat((q_sizes, extra), -1).to(torch.int32).contiguous(),
-            torch.cat((k_sizes, extra), -1).to(torch.int32).contiguous())
+    """The video-cluster partition [B, H, CQ, CK] grown by two groups on each
+    side (peco/processor.py:68-84): group CQ / CK is the valid text and group
+    CQ+1 / CK+1 the text padding.  Video clusters and valid text attend to
+    each other, padding attends only to padding.  Returns (map [B, H, CQ+2,
+    CK+2], q sizes [B, H, CQ+2], k sizes [B, H, CK+2]), int32 sizes."""
+    b, h, cq, ck = dynamic_map.shape
+    grown = torch.zeros((b, h, cq + 2, ck + 2), dtype=torch.bool, device=dynamic_map.device)
+    grown[..., :cq, :ck] = dynamic_map
+    grown[..., : cq + 1, ck] = True  # every non-padding row sees the valid text
+    grown[..., cq, : ck + 1] = True  # the valid text sees video and itself
+    grown[..., cq + 1, ck + 1] = True
+    text = torch.tensor([valid_text, text_length - valid_text], dtype=torch.int32).to(q_sizes.device,
+                                                                                       non_blocking=True)
+
+    def with_text(sizes):
+        out = torch.empty((*sizes.shape[:-1], sizes.shape[-1] + 2), dtype=torch.int32, device=sizes.device)
+        out[..., :-2] = sizes
+        out[..., -2:] = text
+        return out
+
+    return grown, with_text(q_sizes), with_text(k_sizes)
 
 
 def _first_tokens_init(x_video, clusters):
@@ -299,46 +293,84 @@ class PecoAttention:
 
     @torch.no_grad()
     def __call__(self, attn, hidden_states, encoder_hidden_states=None, attention_mask=None, image_rotary_emb=None):
-        """diffusers attention-processor entry (peco/processor.py:159-197)."""
-        apply_rotary_emb = _rotary()
-        text_length = 0 if encoder_hidden_states is None else encoder_hidden_states.shape[1]
-        if attn.add_q_proj is None and text_length:
-            hidden_states = torch.cat((hidden_states, encoder_hidden_states), 1)
+        """Attention-processor entry of one HunyuanVideo attention module
+        (drop-in for peco/processor.py:159-197; ``attention_mask`` is unused
+        there too: the text lengths come from the shared context).
 
-        def split_heads(x):
-            return x.unflatten(2, (attn.heads, -1)).transpose(1, 2)
-
-        query, key, value = (split_heads(proj(hidden_states)) for proj in (attn.to_q, attn.to_k, attn.to_v))
-        if attn.norm_q is not None:
-            query = attn.norm_q(query)
-        if attn.norm_k is not None:
-            key = attn.norm_k(key)
+        Each stream is projected with the module's own linear layers (video
+        rows by ``to_q/to_k/to_v``; text rows by ``add_*_proj`` in a
+        dual-stream module, by the same layers in a single-stream one).
+        ``peco_prepare_qkv`` then writes the call's [1, H, S, D] Q/K/V in one
+        pass: head split, the modules' RMSNorm (``norm_q/norm_k``, or
+        ``norm_added_*`` for a dual-stream module's text), the rotary
+        embedding of the video rows and the text rows appended after them.
+        The attention output goes back through ``to_out`` (video) and
+        ``to_add_out`` (text) where the module has them.
+        """
+        _native.require_cuda(hidden_states)
+        n_text = 0 if encoder_hidden_states is None else encoder_hidden_states.shape[1]
+        separate_text = attn.add_q_proj is not None  # dual-stream: text has its own weights
+        heads = attn.heads
+        video_proj = [layer(hidden_states) for layer in (attn.to_q, attn.to_k, attn.to_v)]
+        text_layers = (attn.add_q_proj, attn.add_k_proj, attn.add_v_proj) if separate_text else \
+            (attn.to_q, attn.to_k, attn.to_v)
+        text_proj = [layer(encoder_hidden_states) for layer in text_layers] if n_text else [None] * 3
+        b, n_video, inner = video_proj[0].shape
+        if b != 1:
+            raise ValueError("This minimal HunyuanVideo entry supports one prompt per call")
+        if inner % heads or inner // heads not in (64, 128):
+            raise ValueError("head dimension must be 64 or 128")
+        if any(t is not None and (t.dtype != torch.bfloat16 or t.stride(-1) != 1) for t in video_proj + text_proj):
+            raise TypeError("the fused PECO call takes bfloat16 projections (HunyuanVideo's attention dtype)")
+        dims = inner // heads
+        video_norms = (_rms_gain(attn.norm_q, dims), _rms_gain(attn.norm_k, dims))
+        text_norms = (_rms_gain(attn.norm_added_q, dims), _rms_gain(attn.norm_added_k, dims)) if separate_text \
+            else video_norms
+        cos = sin = None
         if image_rotary_emb is not None:
-            if attn.add_q_proj is None and text_length:
-                query = torch.cat((apply_rotary_emb(query[:, :, :-text_length], image_rotary_emb),
-                                   query[:, :, -text_length:]), 2)
-                key = torch.cat((apply_rotary_emb(key[:, :, :-text_length], image_rotary_emb),
-                                 key[:, :, -text_length:]), 2)
-            else:
-                query, key = (apply_rotary_emb(x, image_rotary_emb) for x in (query, key))
-        if attn.add_q_proj is not None and text_length:
-            eq, ek, ev = (split_heads(proj(encoder_hidden_states))
-                          for proj in (attn.add_q_proj, attn.add_k_proj, attn.add_v_proj))
-            if attn.norm_added_q is not None:
-                eq = attn.norm_added_q(eq)
-            if attn.norm_added_k is not None:
-                ek = attn.norm_added_k(ek)
-            query, key, value = torch.cat((query, eq), 2), torch.cat((key, ek), 2), torch.cat((value, ev), 2)
-        output = self.attention(query.contiguous(), key.contiguous(), value.contiguous())
-        output = output.transpose(1, 2).flatten(2, 3).to(query.dtype)
-        if not text_length:
-            return output, encoder_hidden_states
-        output, encoder_output = output[:, :-text_length], output[:, -text_length:]
+            cos, sin = (t.to(device=hidden_states.device, dtype=torch.float32).reshape(n_video, dims).contiguous()
+                        for t in image_rotary_emb)
+        seq = n_video + n_text
+        q, k, v = (torch.empty((1, heads, seq, dims), dtype=torch.bfloat16, device=hidden_states.device)
+                   for _ in range(3))
+        lib = _native.load()
+        opt = (lambda t: _native.ptr(t) if t is not None else _native.P(0))
+        keep = [t for t in (*video_proj, *text_proj, cos, sin, q, k, v) if t is not None] + \
+            [g for g, _ in (*video_norms, *text_norms) if g is not None]
+        dev = hidden_states.device
+        with torch.cuda.device(dev):
+            st = lib.peco_prepare_qkv(
+                *[_native.ptr(t) for t in video_proj], video_proj[0].stride(1), n_video,
+                *[opt(t) for t in text_proj], text_proj[0].stride(1) if n_text else 0, n_text,
+                opt(video_norms[0][0]), opt(video_norms[1][0]), video_norms[0][1], opt(text_norms[0][0]),
+                opt(text_norms[1][0]), text_norms[0][1], opt(cos), opt(sin), _native.ptr(q), _native.ptr(k),
+                _native.ptr(v), heads, dims, _native.stream_of(dev, *keep))
+        _native.check(st, "peco_prepare_qkv")
+        out = self.attention(q, k, v)
+        rows = out.transpose(1, 2).reshape(1, seq, inner)  # token-major, heads side by side
+        video_out, text_out = rows[:, :n_video], rows[:, n_video:]
+        if not n_text:
+            return video_out, encoder_hidden_states
         if getattr(attn, "to_out", None) is not None:
-            output = attn.to_out[1](attn.to_out[0](output))
+            for layer in attn.to_out:
+                video_out = layer(video_out)
         if getattr(attn, "to_add_out", None) is not None:
-            encoder_output = attn.to_add_out(encoder_output)
-        return output, encoder_output
+            text_out = attn.to_add_out(text_out)
+        return video_out, text_out
+
+
+def _rms_gain(norm, dims):
+    """(fp32 gain [D], eps) of an RMSNorm module, (None, 0.0) without one.
+
+    Any module with ``weight`` and ``eps`` attributes qualifies: the kernel
+    computes x * rsqrt(mean(x^2) + eps) * weight in fp32, rounded once to
+    bf16."""
+    if norm is None:
+        return None, 0.0
+    weight, eps = getattr(norm, "weight", None), getattr(norm, "eps", None)
+    if weight is None or eps is None or weight.numel() != dims:
+        raise TypeError("query/key norms must be RMSNorm modules (per-head ``weight`` and ``eps``)")
+    return weight.detach().float().contiguous(), float(eps)
 
 
 def _rows_view(x):
@@ -347,19 +379,3 @@ def _rows_view(x):
     if x.stride(3) != 1 or x.stride(2) != x.shape[3]:
         x = x.contiguous()
     return x, x.stride(1) // x.shape[3]
-
-
-def _rotary():
-    """diffusers' apply_rotary_emb when installed, else the same rotation
-    (real cos/sin tables, pairs interleaved along the last dim)."""
-    try:
-        from diffusers.models.embeddings import apply_rotary_emb
-        return apply_rotary_emb
-    except Exception:  # diffusers is optional
-        def apply_rotary_emb(x, freqs_cis):
-            cos, sin = freqs_cis
-            cos, sin = cos[None, None].to(x.device), sin[None, None].to(x.device)
-            xr, xi = x.reshape(*x.shape[:-1], -1, 2).unbind(-1)
-            rotated = torch.stack([-xi, xr], dim=-1).flatten(3)
-            return (x.float() * cos + rotated.float() * sin).to(x.dtype)
-        return apply_rotary_emb
