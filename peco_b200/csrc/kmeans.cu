@@ -49,11 +49,15 @@ namespace {
 constexpr int kTileM = 128;
 constexpr int kMaxCand = 4;
 // warp 0: TMA / bulk-copy producer (and the centroid norms of each head);
-// warp 1: MMA issuer and TMEM owner; warps 2-9: epilogue, two warps per TMEM
-// lane quarter, each scanning half of the centroid columns (measured: three
-// or four warps per quarter gain nothing, and four spill registers)
+// warp 1: MMA issuer and TMEM owner; warps 2-9: epilogue in two groups of
+// four, group g taking the CTA's tiles of parity g in accumulator slot g.  A
+// warp owns one TMEM lane quarter (32 tokens) and scans all of their centroid
+// columns, so no warp waits for another's partial result and two tiles are
+// scanned at once (a per-tile clock64 timeline of the earlier split -- two
+// warps per row, half the columns each, merged through shared memory --
+// showed the merge hand-off and its serial tail as the period's largest part)
 constexpr int kEpiWarps = 8;
-constexpr int kParts = kEpiWarps / 4;  // column parts per row
+constexpr int kGroupWarps = 4;  // an epilogue group: one warp per TMEM lane quarter
 constexpr int kMaxASlots = 4;          // token-tile ring depth when a CTA's centroid image leaves room
 constexpr int kMmaWarp = 1, kEpiWarp0 = 2;
 constexpr int kAssignThreads = 32 * (kEpiWarp0 + kEpiWarps);
@@ -199,9 +203,7 @@ struct __align__(8) AssignBars {
   uint64_t g_full, g_free;
   uint64_t a_full[kMaxASlots], a_empty[kMaxASlots];
   uint64_t b_full[2], b_empty[2];
-  uint64_t acc_full[2], acc_empty[2];
-  uint64_t xch_full[2];        // parts 1.. -> part 0 hand-off, per accumulator slot
-  float4 xch[2][kParts - 1][kTileM];  // (best, runner-up, index bits, partial |x|^2)
+  uint64_t acc_full[2], acc_empty[2];  // per accumulator slot = per epilogue group
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -316,10 +318,11 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
   }
   if (f_begin >= f_end) return;
   const AssignSmem S = assign_smem(jobs.job[0].clusters, jobs.njobs > 1 ? jobs.job[1].clusters : 1, jobs.njobs, D, SPLIT);
-  // The token tile in shared memory is read by the MMA, and by the epilogue
-  // only to compute |x| (when no cached norms are given): the exact recompute
-  // of near-ties reads its rows from global memory, so a slot is free for the
-  // next tile as soon as the MMAs (and the |x| pass, if any) are done.
+  // The token tile in shared memory is read by the MMA, and by its epilogue
+  // group only to compute |x| (when no cached norms are given): the exact
+  // recompute of near-ties reads its rows from global memory, so a slot is
+  // free for the next tile as soon as the MMAs (and the |x| pass, if any) are
+  // done.
   const bool epi_reads_a = jobs.job[0].xn_in == nullptr || (jobs.njobs > 1 && jobs.job[1].xn_in == nullptr);
 
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -351,16 +354,15 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
     mbar_init(&sb.g_free, 1 + kEpiWarps);
     for (int i = 0; i < NA; ++i) {
       mbar_init(&sb.a_full[i], 1);
-      // the tile's MMAs always release it; the epilogue warps too when they
-      // read it for the token norms
-      mbar_init(&sb.a_empty[i], 1 + (epi_reads_a ? kEpiWarps : 0));
+      // the tile's MMAs always release it; its epilogue group too when it
+      // reads the tile for the token norms
+      mbar_init(&sb.a_empty[i], 1 + (epi_reads_a ? kGroupWarps : 0));
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sb.b_full[i], 1);
       mbar_init(&sb.b_empty[i], 1);
       mbar_init(&sb.acc_full[i], 1);
-      mbar_init(&sb.acc_empty[i], kEpiWarps);
-      mbar_init(&sb.xch_full[i], kEpiWarps - kEpiWarps / kParts);
+      mbar_init(&sb.acc_empty[i], kGroupWarps);
     }
     sb.abort_flag = 0;
     fence_barrier_init();
@@ -375,8 +377,11 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
   const int a_panel = kTileM * 128;  // bytes per 64-column panel of an A tile
   // group = (problem, head): the centroids in smem change with it
   auto group_of = [&](const Item& it) { return it.j * jobs.bh + it.head; };
-  // the item is its group's last in this CTA (the next is another group, or none)
-  auto last_of_group = [&](long long f, const ItemCursor& cur) { return f + 1 >= f_end || cur.last_in_group(); };
+  // Tiles go in pairs of consecutive items of one group (a single tile where
+  // the group or the range ends): the two tiles' MMAs alternate chunk by
+  // chunk, so each streamed centroid chunk serves both.  Every role derives
+  // the same pairing from its own cursor.
+  auto pair_size = [&](long long f, const ItemCursor& cur) { return (f + 1 < f_end && !cur.last_in_group()) ? 2 : 1; };
 
   if (warp == 0) {
     // ------------------------------------------------ TMA / bulk producer
@@ -391,16 +396,17 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
     cur.start(jobs, f_begin);
     Ring ring;
     ring.n = NA;
-    for (long long f = f_begin; f < f_end && ok; ++f, ++i, cur.next(jobs), ring.next()) {
-      const Item it = cur.it;
-      const AssignJob& J = jobs.job[it.j];
+    for (long long f = f_begin; f < f_end && ok;) {
+      const int np = pair_size(f, cur);
+      const Item it0 = cur.it;
+      const AssignJob& J = jobs.job[it0.j];
       const CenterGeom cg = center_geom(J.clusters, D);
-      const unsigned char* img = J.image + static_cast<long long>(it.head) * cg.nchunks * cg.b_bytes;
-      if (group_of(it) != group) {
+      const unsigned char* img = J.image + static_cast<long long>(it0.head) * cg.nchunks * cg.b_bytes;
+      if (group_of(it0) != group) {
         if (ngroups > 0) ok = mbar_wait_warp(&sb.g_free, (ngroups - 1) & 1, abort_flag, status);
         if (!ok) break;
         // centroid norms (+inf for padding columns) and, when resident, the image
-        const float* nr = J.norms + static_cast<long long>(it.head) * J.clusters;
+        const float* nr = J.norms + static_cast<long long>(it0.head) * J.clusters;
         for (int c = lane; c < ((cg.nchunks * cg.nc + 31) & ~31); c += 32) cn[c] = c < J.clusters ? nr[c] : INFINITY;
         if (lane == 0) {
           mbar_arrive_expect_tx(&sb.g_full, S.resident ? cg.b_bytes : 0);
@@ -410,23 +416,28 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
         } else {
           mbar_arrive(&sb.g_full);
         }
-        group = group_of(it);
+        group = group_of(it0);
         ++ngroups;
       }
-      const int s = ring.s;
-      if (i >= NA) ok = mbar_wait_warp(&sb.a_empty[s], ring.p ^ 1u, abort_flag, status);
-      if (!ok) break;
-      if (lane == 0) {
-        unsigned char* a = base + a_off + s * S.a_bytes;
-        mbar_arrive_expect_tx(&sb.a_full[s], S.a_bytes);
-        const int row = static_cast<int>(static_cast<long long>(it.head) * J.head_rows + static_cast<long long>(it.tile) * kTileM);
+      for (int p = 0; p < np && ok; ++p, ++f, ++i, cur.next(jobs), ring.next()) {
+        const Item it = cur.it;
+        const int s = ring.s;
+        if (i >= NA) ok = mbar_wait_warp(&sb.a_empty[s], ring.p ^ 1u, abort_flag, status);
+        if (!ok) break;
+        if (lane == 0) {
+          unsigned char* a = base + a_off + s * S.a_bytes;
+          mbar_arrive_expect_tx(&sb.a_full[s], S.a_bytes);
+          const int row = static_cast<int>(static_cast<long long>(it.head) * J.head_rows + static_cast<long long>(it.tile) * kTileM);
 #pragma unroll
-        for (int p = 0; p < D / 64; ++p) {
-          tma_load_2d(a + p * a_panel, &maps.xhi[it.j], 64 * p, row, &sb.a_full[s]);
-          if (SPLIT) tma_load_2d(a + kTileM * D * 2 + p * a_panel, &maps.xlo[it.j], 64 * p, row, &sb.a_full[s]);
+          for (int q = 0; q < D / 64; ++q) {
+            tma_load_2d(a + q * a_panel, &maps.xhi[it.j], 64 * q, row, &sb.a_full[s]);
+            if (SPLIT) tma_load_2d(a + kTileM * D * 2 + q * a_panel, &maps.xlo[it.j], 64 * q, row, &sb.a_full[s]);
+          }
         }
+        __syncwarp();
       }
       if (!S.resident) {
+        // each chunk once per pair
         for (int k = 0; k < cg.nchunks && ok; ++k, ++bchunk) {
           const int bs = bchunk % S.nbslots, bu = bchunk / S.nbslots;
           if (bu > 0) ok = mbar_wait_warp(&sb.b_empty[bs], (bu - 1) & 1, abort_flag, status);
@@ -437,88 +448,121 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
               bulk_load(base + bs * S.b_bytes + off, img + static_cast<long long>(k) * cg.b_bytes + off,
                         min(kCopyPiece, cg.b_bytes - off), &sb.b_full[bs]);
           }
+          __syncwarp();
         }
       }
-      __syncwarp();
     }
     __syncwarp();
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------ MMA
     if (lane == 0) {
       bool ok = true;
-      int group = -1, ngroups = 0, bchunk = 0, gacc = 0;
+      int group = -1, ngroups = 0, bchunk = 0;
+      int uses0 = 0, uses1 = 0;  // accumulator slot uses so far
       int i = 0;
       ItemCursor cur;
       cur.start(jobs, f_begin);
       Ring ring;
       ring.n = NA;
-      for (long long f = f_begin; f < f_end && ok; ++f, ++i, cur.next(jobs), ring.next()) {
-        const Item it = cur.it;
-        const CenterGeom cg = center_geom(jobs.job[it.j].clusters, D);
+      for (long long f = f_begin; f < f_end && ok;) {
+        const int np = pair_size(f, cur);
+        const Item it0 = cur.it;
+        const CenterGeom cg = center_geom(jobs.job[it0.j].clusters, D);
         const uint32_t idesc = instr_desc(128, cg.nc, 1, false, false);
-        if (group_of(it) != group) {
+        if (group_of(it0) != group) {
           ok = mbar_wait(&sb.g_full, ngroups & 1, abort_flag, status);
-          group = group_of(it);
+          group = group_of(it0);
           ++ngroups;
         }
-        const int s = ring.s;
-        if (ok) ok = mbar_wait(&sb.a_full[s], ring.p, abort_flag, status);
-        if (!ok) break;
-        const uint32_t a_hi = smem_u32(base + a_off + s * S.a_bytes);
-        const uint32_t a_lo = a_hi + kTileM * D * 2;
-        for (int k = 0; k < cg.nchunks && ok; ++k, ++gacc) {
-          const int as = gacc & 1;
-          if (gacc >= 2) ok = mbar_wait(&sb.acc_empty[as], ((gacc >> 1) - 1) & 1, abort_flag, status);
+        // the pair's ring slots and accumulator slots (slot = tile index parity)
+        int as_of[2] = {i & 1, (i + 1) & 1};
+        int rs_of[2] = {ring.s, 0};
+        uint32_t rp_of[2] = {ring.p, 0};
+        bool last_of[2] = {np == 1 && cur.last_in_group(), false};
+        {
+          Ring r2 = ring;
+          ItemCursor c2 = cur;
+          r2.next();
+          c2.next(jobs);
+          rs_of[1] = r2.s;
+          rp_of[1] = r2.p;
+          if (np == 2) last_of[1] = f + 2 >= f_end || c2.last_in_group();
+        }
+        if (np == 1) last_of[0] = last_of[0] || f + 1 >= f_end;
+#pragma unroll
+        for (int p = 0; p < 2; ++p)
+          if (p < np && ok) ok = mbar_wait(&sb.a_full[rs_of[p]], rp_of[p], abort_flag, status);
+        for (int k = 0; k < cg.nchunks && ok; ++k) {
           int bs = 0;
-          if (ok && !S.resident) {
+          if (!S.resident) {
             bs = bchunk % S.nbslots;
             ok = mbar_wait(&sb.b_full[bs], (bchunk / S.nbslots) & 1, abort_flag, status);
             ++bchunk;
           }
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t b_hi = smem_u32(base + bs * S.b_bytes);
-          const uint32_t b_lo = b_hi + cg.term_bytes;
-          const uint32_t acc = tmem + as * 256;
-          // terms, smallest first: x.c_lo, [x_lo.c_hi], x.c_hi
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off_a = (kk >> 2) * a_panel + (kk & 3) * 32;
-            const uint32_t off_b = (kk >> 2) * cg.panel_bytes + (kk & 3) * 32;
-            umma_ss(acc, smem_desc(a_hi + off_a, 16, 1024), smem_desc(b_lo + off_b, 16, 1024), idesc, kk > 0 ? 1u : 0u);
-          }
-          if (SPLIT) {
+          for (int p = 0; p < 2; ++p) {
+            if (p >= np || !ok) continue;
+            const int as = as_of[p];
+            const int u = as ? uses1 : uses0;
+            if (u > 0) ok = mbar_wait(&sb.acc_empty[as], (u - 1) & 1, abort_flag, status);
+            if (!ok) continue;
+            if (as) ++uses1;
+            else ++uses0;
+            tc_fence_after();
+            const uint32_t a_hi = smem_u32(base + a_off + rs_of[p] * S.a_bytes);
+            const uint32_t a_lo = a_hi + kTileM * D * 2;
+            const uint32_t b_hi = smem_u32(base + bs * S.b_bytes);
+            const uint32_t b_lo = b_hi + cg.term_bytes;
+            const uint32_t acc = tmem + as * 256;
+            // terms, smallest first: x.c_lo, [x_lo.c_hi], x.c_hi
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk) {
               const uint32_t off_a = (kk >> 2) * a_panel + (kk & 3) * 32;
               const uint32_t off_b = (kk >> 2) * cg.panel_bytes + (kk & 3) * 32;
-              umma_ss(acc, smem_desc(a_lo + off_a, 16, 1024), smem_desc(b_hi + off_b, 16, 1024), idesc, 1u);
+              umma_ss(acc, smem_desc(a_hi + off_a, 16, 1024), smem_desc(b_lo + off_b, 16, 1024), idesc, kk > 0 ? 1u : 0u);
+            }
+            if (SPLIT) {
+#pragma unroll
+              for (int kk = 0; kk < D / 16; ++kk) {
+                const uint32_t off_a = (kk >> 2) * a_panel + (kk & 3) * 32;
+                const uint32_t off_b = (kk >> 2) * cg.panel_bytes + (kk & 3) * 32;
+                umma_ss(acc, smem_desc(a_lo + off_a, 16, 1024), smem_desc(b_hi + off_b, 16, 1024), idesc, 1u);
+              }
+            }
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint32_t off_a = (kk >> 2) * a_panel + (kk & 3) * 32;
+              const uint32_t off_b = (kk >> 2) * cg.panel_bytes + (kk & 3) * 32;
+              umma_ss(acc, smem_desc(a_hi + off_a, 16, 1024), smem_desc(b_hi + off_b, 16, 1024), idesc, 1u);
+            }
+            umma_commit(&sb.acc_full[as]);
+            if (k + 1 == cg.nchunks) {
+              umma_commit(&sb.a_empty[rs_of[p]]);
+              if (last_of[p]) umma_commit(&sb.g_free);
             }
           }
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off_a = (kk >> 2) * a_panel + (kk & 3) * 32;
-            const uint32_t off_b = (kk >> 2) * cg.panel_bytes + (kk & 3) * 32;
-            umma_ss(acc, smem_desc(a_hi + off_a, 16, 1024), smem_desc(b_hi + off_b, 16, 1024), idesc, 1u);
-          }
-          umma_commit(&sb.acc_full[as]);
-          if (!S.resident) umma_commit(&sb.b_empty[bs]);
+          if (ok && !S.resident) umma_commit(&sb.b_empty[bs]);
         }
-        if (ok) umma_commit(&sb.a_empty[s]);
-        if (ok && last_of_group(f, cur)) umma_commit(&sb.g_free);
+        for (int p = 0; p < np; ++p, ++f, ++i, cur.next(jobs), ring.next()) {
+        }
       }
       // drain our MMAs before TMEM is released
-      if (gacc > 0) mbar_wait(&sb.acc_full[(gacc - 1) & 1], ((gacc - 1) >> 1) & 1, abort_flag, status);
+      if (uses0 > 0) mbar_wait(&sb.acc_full[0], (uses0 - 1) & 1, abort_flag, status);
+      if (uses1 > 0) mbar_wait(&sb.acc_full[1], (uses1 - 1) & 1, abort_flag, status);
     }
     __syncwarp();
   } else {
     // ------------------------------------------------------------- epilogue
+    // Group g = (warp - 2) / 4 takes the CTA's tiles of parity g: each of its
+    // warps owns one TMEM lane quarter (32 tokens) and scans every centroid
+    // column of its rows, so a tile needs no exchange between warps and the
+    // two groups work on two tiles at once.
     const int quarter = warp & 3;
-    const int part = (warp - kEpiWarp0) >> 2;  // which part of the columns (and of x's dims)
+    const int eg = (warp - kEpiWarp0) >> 2;
     const int r = quarter * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     bool ok = true;
-    int group = -1, ngroups = 0, gacc = 0;
+    int group = -1, ngroups = 0, use = 0;
     float cmax = 0.0f;
     int i = 0;
     ItemCursor cur;
@@ -539,6 +583,13 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
         group = group_of(it);
         ++ngroups;
       }
+      const bool last_in_group = f + 1 >= f_end || cur.last_in_group();
+      if ((i & 1) != eg) {
+        // the other group's tile; this warp's tiles of the group are done
+        if (last_in_group && lane == 0) mbar_arrive(&sb.g_free);
+        __syncwarp();
+        continue;
+      }
       const int s = ring.s;
       // Only a launch whose epilogue reads the tile waits for it (and holds
       // the slot until it has): otherwise the MMA may already have released
@@ -547,39 +598,42 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
       if (epi_reads_a) ok = mbar_wait_warp(&sb.a_full[s], ring.p, abort_flag, status);
       if (!ok) break;
       const unsigned char* a_hi = base + a_off + s * S.a_bytes;
-      // the token norm: cached by an earlier iteration, or this part's share
-      // of |x|^2 (dims [part D/kParts, (part + 1) D/kParts)), merged below
+      // the token norm: cached by an earlier iteration, or computed here
       const int tok_r = it.tile * kTileM + r;
       const bool cached_xn = J.xn_in != nullptr;
-      float xn_cached = 0.0f;
-      if (cached_xn && part == 0 && tok_r < J.tokens) xn_cached = J.xn_in[static_cast<long long>(it.head) * J.tokens + tok_r];
-      float ss = 0.0f;
-      if (!cached_xn)
+      float xn = 0.0f;
+      if (cached_xn) {
+        if (tok_r < J.tokens) xn = J.xn_in[static_cast<long long>(it.head) * J.tokens + tok_r];
+      } else {
+        float ss = 0.0f;
 #pragma unroll 1
-      for (int ch = part * (D / 8) / kParts; ch < (part + 1) * (D / 8) / kParts; ++ch) {
-        const int off = (ch >> 3) * a_panel + r * 128 + (((ch & 7) ^ (r & 7)) << 4);
-        const uint4 u = *reinterpret_cast<const uint4*>(a_hi + off);
-        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
-        float2 lo2[4] = {};
-        if (SPLIT) {
-          const uint4 w = *reinterpret_cast<const uint4*>(a_hi + kTileM * D * 2 + off);
-          const __nv_bfloat162* l2 = reinterpret_cast<const __nv_bfloat162*>(&w);
+        for (int ch = 0; ch < D / 8; ++ch) {
+          const int off = (ch >> 3) * a_panel + r * 128 + (((ch & 7) ^ (r & 7)) << 4);
+          const uint4 u = *reinterpret_cast<const uint4*>(a_hi + off);
+          const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+          float2 lo2[4] = {};
+          if (SPLIT) {
+            const uint4 w = *reinterpret_cast<const uint4*>(a_hi + kTileM * D * 2 + off);
+            const __nv_bfloat162* l2 = reinterpret_cast<const __nv_bfloat162*>(&w);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) lo2[e] = __bfloat1622float2(l2[e]);
-        }
+            for (int e = 0; e < 4; ++e) lo2[e] = __bfloat1622float2(l2[e]);
+          }
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f2 = __bfloat1622float2(h2[e]);
-          const float x0 = f2.x + lo2[e].x, x1 = f2.y + lo2[e].y;
-          ss = fmaf(x0, x0, ss);
-          ss = fmaf(x1, x1, ss);
+          for (int e = 0; e < 4; ++e) {
+            const float2 f2 = __bfloat1622float2(h2[e]);
+            const float x0 = f2.x + lo2[e].x, x1 = f2.y + lo2[e].y;
+            ss = fmaf(x0, x0, ss);
+            ss = fmaf(x1, x1, ss);
+          }
         }
+        xn = sqrtf(ss);
+        if (J.xn_out && tok_r < J.tokens) J.xn_out[static_cast<long long>(it.head) * J.tokens + tok_r] = xn;
       }
       if (epi_reads_a) {  // done with the tile in shared memory
         __syncwarp();
         if (lane == 0) mbar_arrive(&sb.a_empty[s]);
       }
-      float E2 = 0.0f;  // part 0: bound once every part's share of |x|^2 is known
+      const float E2 = 2.0f * (kBoundScale * xn * cmax + kBoundTiny * (cmax * cmax + 2.0f * xn * cmax));
       float best = INFINITY;
       float cd[kMaxCand];
       int ci[kMaxCand];
@@ -614,21 +668,18 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
           overflow = true;
         }
       };
-      for (int k = 0; k < cg.nchunks && ok; ++k, ++gacc) {
-        const int as = gacc & 1;
-        ok = mbar_wait_warp(&sb.acc_full[as], (gacc >> 1) & 1, abort_flag, status);
+      for (int k = 0; k < cg.nchunks && ok; ++k, ++use) {
+        ok = mbar_wait_warp(&sb.acc_full[eg], use & 1, abort_flag, status);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t acc = tmem + as * 256 + lane_off;
+        const uint32_t acc = tmem + eg * 256 + lane_off;
         const float* cnk = cn + k * cg.nc;
         const int nblk = cg.nc / 32 + ((cg.nc & 31) ? 1 : 0);
-        // part p takes blocks [nblk p / kParts, nblk (p + 1) / kParts)
-        const int blo = nblk * part / kParts, bhi = nblk * (part + 1) / kParts;
-        // One pass over this part's blocks: best distance d = |c|^2 - 2 x.c,
-        // its index and the runner-up, in four independent chains (column
-        // j mod 4); 64 columns per TMEM wait.  Block loops stay rolled: the
-        // unrolled body must fit the instruction cache.
-        constexpr int kChains = 8;  // independent compare chains (column j -> chain j % kChains)
+        // One pass over the chunk's columns: best distance d = |c|^2 - 2 x.c,
+        // its index and the runner-up, in independent chains (column j ->
+        // chain j mod kChains); 32 columns per TMEM wait.  The block loop stays
+        // rolled: the unrolled body must fit the instruction cache.
+        constexpr int kChains = 8;
         float b1[kChains], b2[kChains];
         int bi[kChains];
 #pragma unroll
@@ -656,7 +707,7 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
           }
         };
 #pragma unroll 1
-        for (int b = blo; b < bhi; ++b) {
+        for (int b = 0; b < nblk; ++b) {
           uint32_t v[32];
           tmem_ld32_sync(acc + b * 32, v);
           scan_block(v, b);
@@ -668,36 +719,6 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
           m2 = fminf(fminf(m2, b2[e]), fmaxf(m1, b1[e]));
           if (b1[e] < m1 || (b1[e] == m1 && bi[e] < i1)) i1 = bi[e];
           m1 = fminf(m1, b1[e]);
-        }
-        if (part > 0) {
-          // hand this part's result to part 0 and move on
-          sb.xch[as][part - 1][r] = make_float4(m1, m2, __int_as_float(i1), ss);
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) {
-            mbar_arrive(&sb.xch_full[as]);
-            mbar_arrive(&sb.acc_empty[as]);
-          }
-          continue;
-        }
-        ok = mbar_wait_warp(&sb.xch_full[as], (gacc >> 1) & 1, abort_flag, status);
-        if (!ok) break;
-        {
-          // parts in ascending column order, so an equal distance keeps the lower index
-#pragma unroll
-          for (int pp = 0; pp < kParts - 1; ++pp) {
-            const float4 o = sb.xch[as][pp][r];
-            const int oi = __float_as_int(o.z);
-            m2 = fminf(fminf(m2, o.y), fmaxf(m1, o.x));
-            if (o.x < m1 || (o.x == m1 && oi < i1)) i1 = oi;
-            m1 = fminf(m1, o.x);
-            ss += o.w;
-          }
-          if (k == 0) {
-            const float xn = cached_xn ? xn_cached : sqrtf(ss);
-            if (J.xn_out && tok_r < J.tokens) J.xn_out[static_cast<long long>(it.head) * J.tokens + tok_r] = xn;
-            E2 = 2.0f * (kBoundScale * xn * cmax + kBoundTiny * (cmax * cmax + 2.0f * xn * cmax));
-          }
         }
         best = fminf(best, m1);
         const float thr = best + E2;
@@ -733,10 +754,10 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sb.acc_empty[as]);
+        if (lane == 0) mbar_arrive(&sb.acc_empty[eg]);
       }
       if (!ok) break;
-      if (part == 0) {
+      {
         const int tok = it.tile * kTileM + r;
         const bool valid = tok < J.tokens;
         if (ncand > 1) prune(best + E2);
@@ -812,7 +833,7 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
         if (valid) J.labels[static_cast<long long>(it.head) * J.tokens + tok] = label;
       }
       __syncwarp();
-      if (lane == 0 && last_of_group(f, cur)) mbar_arrive(&sb.g_free);
+      if (lane == 0 && last_in_group) mbar_arrive(&sb.g_free);
     }
   }
   __syncwarp();
