@@ -675,58 +675,71 @@ __global__ void __launch_bounds__(kAssignThreads, 1) kmeans_assign_kernel(const 
         const uint32_t acc = tmem + eg * 256 + lane_off;
         const float* cnk = cn + k * cg.nc;
         const int nblk = cg.nc / 32 + ((cg.nc & 31) ? 1 : 0);
-        // One pass over the chunk's columns: best distance d = |c|^2 - 2 x.c,
-        // its index and the runner-up, in independent chains (column j ->
-        // chain j mod kChains); 32 columns per TMEM wait.  The block loop stays
-        // rolled: the unrolled body must fit the instruction cache.
-        constexpr int kChains = 8;
-        float b1[kChains], b2[kChains];
-        int bi[kChains];
-#pragma unroll
-        for (int e = 0; e < kChains; ++e) {
-          b1[e] = INFINITY;
-          b2[e] = INFINITY;
-          bi[e] = 0x7fffffff;
-        }
-        auto scan_block = [&](const uint32_t* v, int b) {
-          const float4* c4 = reinterpret_cast<const float4*>(cnk + b * 32);
-          const int cbase = k * cg.nc + b * 32;
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const float4 nq = c4[q];
-            const float nv[4] = {nq.x, nq.y, nq.z, nq.w};
-#pragma unroll
-            for (int e4 = 0; e4 < 4; ++e4) {
-              const int j = 4 * q + e4, e = j % kChains;
-              const float d = fmaf(-2.0f, __uint_as_float(v[j]), nv[e4]);
-              const bool lt = d < b1[e];
-              b2[e] = fminf(b2[e], fmaxf(d, b1[e]));
-              bi[e] = lt ? cbase + j : bi[e];
-              b1[e] = fminf(b1[e], d);
-            }
-          }
+        // Two passes over the chunk's columns, each value's distance
+        // d = |c|^2 - 2 x.c recomputed identically (one paired FMA per two
+        // columns).  Pass 1: the chunk's best distance (independent min
+        // chains).  Pass 2: how many columns lie within the near-tie
+        // threshold of the running best and, from that count and a weighted
+        // sum of their column numbers, the column itself when it is alone.
+        // Both passes are mostly min / compare / FMA-pipe adds: the compare-
+        // select argmin with a tracked runner-up they replace spent about
+        // five half-rate ALU instructions per value, which bounded the kernel.
+        // The block loops stay rolled: the unrolled body must fit the
+        // instruction cache.
+        auto dist2 = [&](const uint32_t* v, const float4* c4, int q, float2& lo, float2& hi) {
+          const float4 nq = c4[q];
+          const float2 m2 = make_float2(-2.0f, -2.0f);
+          lo = ffma2(make_float2(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1])), m2, make_float2(nq.x, nq.y));
+          hi = ffma2(make_float2(__uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3])), m2, make_float2(nq.z, nq.w));
         };
+        float mins[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) mins[e] = INFINITY;
 #pragma unroll 1
         for (int b = 0; b < nblk; ++b) {
           uint32_t v[32];
           tmem_ld32_sync(acc + b * 32, v);
-          scan_block(v, b);
-        }
-        float m1 = b1[0], m2 = b2[0];
-        int i1 = bi[0];
+          const float4* c4 = reinterpret_cast<const float4*>(cnk + b * 32);
 #pragma unroll
-        for (int e = 1; e < kChains; ++e) {
-          m2 = fminf(fminf(m2, b2[e]), fmaxf(m1, b1[e]));
-          if (b1[e] < m1 || (b1[e] == m1 && bi[e] < i1)) i1 = bi[e];
-          m1 = fminf(m1, b1[e]);
+          for (int q = 0; q < 8; ++q) {
+            float2 lo, hi;
+            dist2(v, c4, q, lo, hi);
+            mins[q] = fminf(mins[q], fminf(fminf(lo.x, lo.y), fminf(hi.x, hi.y)));
+          }
         }
+        float m1 = fminf(fminf(fminf(mins[0], mins[1]), fminf(mins[2], mins[3])),
+                         fminf(fminf(mins[4], mins[5]), fminf(mins[6], mins[7])));
         best = fminf(best, m1);
         const float thr = best + E2;
         if (ncand > 0) prune(thr);
-        // candidates of this chunk: none (m1 > thr), exactly its best
-        // (runner-up > thr), or several -- then rescan it (rare)
-        const bool many = m1 <= thr && m2 <= thr;
-        if (m1 <= thr && !many) push(m1, i1);
+        float count = 0.0f, where = 0.0f;
+        if (__any_sync(0xffffffffu, m1 <= thr)) {
+#pragma unroll 1
+          for (int b = 0; b < nblk; ++b) {
+            uint32_t v[32];
+            tmem_ld32_sync(acc + b * 32, v);
+            const float4* c4 = reinterpret_cast<const float4*>(cnk + b * 32);
+            float2 cnt2 = make_float2(0.0f, 0.0f), pos2 = make_float2(0.0f, 0.0f);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              float2 lo, hi;
+              dist2(v, c4, q, lo, hi);
+              const float2 f_lo = make_float2(lo.x <= thr ? 1.0f : 0.0f, lo.y <= thr ? 1.0f : 0.0f);
+              const float2 f_hi = make_float2(hi.x <= thr ? 1.0f : 0.0f, hi.y <= thr ? 1.0f : 0.0f);
+              cnt2 = fadd2(cnt2, fadd2(f_lo, f_hi));
+              pos2 = ffma2(f_lo, make_float2(4 * q, 4 * q + 1), pos2);
+              pos2 = ffma2(f_hi, make_float2(4 * q + 2, 4 * q + 3), pos2);
+            }
+            const float cnt_b = cnt2.x + cnt2.y;
+            count += cnt_b;
+            where += fmaf(cnt_b, static_cast<float>(k * cg.nc + b * 32), pos2.x + pos2.y);
+          }
+        }
+        // candidates of this chunk: none (m1 > thr), exactly its best (one
+        // column within the threshold), or several -- then rescan it (rare)
+        const bool many = count > 1.5f;
+        const int i1 = static_cast<int>(where);
+        if (count > 0.5f && !many) push(m1, i1);
         if (__any_sync(0xffffffffu, many)) {
 #pragma unroll 1
           for (int b = 0; b < nblk; ++b) {
