@@ -80,3 +80,55 @@ class PecoCallGraph:
                 dst.copy_(src)
         self.graph.replay()
         return self.output
+
+
+class PecoStepGraph:
+    """One denoising step of a PECO-installed transformer, all layers in one
+    CUDA graph: each replay launches every layer's attention call (its whole
+    k-means, selection, quantise/gather and attention sequence) and the model's
+    own kernels in between, so the step costs one graph launch instead of a
+    few thousand kernel launches scheduled from Python.
+
+    ``model`` is the transformer ``peco_b200.model.install_attention`` set up,
+    past its warm-up steps with every processor's centroids cached (one eager
+    step ran).  The context's step counter and text lengths are frozen at
+    capture (its pre-hook, which reads the mask on the host, runs only
+    eagerly); every processor's centroids become fixed tensors that each
+    replay reads as the k-means init and overwrites, so replays chain like
+    eager steps.  ``inputs`` are the forward's positional arguments (CUDA
+    tensors); a replay copies new values into the captured ones.
+    """
+
+    def __init__(self, model, *inputs):
+        processors = getattr(model, "_peco_processors", None)
+        ctx = getattr(model, "_peco_context", None)
+        if not processors or ctx is None:
+            raise ValueError("install PECO attention on the model first (peco_b200.model.install_attention)")
+        for p in processors:
+            cfg = p.config
+            if p.q_centroids is None or ctx.step < cfg.warmup_steps or p.layer_idx < cfg.warmup_layers:
+                raise ValueError("capture a steady-state step: run one eager step past the warm-up first")
+            p.q_centroids = p.q_centroids.float().contiguous().clone()
+            p.k_centroids = p.k_centroids.float().contiguous().clone()
+            p.update_centroids_in_place = True
+        self.model = model
+        self.frozen = (ctx.step, ctx.text_length, ctx.valid_text_length)
+        self.inputs = tuple(t.detach().clone() if torch.is_tensor(t) else t for t in inputs)
+        hook = getattr(model, "_peco_context_hook", None)
+        if hook is not None:
+            hook.remove()
+        self.graph = torch.cuda.CUDAGraph()
+        try:
+            with torch.no_grad(), torch.cuda.graph(self.graph):
+                self.output = model(*self.inputs)
+        finally:
+            if hook is not None:  # put the eager step counter back
+                from .model import _register_context_hook
+                _register_context_hook(model, ctx)
+
+    def __call__(self, *inputs):
+        for dst, src in zip(self.inputs, inputs):
+            if torch.is_tensor(dst) and src.data_ptr() != dst.data_ptr():
+                dst.copy_(src)
+        self.graph.replay()
+        return self.output

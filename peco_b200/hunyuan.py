@@ -18,6 +18,17 @@ architecture matters (weights are random, N(0, 0.02)):
   (head dim split 16 / 56 / 56 over time / height / width);
 * adaLN output norm and un-patchify back to the latent shape.
 
+Head parallelism (``TensorParallel``): rank r of P owns attention heads
+[r H/P, (r+1) H/P) and the matching 1/P of every MLP hidden layer.  Q/K/V
+and the first MLP layers are column slices of the full weights; the output
+projections (``to_out``, ``to_add_out``, the MLPs' second layers, the
+single-stream ``proj_out``) are row slices whose partial products are summed
+by one all-reduce each; embedders, modulation and the final layer are
+replicated.  Every parameter is drawn from a generator seeded by its own
+name, so a sharded model holds exactly the slices of the unsharded one.  The
+PECO processor of a rank clusters and attends only its own heads: per-head
+work needs no communication, as in the reference's per-(batch, head) kernels.
+
 The attention modules expose the attributes the PECO processor reads
 (``heads``, ``to_q``/``to_k``/``to_v``, ``norm_q``/``norm_k``,
 ``add_q_proj``... for the text stream, ``to_out``, ``to_add_out``) and call
@@ -28,9 +39,11 @@ attention_mask, image_rotary_emb)`` (peco/processor.py:159-197).
 from __future__ import annotations
 
 import math
+import zlib
 from dataclasses import dataclass
 
 import torch
+import torch.distributed as dist
 import torch.nn as nn
 import torch.nn.functional as F
 
@@ -51,6 +64,62 @@ class HunyuanConfig:
     patch: tuple = (1, 2, 2)
     rope_axes: tuple = (16, 56, 56)
     rope_theta: float = 256.0
+
+
+class TensorParallel:
+    """Head-parallel placement: this process is ``rank`` of ``world`` in ``group``."""
+
+    def __init__(self, rank: int = 0, world: int = 1, group=None):
+        if world < 1 or not 0 <= rank < world:
+            raise ValueError("rank must lie in [0, world)")
+        self.rank, self.world, self.group = rank, world, group
+
+    def span(self, full: int) -> tuple:
+        """(start, stop) of this rank's equal share of ``full`` features."""
+        if full % self.world:
+            raise ValueError(f"{full} features do not split over {self.world} ranks")
+        n = full // self.world
+        return self.rank * n, (self.rank + 1) * n
+
+
+SINGLE = TensorParallel()
+
+
+def _shard(param, full_shape, rows=None, cols=None):
+    """Record how ``param`` is cut from the full tensor: ``rows`` a (start,
+    stop) range of dim 0, ``cols`` a list of ranges of dim 1, concatenated."""
+    param.full_shape = tuple(full_shape)
+    param.shard_rows = rows
+    param.shard_cols = cols
+    return param
+
+
+def column_linear(dim_in, dim_out, tp: TensorParallel):
+    """nn.Linear holding this rank's rows (output features) of a [dim_out, dim_in] layer."""
+    a, b = tp.span(dim_out)
+    layer = nn.Linear(dim_in, b - a)
+    _shard(layer.weight, (dim_out, dim_in), rows=(a, b))
+    _shard(layer.bias, (dim_out,), rows=(a, b))
+    return layer
+
+
+class RowParallelLinear(nn.Module):
+    """y = sum over ranks of x_r W_r^T, plus the bias: each rank holds the
+    weight columns of its input features (``cols``, ranges of the full input)
+    and one all-reduce adds the partial products."""
+
+    def __init__(self, dim_out, full_in, cols, tp: TensorParallel):
+        super().__init__()
+        local = sum(b - a for a, b in cols)
+        self.tp = tp
+        self.weight = _shard(nn.Parameter(torch.empty(dim_out, local)), (dim_out, full_in), cols=list(cols))
+        self.bias = _shard(nn.Parameter(torch.empty(dim_out)), (dim_out,))
+
+    def forward(self, x):
+        y = F.linear(x, self.weight)
+        if self.tp.world > 1:
+            dist.all_reduce(y, group=self.tp.group)
+        return y + self.bias
 
 
 class RMSNorm(nn.Module):
@@ -132,23 +201,24 @@ def rotate_pairs(x, cos, sin):
 
 
 class Attention(nn.Module):
-    """Projections and norms of one attention layer; the math is the processor's."""
+    """Projections and norms of one attention layer (this rank's heads); the math is the processor's."""
 
-    def __init__(self, dim, heads, head_dim, joint_text: bool, pre_only: bool):
+    def __init__(self, dim, heads, head_dim, joint_text: bool, pre_only: bool, tp: TensorParallel = SINGLE):
         super().__init__()
         inner = heads * head_dim
-        self.heads = heads
-        self.to_q, self.to_k, self.to_v = (nn.Linear(dim, inner) for _ in range(3))
+        lo, hi = tp.span(inner)
+        self.heads = heads // tp.world
+        self.to_q, self.to_k, self.to_v = (column_linear(dim, inner, tp) for _ in range(3))
         self.norm_q, self.norm_k = RMSNorm(head_dim), RMSNorm(head_dim)
         if joint_text:
-            self.add_q_proj, self.add_k_proj, self.add_v_proj = (nn.Linear(dim, inner) for _ in range(3))
+            self.add_q_proj, self.add_k_proj, self.add_v_proj = (column_linear(dim, inner, tp) for _ in range(3))
             self.norm_added_q, self.norm_added_k = RMSNorm(head_dim), RMSNorm(head_dim)
-            self.to_add_out = nn.Linear(inner, dim)
+            self.to_add_out = RowParallelLinear(dim, inner, [(lo, hi)], tp)
         else:
             self.add_q_proj = self.add_k_proj = self.add_v_proj = None
             self.norm_added_q = self.norm_added_k = None
             self.to_add_out = None
-        self.to_out = None if pre_only else nn.ModuleList([nn.Linear(inner, dim), nn.Identity()])
+        self.to_out = None if pre_only else nn.ModuleList([RowParallelLinear(dim, inner, [(lo, hi)], tp), nn.Identity()])
         self.processor = None
 
     def set_processor(self, processor):
@@ -158,19 +228,21 @@ class Attention(nn.Module):
         return self.processor(self, hidden_states, encoder_hidden_states, attention_mask, image_rotary_emb)
 
 
-def _mlp(dim, ratio):
-    return nn.Sequential(nn.Linear(dim, dim * ratio), nn.GELU(approximate="tanh"), nn.Linear(dim * ratio, dim))
+def _mlp(dim, ratio, tp: TensorParallel = SINGLE):
+    hidden = dim * ratio
+    return nn.Sequential(column_linear(dim, hidden, tp), nn.GELU(approximate="tanh"),
+                         RowParallelLinear(dim, hidden, [tp.span(hidden)], tp))
 
 
 class DualStreamBlock(nn.Module):
-    def __init__(self, cfg: HunyuanConfig):
+    def __init__(self, cfg: HunyuanConfig, tp: TensorParallel = SINGLE):
         super().__init__()
         d = cfg.hidden
         self.img_mod = nn.Linear(d, 6 * d)
         self.txt_mod = nn.Linear(d, 6 * d)
-        self.attn = Attention(d, cfg.heads, cfg.head_dim, joint_text=True, pre_only=False)
-        self.ff = _mlp(d, cfg.mlp_ratio)
-        self.ff_context = _mlp(d, cfg.mlp_ratio)
+        self.attn = Attention(d, cfg.heads, cfg.head_dim, joint_text=True, pre_only=False, tp=tp)
+        self.ff = _mlp(d, cfg.mlp_ratio, tp)
+        self.ff_context = _mlp(d, cfg.mlp_ratio, tp)
 
     def forward(self, img, txt, temb, rope):
         e = F.silu(temb)
@@ -185,13 +257,17 @@ class DualStreamBlock(nn.Module):
 
 
 class SingleStreamBlock(nn.Module):
-    def __init__(self, cfg: HunyuanConfig):
+    def __init__(self, cfg: HunyuanConfig, tp: TensorParallel = SINGLE):
         super().__init__()
         d = cfg.hidden
+        inner, hidden = cfg.heads * cfg.head_dim, cfg.mlp_ratio * d
         self.mod = nn.Linear(d, 3 * d)
-        self.attn = Attention(d, cfg.heads, cfg.head_dim, joint_text=False, pre_only=True)
-        self.proj_mlp = nn.Linear(d, cfg.mlp_ratio * d)
-        self.proj_out = nn.Linear(d + cfg.mlp_ratio * d, d)
+        self.attn = Attention(d, cfg.heads, cfg.head_dim, joint_text=False, pre_only=True, tp=tp)
+        self.proj_mlp = column_linear(d, hidden, tp)
+        # input = [attention rows (inner) | MLP hidden (hidden)]: this rank's slice of each
+        a, b = tp.span(inner)
+        c, e = tp.span(hidden)
+        self.proj_out = RowParallelLinear(d, inner + hidden, [(a, b), (inner + c, inner + e)], tp)
 
     def forward(self, img, txt, temb, rope):
         n_txt = txt.shape[1]
@@ -225,27 +301,37 @@ def rope_3d(grid, axes, theta, device):
 
 
 class HunyuanVideoTransformer(nn.Module):
-    def __init__(self, cfg: HunyuanConfig = HunyuanConfig()):
+    def __init__(self, cfg: HunyuanConfig = HunyuanConfig(), tp: TensorParallel = SINGLE):
         super().__init__()
         self.cfg = cfg
+        self.tp = tp
         d = cfg.hidden
         self.x_embedder = nn.Conv3d(cfg.in_channels, d, kernel_size=cfg.patch, stride=cfg.patch)
         self.context_embedder = nn.Linear(cfg.text_dim, d)
         self.time_in = nn.Sequential(nn.Linear(256, d), nn.SiLU(), nn.Linear(d, d))
         self.vector_in = nn.Sequential(nn.Linear(cfg.pooled_dim, d), nn.SiLU(), nn.Linear(d, d))
-        self.transformer_blocks = nn.ModuleList(DualStreamBlock(cfg) for _ in range(cfg.dual_blocks))
-        self.single_transformer_blocks = nn.ModuleList(SingleStreamBlock(cfg) for _ in range(cfg.single_blocks))
+        self.transformer_blocks = nn.ModuleList(DualStreamBlock(cfg, tp) for _ in range(cfg.dual_blocks))
+        self.single_transformer_blocks = nn.ModuleList(SingleStreamBlock(cfg, tp) for _ in range(cfg.single_blocks))
         self.norm_out = nn.Linear(d, 2 * d)
         self.proj_out = nn.Linear(d, cfg.in_channels * math.prod(cfg.patch))
 
     @torch.no_grad()
     def init_random(self, std=0.02, seed=0):
-        """Weights ~N(0, std) drawn on the parameters' device, biases 0, RMSNorm gains 1."""
+        """Weights ~N(0, std) drawn on the parameters' device, biases 0, RMSNorm
+        gains 1.  Each weight comes from a generator seeded by (seed, its name)
+        and is drawn at its full unsharded shape, then cut to this rank's
+        slice, so every placement holds slices of the same model."""
         dev = next(self.parameters()).device
-        g = torch.Generator(device=dev).manual_seed(seed)
         for name, p in self.named_parameters():
             if p.ndim > 1:
-                p.copy_(torch.randn(p.shape, generator=g, device=dev, dtype=torch.float32).mul_(std))
+                g = torch.Generator(device=dev).manual_seed(seed * 1000003 + zlib.crc32(name.encode()))
+                full = torch.randn(getattr(p, "full_shape", p.shape), generator=g, device=dev, dtype=torch.float32)
+                rows, cols = getattr(p, "shard_rows", None), getattr(p, "shard_cols", None)
+                if rows is not None:
+                    full = full[rows[0]:rows[1]]
+                if cols is not None:
+                    full = torch.cat([full[:, a:b] for a, b in cols], 1)
+                p.copy_(full.mul_(std))
             elif name.endswith("norm_q.weight") or name.endswith("norm_k.weight") or "norm_added" in name:
                 p.fill_(1.0)
             else:
@@ -260,7 +346,11 @@ class HunyuanVideoTransformer(nn.Module):
         img = self.x_embedder(hidden_states).flatten(2).transpose(1, 2)
         txt = self.context_embedder(encoder_hidden_states)
         temb = self.time_in(_timestep_embedding(timestep).to(img.dtype)) + self.vector_in(pooled_projections)
-        rope = rope_3d(grid, self.cfg.rope_axes, self.cfg.rope_theta, img.device)
+        key = (grid, img.device)
+        rope = self._rope.get(key) if hasattr(self, "_rope") else None
+        if rope is None:  # built once per grid (host tables copied to the device)
+            rope = rope_3d(grid, self.cfg.rope_axes, self.cfg.rope_theta, img.device)
+            self._rope = {key: rope}
         for block in self.transformer_blocks:
             img, txt = block(img, txt, temb, rope)
         for block in self.single_transformer_blocks:
@@ -271,11 +361,21 @@ class HunyuanVideoTransformer(nn.Module):
         return out.reshape(b, c, t, h, w)
 
 
-def build_transformer(cfg: HunyuanConfig = HunyuanConfig(), device="cuda", dtype=torch.bfloat16, seed=0):
-    """Random-init model built straight on ``device`` (no default initialisation pass)."""
+def build_transformer(cfg: HunyuanConfig = HunyuanConfig(), device="cuda", dtype=torch.bfloat16, seed=0,
+                      tp: TensorParallel = SINGLE):
+    """Random-init model (this rank's shard under ``tp``) built straight on
+    ``device`` (no default initialisation pass)."""
+    if cfg.heads % tp.world or (cfg.hidden * cfg.mlp_ratio) % tp.world:
+        raise ValueError(f"{cfg.heads} heads / {cfg.hidden * cfg.mlp_ratio} MLP units do not split over {tp.world} ranks")
     with torch.device("meta"):
-        model = HunyuanVideoTransformer(cfg)
+        model = HunyuanVideoTransformer(cfg, tp)
+    shard_info = {n: (getattr(p, "full_shape", None), getattr(p, "shard_rows", None), getattr(p, "shard_cols", None))
+                  for n, p in model.named_parameters()}
     model = model.to_empty(device=device).to(dtype)
+    for n, p in model.named_parameters():  # to_empty/to() make new parameters: keep the shard records
+        full_shape, rows, cols = shard_info[n]
+        if full_shape is not None:
+            _shard(p, full_shape, rows, cols)
     return model.init_random(seed=seed).eval()
 
 

@@ -48,6 +48,14 @@ def install_attention(pipe, config: PecoConfig) -> InferenceContext:
     for index, block in enumerate(layers):
         processors.append(PecoAttention(index, config, context))
         block.attn.set_processor(processors[-1])
+    model._peco_context = context
+    model._peco_processors = processors
+    _register_context_hook(model, context)
+    return context
+
+
+def _register_context_hook(model, context: InferenceContext) -> None:
+    """Forward pre-hook: advance the step and read the text lengths from the mask."""
     bind = inspect.signature(model.forward).bind_partial
 
     def before_forward(_module, args, kwargs):
@@ -57,9 +65,6 @@ def install_attention(pipe, config: PecoConfig) -> InferenceContext:
         context.valid_text_length = valid
 
     model._peco_context_hook = model.register_forward_pre_hook(before_forward, with_kwargs=True)
-    model._peco_context = context
-    model._peco_processors = processors
-    return context
 
 
 def reset_state(pipe) -> None:

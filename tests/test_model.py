@@ -92,3 +92,93 @@ def test_peco_steps_match_dense_when_every_pair_is_kept():
     assert torch.isfinite(g).all()
     cos = torch.nn.functional.cosine_similarity(g, r, dim=0).item()
     assert cos >= 0.999, cos
+
+
+def _free_port():
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _tensor_parallel_worker(rank, world, port, out_q):
+    import os
+
+    import torch.distributed as dist
+
+    from peco_b200.hunyuan import TensorParallel
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        cfg = HunyuanConfig(hidden=256, heads=4, head_dim=64, dual_blocks=2, single_blocks=2, text_dim=64,
+                            pooled_dim=32, rope_axes=(16, 24, 24))
+        full = build_transformer(cfg, device="cpu", dtype=torch.float32)
+        part = build_transformer(cfg, device="cpu", dtype=torch.float32, tp=TensorParallel(rank, world))
+        ctx = InferenceContext(step=0, text_length=16, valid_text_length=12)
+        use_dense_attention(full, ctx)
+        use_dense_attention(part, ctx)
+        g = torch.Generator().manual_seed(0)
+        x = torch.randn(1, 16, 2, 8, 8, generator=g)
+        txt = torch.randn(1, 16, 64, generator=g)
+        mask = torch.zeros(1, 16, dtype=torch.bool)
+        mask[0, :12] = True
+        pooled = torch.randn(1, 32, generator=g)
+        t = torch.tensor([500.0])
+        with torch.no_grad():
+            want = full(x, t, txt, mask, pooled)
+            got = part(x, t, txt, mask, pooled)
+        heads = part.transformer_blocks[0].attn.heads
+        out_q.put((rank, bool(torch.allclose(got, want, atol=1e-4, rtol=1e-4)) and heads == 4 // world))
+    except Exception as e:  # report instead of leaving the other ranks waiting
+        out_q.put((rank, repr(e)))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_head_parallel_model_equals_unsharded(world):
+    """Heads and MLP units sharded over gloo ranks (column slices in, row slices
+    plus an all-reduce out) reproduce the unsharded model's output."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_tensor_parallel_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    assert all(results[r] is True for r in range(world)), results
+    assert all(p.exitcode == 0 for p in procs)
+
+
+@pytest.mark.gpu
+def test_step_graph_replays_the_eager_step():
+    """A steady-state step captured whole (every layer's PECO call and the
+    model's kernels) replays bit-identically to the eager step, and keeps
+    chaining the centroids like eager steps do."""
+    from peco_b200.graph import PecoStepGraph
+    cfg = PecoConfig(num_q_centroids=8, num_k_centroids=16, top_p=0.5, min_kc_ratio=0.25, kmeans_iter_init=3,
+                     kmeans_iter_step=2, warmup_steps=1, base_offset_bits=4)
+    models = [build_transformer(TINY, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
+    ctxs = [install_attention(Pipe(m), cfg) for m in models]
+    x, t, txt, mask, pooled = _inputs("cuda", torch.bfloat16, frames=2, size=16)
+    with torch.no_grad():
+        for m in models:
+            torch.manual_seed(0)  # the first fit draws its initial centroids at random
+            m(x, t, txt, mask, pooled)  # dense warm-up step, centroids initialised
+            m(x, t, txt, mask, pooled)  # first sparse step
+    graph = PecoStepGraph(models[1], x, t, txt, mask, pooled)
+    for i in range(2):
+        x2 = x + 0.01 * (i + 1)
+        with torch.no_grad():
+            want = models[0](x2, t, txt, mask, pooled)
+        got = graph(x2, t, txt, mask, pooled)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want)
+        for p0, p1 in zip(models[0]._peco_processors, models[1]._peco_processors):
+            assert torch.equal(p0.q_centroids, p1.q_centroids) and torch.equal(p0.k_centroids, p1.k_centroids)
+    assert ctxs[1].step == 1  # the graph does not advance the eager step counter
