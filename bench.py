@@ -189,7 +189,8 @@ def run_ulysses(args, world, rank, local, steps=None, warmup=None, config=None):
     time per step (max over ranks) is the whole job's time."""
     import torch
     from peco_b200 import _native, synthetic
-    from peco_b200.distributed import heads_to_seq, seq_to_heads, seq_to_heads_async
+    from peco_b200 import distributed as pdist
+    from peco_b200.distributed import SLOT_K, SLOT_Q, SLOT_V, heads_to_seq, seq_to_heads, seq_to_heads_async
 
     steps = args.steps if steps is None else steps
     warmup = args.warmup if warmup is None else warmup
@@ -211,10 +212,10 @@ def run_ulysses(args, world, rank, local, steps=None, warmup=None, config=None):
         proc.q_centroids, proc.k_centroids = q_init, k_init
         rec = (lambda n: evs[n].record()) if evs else (lambda n: None)
         rec("start")
-        q = seq_to_heads(q_sh)
+        q = seq_to_heads(q_sh, slot=SLOT_Q)
         rec("q_in")
-        k, k_wait = seq_to_heads_async(k_sh)
-        v, v_wait = seq_to_heads_async(v_sh)
+        k, k_wait = seq_to_heads_async(k_sh, slot=SLOT_K)
+        v, v_wait = seq_to_heads_async(v_sh, slot=SLOT_V)
 
         def k_ready():
             rec("k0")
@@ -284,8 +285,10 @@ def run_ulysses(args, world, rank, local, steps=None, warmup=None, config=None):
             "workload": f"{w.name}: {h} heads x {s} tokens ({nv} video + {w.text_length} text), d={d}, "
                         f"CQ={w.q_clusters}, CK={w.k_clusters}, {w.iters} Lloyd iterations, top-{w.top_k}, "
                         f"{w.bits}-bit Base-Offset",
-            "parallelism": f"ulysses: tokens sequence-sharded over {world} rank(s), point-to-point NCCL exchanges to "
-                           f"{hl} heads per rank and back; K's exchange overlaps Q's k-means, V's both",
+            "parallelism": f"ulysses: tokens sequence-sharded over {world} rank(s), exchanged to {hl} heads per "
+                           f"rank and back ({pdist.last_transport or 'none'}: "
+                           f"{'stores into peer memory over NVLink' if pdist.last_transport == 'peer-memory' else 'point-to-point transfers'}); "
+                           "K's exchange overlaps Q's k-means, V's both",
             "l2": "flushed before every step (256 MB write), outside the step events",
         },
         "stages": {

@@ -216,6 +216,25 @@ int peco_prepare_qkv(const void* vq, const void* vk, const void* vv, long long v
                      float eps_t, const float* cos, const float* sin, void* q, void* k, void* v, int heads,
                      int dims, void* stream);
 
+/* Sequence <-> head reshard of sequence-sharded attention over NVLink peer
+ * memory (no counterpart in the reference, which runs on one GPU; it replaces
+ * the NCCL all-to-all of the long-video configuration).  ``buffers`` and
+ * ``flags`` are device arrays of every rank's receive buffer and flag array
+ * (int64 [slots][world]) as mapped in this process (torch symmetric memory).
+ * peco_exchange_put copies ``pieces`` contiguous blocks of ``piece_bytes``
+ * (16-byte multiple) from src + src_offsets[i] to rank dst_ranks[i]'s buffer
+ * + dst_offsets[i] with plain stores, then sets this rank's entry of slot
+ * ``flag_slot`` in every rank's flag array to ``epoch``; ``done_counter`` is a
+ * zeroed device unsigned the launch uses and resets.  peco_exchange_wait
+ * makes ``stream`` wait until every rank's entry of the slot in this rank's
+ * flag array has reached ``epoch`` (bounded: on expiry the device status word
+ * records a timeout). */
+int peco_exchange_put(const void* src, const long long* src_offsets, const int* dst_ranks,
+                      const long long* dst_offsets, long long piece_bytes, int pieces,
+                      const unsigned long long* buffers, const unsigned long long* flags, int flag_slot,
+                      int rank, int world, long long epoch, unsigned* done_counter, void* stream);
+int peco_exchange_wait(const long long* flags, int world, int flag_slot, long long epoch, void* stream);
+
 /* ---- diagnostics --------------------------------------------------------- */
 
 /* Copies the device status word of the current device to *out (synchronising

@@ -39,6 +39,8 @@ _SIGNATURES = {
     "peco_pack_key_blocks": [P] * 5 + [I] * 6 + [P],
     "peco_sparse_attention_restore": [P] * 5 + [I] * 6 + [P, I, P],
     "peco_prepare_qkv": [P, P, P, LL, I, P, P, P, LL, I, P, P, F, P, P, F, P, P, P, P, P, I, I, P],
+    "peco_exchange_put": [P, P, P, P, LL, I, P, P, I, I, I, LL, P, P],
+    "peco_exchange_wait": [P, I, I, LL, P],
     "peco_attention_workspace_stride": [I, I, I, I],
     "peco_key_block_rows": [I, I],
     "peco_kmeans_work_floats": [I, I, I],
