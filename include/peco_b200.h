@@ -133,10 +133,12 @@ long long peco_kmeans_work_floats(int clusters, int dims, int tokens);
 /* Boolean map [BH,CQ,CK] of kept (query cluster, key cluster) pairs: stable
  * descending sort of softmax(Cq.Ck^T/sqrt(D) + log count_k), keep while the
  * mass before < top_p (all if top_p == 1), the first, and the first
- * ``minimum``; AND nonempty.  Replaces peco/clustering.py:139-186. */
+ * ``minimum``; AND nonempty.  ``logits``: fp32 [BH,CQ,CK] scratch of the
+ * caller, or null for stream-ordered scratch of the call.  Replaces
+ * peco/clustering.py:139-186. */
 int peco_select_cluster_connections(const float* q_centroids, const float* k_centroids, const int32_t* q_sizes,
                                     const int32_t* k_sizes, uint8_t* map, int bh, int cq, int ck, int dims,
-                                    float top_p, int minimum, void* stream);
+                                    float top_p, int minimum, float* logits, void* stream);
 
 /* Same selection written straight into the text-extended map
  * [BH,CQ+2,CK+2] with extended sizes [BH,CQ+2]/[BH,CK+2].
@@ -144,7 +146,7 @@ int peco_select_cluster_connections(const float* q_centroids, const float* k_cen
 int peco_select_text_partition(const float* q_centroids, const float* k_centroids, const int32_t* q_sizes,
                                const int32_t* k_sizes, uint8_t* map_ext, int32_t* q_sizes_ext,
                                int32_t* k_sizes_ext, int bh, int cq, int ck, int dims, float top_p, int minimum,
-                               int valid_text, int text_length, void* stream);
+                               int valid_text, int text_length, float* logits, void* stream);
 
 /* Base-Offset PE over [BH,N,D] (dtype 0 fp16, 1 bf16, 2 fp32; D in {64,128};
  * bits 4 or 8).  mode 0: out = fake-quantized x; mode 1: codes uint8

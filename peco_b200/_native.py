@@ -31,8 +31,8 @@ _SIGNATURES = {
     "peco_sparse_attention": [P] * 8 + [I] * 7 + [P],
     "peco_sort_labels": [P] * 4 + [I] * 3 + [P],
     "peco_kmeans_fit": [P, LL, I, I, P, P, P, P, P, P, P, P, P, LL, I, I, P, P, P, P, P, P, P, P, I, I, I, P],
-    "peco_select_cluster_connections": [P] * 5 + [I] * 4 + [F, I, P],
-    "peco_select_text_partition": [P] * 7 + [I] * 4 + [F, I, I, I, P],
+    "peco_select_cluster_connections": [P] * 5 + [I] * 4 + [F, I, P, P],
+    "peco_select_text_partition": [P] * 7 + [I] * 4 + [F, I, I, I, P, P],
     "peco_base_offset": [I] + [P] * 7 + [I] * 6 + [P],
     "peco_quantize_gather": [P] * 12 + [I] * 7 + [P, I, I, P],
     "peco_attention_plan": [P] * 6 + [I] * 6 + [P],

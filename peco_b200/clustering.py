@@ -215,6 +215,6 @@ def select_cluster_connections(query_centroids, key_centroids, q_cluster_sizes, 
     with torch.cuda.device(dev):
         status = lib.peco_select_cluster_connections(
             _native.ptr(qc), _native.ptr(kc), _native.ptr(qs), _native.ptr(ks), _native.ptr(out), b * h, cq, ck, d,
-            float(p), int(minimum), _native.stream_of(dev, qc, kc, qs, ks, out))
+            float(p), int(minimum), _native.P(0), _native.stream_of(dev, qc, kc, qs, ks, out))
     _native.check(status, "peco_select_cluster_connections")
     return out

@@ -55,7 +55,7 @@ int launch_stable_sort_jobs(const SortJobInput* jobs, int njobs, cudaStream_t st
 
 int launch_select(const float* qc, const float* kc, const int32_t* qs, const int32_t* ks, uint8_t* map, int bh,
                   int cq, int ck, int dims, float top_p, int minimum, int extend, int valid_text, int text_length,
-                  int32_t* q_ext, int32_t* k_ext, cudaStream_t stream);
+                  int32_t* q_ext, int32_t* k_ext, float* logits, cudaStream_t stream);
 
 // ---------------------------------------------------------------------------
 // Attention plan and key blocks

@@ -329,7 +329,7 @@ __global__ void text_partition_kernel(uint8_t* __restrict__ map, const int32_t* 
 
 int launch_select(const float* qc, const float* kc, const int32_t* qs, const int32_t* ks, uint8_t* map, int bh,
                   int cq, int ck, int dims, float top_p, int minimum, int extend, int valid_text, int text_length,
-                  int32_t* q_ext, int32_t* k_ext, cudaStream_t stream) {
+                  int32_t* q_ext, int32_t* k_ext, float* logits_in, cudaStream_t stream) {
   if (bh < 1 || bh > 65535 || cq < 1 || ck < 1 || cq > 65535) return kErrInvalidValue;
   if (dims != 64 && dims != 128) return kErrUnsupported;
   if ((reinterpret_cast<uintptr_t>(qc) | reinterpret_cast<uintptr_t>(kc)) & 15) return kErrInvalidValue;
@@ -337,11 +337,14 @@ int launch_select(const float* qc, const float* kc, const int32_t* qs, const int
   while (np2 < ck) np2 <<= 1;
   const size_t row_smem = (sizeof(unsigned long long) + sizeof(float)) * static_cast<size_t>(np2);
   if (row_smem > 200 * 1024) return kErrUnsupported;
-  // logits in stream-ordered scratch of this call
+  // logits in the caller's buffer, else in stream-ordered scratch of this call
   void* scratch = nullptr;
-  cudaError_t e = cudaMallocAsync(&scratch, sizeof(float) * static_cast<size_t>(bh) * cq * ck, stream);
-  if (e != cudaSuccess) return static_cast<int>(e);
-  float* logits = static_cast<float*>(scratch);
+  cudaError_t e = cudaSuccess;
+  if (!logits_in) {
+    e = cudaMallocAsync(&scratch, sizeof(float) * static_cast<size_t>(bh) * cq * ck, stream);
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
+  float* logits = logits_in ? logits_in : static_cast<float*>(scratch);
   const size_t tile_smem = sizeof(float) * 2 * kTile * dims;
   dim3 sgrid((ck + kTile - 1) / kTile, (cq + kTile - 1) / kTile, bh);
   int rc = 0;
@@ -375,8 +378,10 @@ int launch_select(const float* qc, const float* kc, const int32_t* qs, const int
     }
     rc = launch_status();
   }
-  e = cudaFreeAsync(scratch, stream);
-  if (!rc && e != cudaSuccess) rc = static_cast<int>(e);
+  if (scratch) {
+    e = cudaFreeAsync(scratch, stream);
+    if (!rc && e != cudaSuccess) rc = static_cast<int>(e);
+  }
   if (rc || !extend) return rc;
   text_partition_kernel<<<bh, 256, 0, stream>>>(map, qs, ks, q_ext, k_ext, cq, ck, valid_text, text_length);
   return launch_status();
@@ -387,19 +392,20 @@ int launch_select(const float* qc, const float* kc, const int32_t* qs, const int
 extern "C" int peco_select_cluster_connections(const float* q_centroids, const float* k_centroids,
                                                const int32_t* q_sizes, const int32_t* k_sizes, uint8_t* map,
                                                int bh, int cq, int ck, int dims, float top_p, int minimum,
-                                               void* stream) {
+                                               float* logits, void* stream) {
   if (!(top_p >= 0.0f && top_p <= 1.0f) || minimum < 0) return peco::kErrInvalidValue;
   return peco::launch_select(q_centroids, k_centroids, q_sizes, k_sizes, map, bh, cq, ck, dims, top_p, minimum, 0,
-                             0, 0, nullptr, nullptr, static_cast<cudaStream_t>(stream));
+                             0, 0, nullptr, nullptr, logits, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int peco_select_text_partition(const float* q_centroids, const float* k_centroids,
                                           const int32_t* q_sizes, const int32_t* k_sizes, uint8_t* map_ext,
                                           int32_t* q_sizes_ext, int32_t* k_sizes_ext, int bh, int cq, int ck,
                                           int dims, float top_p, int minimum, int valid_text, int text_length,
-                                          void* stream) {
+                                          float* logits, void* stream) {
   if (!(top_p >= 0.0f && top_p <= 1.0f) || minimum < 0 || valid_text < 0 || valid_text > text_length)
     return peco::kErrInvalidValue;
   return peco::launch_select(q_centroids, k_centroids, q_sizes, k_sizes, map_ext, bh, cq, ck, dims, top_p, minimum, 1,
-                             valid_text, text_length, q_sizes_ext, k_sizes_ext, static_cast<cudaStream_t>(stream));
+                             valid_text, text_length, q_sizes_ext, k_sizes_ext, logits,
+                             static_cast<cudaStream_t>(stream));
 }

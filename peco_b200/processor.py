@@ -240,12 +240,14 @@ class PecoAttention:
         qs_ext = torch.empty((1, h, gq), dtype=torch.int32, device=dev)
         ks_ext = torch.empty((1, h, gk), dtype=torch.int32, device=dev)
         minimum = math.ceil(self.config.min_kc_ratio * ck)
-        stream = _native.stream_of(dev, emap, qs_ext, ks_ext)
+        logits = torch.empty((h, cq, ck), dtype=torch.float32, device=dev)  # the selection's scratch
+        stream = _native.stream_of(dev, emap, qs_ext, ks_ext, logits)
         with torch.cuda.device(dev):
             st = lib.peco_select_text_partition(
                 _native.ptr(self.q_centroids), _native.ptr(self.k_centroids), _native.ptr(qb.counts),
                 _native.ptr(kb.counts), _native.ptr(emap), _native.ptr(qs_ext), _native.ptr(ks_ext), h, cq, ck, d,
-                float(self.config.top_p), int(minimum), int(valid_text), int(text_length), stream)
+                float(self.config.top_p), int(minimum), int(valid_text), int(text_length), _native.ptr(logits),
+                stream)
             _native.check(st, "peco_select_text_partition")
             if ev:
                 ev["select"].record()

@@ -45,11 +45,15 @@ class BaseOffsetQuantized:
         return dequantize_base_offset(self)
 
 
-def _validate_bits(bits: int, *, allow_bypass: bool) -> None:
-    allowed = (0, 4, 8) if allow_bypass else (4, 8)
-    if type(bits) is not int or bits not in allowed:
-        suffix = "; use fake_quantize_base_offset(..., bits=0) to bypass" if not allow_bypass else ""
-        raise ValueError(f"bits must be one of {allowed}{suffix}")
+def _check_bits(bits: int, *, bypass_ok: bool) -> None:
+    """Accept 4 or 8 bits, and 0 (the identity) where a bypass is allowed.
+
+    The error text is the reference's (peco/quantization.py:55-59) so callers
+    see the same exception; a bool or any non-int type is refused."""
+    choices = (0, 4, 8) if bypass_ok else (4, 8)
+    if type(bits) is not int or bits not in choices:
+        hint = "" if bypass_ok else "; use fake_quantize_base_offset(..., bits=0) to bypass"
+        raise ValueError(f"bits must be one of {choices}{hint}")
 
 
 def _flatten_inputs(x, labels, centroids):
@@ -89,7 +93,7 @@ def _call(mode, flat, lab32, cen, out, codes, low, scale, bits, dtype):
 @torch.no_grad()
 def quantize_base_offset(x, labels, centroids, bits: int = 4) -> BaseOffsetQuantized:
     """Encode Q or K using its assigned cluster's vector centroid (bits 4 or 8)."""
-    _validate_bits(bits, allow_bypass=False)
+    _check_bits(bits, bypass_ok=False)
     flat, lab32, cen = _flatten_inputs(x, labels, centroids)
     bh, n, d = flat.shape
     codes = torch.empty((bh, n, d), dtype=torch.uint8, device=flat.device)
@@ -115,7 +119,7 @@ def dequantize_base_offset(encoded: BaseOffsetQuantized) -> torch.Tensor:
 @torch.no_grad()
 def fake_quantize_base_offset(x, labels, centroids, bits: int = 4) -> torch.Tensor:
     """Quantize/dequantize Q or K in one pass; bits=0 returns ``x`` itself."""
-    _validate_bits(bits, allow_bypass=True)
+    _check_bits(bits, bypass_ok=True)
     if bits == 0:
         return x
     flat, lab32, cen = _flatten_inputs(x, labels, centroids)

@@ -235,8 +235,9 @@ def test_select_text_partition_fused(golden):
     ek = torch.empty((1, h, ck + 2), dtype=torch.int32, device=DEV)
     lib = _native.load()
     args = [qc, kc, qs, ks, emap, eq, ek]
+    logits = torch.empty((h, cq, ck), dtype=torch.float32, device=DEV)  # the caller's scratch
     st = lib.peco_select_text_partition(*[_native.ptr(t) for t in args], h, cq, ck, 128, 1e-9, 8, 24, 32,
-                                        _native.stream_of(qc.device, *args))
+                                        _native.ptr(logits), _native.stream_of(qc.device, *args, logits))
     _native.check(st, "peco_select_text_partition")
     assert torch.equal(emap.cpu(), torch.from_numpy(gd["ext_map"]))
     assert torch.equal(eq.cpu(), torch.from_numpy(gd["ext_q_sizes"]))
