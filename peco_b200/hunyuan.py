@@ -114,6 +114,12 @@ class RowParallelLinear(nn.Module):
         self.tp = tp
         self.weight = _shard(nn.Parameter(torch.empty(dim_out, local)), (dim_out, full_in), cols=list(cols))
         self.bias = _shard(nn.Parameter(torch.empty(dim_out)), (dim_out,))
+        # nn.Linear's default initialisation, with the unsharded fan-in
+        bound = 1.0 / math.sqrt(full_in)
+        with torch.no_grad():
+            if self.weight.device.type != "meta":
+                self.weight.uniform_(-bound, bound)
+                self.bias.uniform_(-bound, bound)
 
     def forward(self, x):
         y = F.linear(x, self.weight)
