@@ -235,44 +235,31 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(const uint8_t* __restri
   if (tid == 0) {
     int nu = 0, cur_lo = 0, cur_rows = 0, cur_ng = 0;
     const int cap = static_cast<int>(g.max_units);
-    for (int q = g.gq - 1; q >= 0; --q) {
-      const int n = gcount[q];
-      if (n > kBM) {
-        if (cur_ng > 0) {
-          if (nu < cap) {
-            ugroup[nu] = (cur_lo << 3) | cur_ng;
-            urows[nu] = cur_rows;
-          }
-          ++nu;
-          cur_rows = cur_ng = 0;
-        }
-        for (int i = 0; i * kBM < n; ++i, ++nu)
-          if (nu < cap) {
-            ugroup[nu] = (q << 3) | 1;
-            urows[nu] = -1 - i;  // piece i of a large group
-          }
-        continue;
-      }
-      if (cur_ng == kMaxGroups || cur_rows + n > kBM) {
-        if (nu < cap) {
-          ugroup[nu] = (cur_lo << 3) | cur_ng;
-          urows[nu] = cur_rows;
-        }
-        ++nu;
-        cur_rows = cur_ng = 0;
-      }
-      if (n == 0 && cur_ng == 0) continue;  // a unit never starts with an empty group
-      cur_lo = q;  // groups are visited in descending order
-      cur_rows += n;
-      ++cur_ng;
-    }
-    if (cur_ng > 0) {
+    auto emit = [&](int code, int rows) {
       if (nu < cap) {
-        ugroup[nu] = (cur_lo << 3) | cur_ng;
-        urows[nu] = cur_rows;
+        ugroup[nu] = code;
+        urows[nu] = rows;
       }
       ++nu;
+    };
+    // per group: the open unit is flushed by a large group, by a fifth group
+    // or by rows beyond kBM; a large group then gets units of its own, any
+    // other group joins the open unit (an empty group never opens one)
+    for (int q = g.gq - 1; q >= 0; --q) {  // groups are visited in descending order
+      const int n = gcount[q];
+      const bool big = n > kBM;
+      const bool flush = cur_ng > 0 && (big || cur_ng == kMaxGroups || cur_rows + n > kBM);
+      if (flush) emit((cur_lo << 3) | cur_ng, cur_rows);
+      cur_rows = flush ? 0 : cur_rows;
+      cur_ng = flush ? 0 : cur_ng;
+      if (big)
+        for (int j = 0; j * kBM < n; ++j) emit((q << 3) | 1, -1 - j);  // piece j of a large group
+      const bool join = !big && (n > 0 || cur_ng > 0);
+      cur_lo = join ? q : cur_lo;
+      cur_rows += join ? n : 0;
+      cur_ng += join ? 1 : 0;
     }
+    if (cur_ng > 0) emit((cur_lo << 3) | cur_ng, cur_rows);
     n_units = min(nu, cap);
     if (part == 0) w[0] = n_units;
   }
@@ -328,22 +315,40 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(const uint8_t* __restri
   __syncthreads();
   const uint8_t* head_map = map + static_cast<long long>(head) * g.gq * g.gk;
   if (map_in_smem) {
-    // eight independent loads in flight per thread
+    // eight independent loads in flight per thread, four map bytes per load
+    // when the head's map is word-aligned (the shared copy always is)
     const int n = g.gq * g.gk;
-    for (int i0 = tid; i0 < n; i0 += 8 * blockDim.x) {
-      uint8_t b[8];
+    if ((reinterpret_cast<uintptr_t>(head_map) & 3) == 0) {
+      const int nw = n >> 2;
+      const uint32_t* src = reinterpret_cast<const uint32_t*>(head_map);
+      uint32_t* dst = reinterpret_cast<uint32_t*>(smap);
+      for (int i0 = tid; i0 < nw; i0 += 8 * blockDim.x) {
+        uint32_t b[8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) b[e] = i0 + e * blockDim.x < n ? head_map[i0 + e * blockDim.x] : 0;
+        for (int e = 0; e < 8; ++e) b[e] = i0 + e * blockDim.x < nw ? src[i0 + e * blockDim.x] : 0u;
 #pragma unroll
-      for (int e = 0; e < 8; ++e)
-        if (i0 + e * blockDim.x < n) smap[i0 + e * blockDim.x] = b[e];
+        for (int e = 0; e < 8; ++e)
+          if (i0 + e * blockDim.x < nw) dst[i0 + e * blockDim.x] = b[e];
+      }
+      for (int i = (nw << 2) + tid; i < n; i += blockDim.x) smap[i] = head_map[i];
+    } else {
+      for (int i0 = tid; i0 < n; i0 += 8 * blockDim.x) {
+        uint8_t b[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) b[e] = i0 + e * blockDim.x < n ? head_map[i0 + e * blockDim.x] : 0;
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (i0 + e * blockDim.x < n) smap[i0 + e * blockDim.x] = b[e];
+      }
     }
     __syncthreads();
     head_map = smap;
   }
   // per unit: the selected key clusters as entries over the unit's block list
   int2* ent_all = reinterpret_cast<int2*>(w + g.off_ent);
-  for (int u = part * nwarps + warp; u < n_units; u += parts * nwarps) {
+  // units dealt round-robin over the head's CTAs first, so each CTA (and
+  // scheduler) scans few of them
+  for (int u = part + parts * warp; u < n_units; u += parts * nwarps) {
     const int lo = ugroup[u] >> 3, ng = ugroup[u] & 7;
     const uint8_t* mrow = head_map + static_cast<long long>(lo) * g.gk;
     int2* ent = ent_all + static_cast<long long>(u) * g.gk;

@@ -999,6 +999,112 @@ __global__ void __launch_bounds__(kUpdateThreads, 8) kmeans_update_kernel(const 
   }
 }
 
+// The same update with W warps per cluster (one block per cluster, bf16
+// tokens), for calls with few heads: there every cluster's block is resident
+// at once and the call waits for its largest cluster, whose rows the one-warp
+// kernel fetches 16 per round trip.  Warp s owns elements [s D/W, (s+1) D/W),
+// lane l the E = D/(32 W) of them from s D/W + l E; the narrower slice per
+// lane lets every warp keep two 32-row batches in flight (the next batch
+// loads while the current one is summed).  Each element is still summed over
+// the cluster's tokens in ascending order, and the norm is reduced in the
+// one-warp kernel's order (per lane of that kernel its D/32 elements, then the
+// lanes by xor) from the means staged in shared memory, so every output is
+// bit-identical to the one-warp kernel's.
+template <int D, int W>
+__global__ void __launch_bounds__(32 * W, 4) kmeans_update_wide_kernel(const UpdateJobs jobs, int bh,
+                                                                       unsigned* status) {
+  using T = __nv_bfloat16;
+  constexpr int E = D / (32 * W);
+  constexpr int kBatch = 32;
+  static_assert(E >= 1 && E * 32 * W == D, "W must divide D / 32");
+  const UpdateJob J = blockIdx.y ? jobs.job[1] : jobs.job[0];  // no dynamic index into the parameters
+  const long long w = blockIdx.x;
+  if (w >= static_cast<long long>(bh) * J.clusters) return;
+  const int sub = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int head = static_cast<int>(w / J.clusters);
+  const int c = static_cast<int>(w - static_cast<long long>(head) * J.clusters);
+  const int start = J.offsets[static_cast<long long>(head) * (J.clusters + 1) + c];
+  int end = J.offsets[static_cast<long long>(head) * (J.clusters + 1) + c + 1];
+  if (J.big_rows > 0 && end - start > J.big_rows) return;  // the block kernel sums it
+  bool bad = start < 0 || end > J.tokens || start > end;
+  if (bad) end = start;
+  const int32_t* perm = J.perm + static_cast<long long>(head) * J.tokens;
+  const int d0 = sub * (D / W) + lane * E;
+  const T* xb = static_cast<const T*>(J.x) + static_cast<long long>(head) * J.head_rows * D + d0;
+  auto token_id = [&](int pos) {
+    int t = 0;
+    if (pos < end) {
+      t = perm[pos];
+      if (t < 0 || t >= J.tokens) {
+        bad = true;
+        t = 0;
+      }
+    }
+    return t;
+  };
+  float acc[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) acc[e] = 0.0f;
+  LaneRaw<T, E> va[kBatch], vb[kBatch];
+  auto load = [&](LaneRaw<T, E>(&v)[kBatch], int ids, int base) {
+    const int cnt = min(kBatch, end - base);
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int t = __shfl_sync(0xffffffffu, ids, u);
+      if (u < cnt) v[u].load(xb + static_cast<long long>(t) * D);
+    }
+  };
+  auto sum = [&](const LaneRaw<T, E>(&v)[kBatch], int base) {
+    const int cnt = min(kBatch, end - base);
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u)
+      if (u < cnt)
+#pragma unroll
+        for (int e = 0; e < E; ++e) acc[e] = __fadd_rn(acc[e], v[u].get(e));
+  };
+  // batch b holds the tokens at positions [start + 32 b, start + 32 b + 32);
+  // its ids are read two batches ahead, its rows one batch ahead
+  int ids_next = token_id(start + kBatch + lane);
+  load(va, token_id(start + lane), start);
+  for (int base = start; base < end; base += 2 * kBatch) {
+    int ids_after = token_id(base + 2 * kBatch + lane);
+    if (base + kBatch < end) load(vb, ids_next, base + kBatch);
+    sum(va, base);
+    if (base + kBatch >= end) break;
+    ids_next = token_id(base + 3 * kBatch + lane);
+    if (base + 2 * kBatch < end) load(va, ids_after, base + 2 * kBatch);
+    sum(vb, base + kBatch);
+  }
+  if (bad) record_status(status, kDevBadIndex);
+  const int n = end - start;
+  const long long o = (static_cast<long long>(head) * J.clusters + c) * D + d0;
+  __shared__ float means[D];
+  float mv[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const float m = n > 0 ? __fdiv_rn(acc[e], static_cast<float>(n)) : J.previous[o + e];
+    mv[e] = m;
+    means[d0 + e] = m;
+    J.means[o + e] = m;
+    if (J.sums) J.sums[o + e] = acc[e];
+  }
+  if (J.image) {
+    const CenterGeom g = center_geom(J.clusters, D);
+    write_image<E>(J.image + static_cast<long long>(head) * g.nchunks * g.b_bytes, g, c, d0, mv);
+  }
+  if (J.norms) {
+    __syncthreads();
+    if (sub == 0) {
+      constexpr int E1 = D / 32;
+      float nsq = 0.0f;
+#pragma unroll
+      for (int e = 0; e < E1; ++e) nsq = fmaf(means[lane * E1 + e], means[lane * E1 + e], nsq);
+      nsq = warp_sum(nsq);
+      if (lane == 0) J.norms[static_cast<long long>(head) * J.clusters + c] = nsq;
+    }
+  }
+}
+
 // The clusters above J.big_rows rows (long sequences, bf16 tokens): one block
 // of D threads per cluster, thread e owning element e.  The whole block loads
 // kBigChunk rows per round trip into shared memory (the next chunk loads while
@@ -1182,13 +1288,37 @@ long long image_bytes_per_head(int C, int dims) {
   return static_cast<long long>(g.nchunks) * g.b_bytes;
 }
 
+// The wide update (two warps per cluster) pays off while every cluster's block
+// is resident at once; measured on B200 at HV-480 shapes (Q 128 + K 256
+// clusters per head): 3, 6 and 12 heads per call gain 60, 58 and 44 us per
+// call, 24 heads (12288 clusters) none.
+constexpr int kUpdateWideWarps = 2;
+constexpr long long kUpdateWideMaxClusters = 8192;
+
 template <typename T>
 int launch_update_t(const UpdateJobs& jobs, int njobs, int bh, int dims, int max_clusters, cudaStream_t stream) {
   const long long warps = static_cast<long long>(bh) * max_clusters;
-  dim3 grid(static_cast<unsigned>((warps * 32 + kUpdateThreads - 1) / kUpdateThreads), njobs);
-  if (dims == 128) kmeans_update_kernel<128, T><<<grid, kUpdateThreads, 0, stream>>>(jobs, bh, device_status_ptr());
-  else if (dims == 64) kmeans_update_kernel<64, T><<<grid, kUpdateThreads, 0, stream>>>(jobs, bh, device_status_ptr());
-  else return kErrUnsupported;
+  // few clusters in all (few heads): a block of several warps per cluster
+  constexpr int kWide = kUpdateWideWarps;
+  bool wide = false;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value && kWide > 1) {
+    wide = warps * njobs <= kUpdateWideMaxClusters;
+    if (wide) {
+      const dim3 wgrid(static_cast<unsigned>(warps), njobs);
+      if (dims == 128)
+        kmeans_update_wide_kernel<128, kWide><<<wgrid, 32 * kWide, 0, stream>>>(jobs, bh, device_status_ptr());
+      else if (dims == 64)
+        kmeans_update_wide_kernel<64, 2><<<wgrid, 64, 0, stream>>>(jobs, bh, device_status_ptr());
+      else
+        return kErrUnsupported;
+    }
+  }
+  if (!wide) {
+    dim3 grid(static_cast<unsigned>((warps * 32 + kUpdateThreads - 1) / kUpdateThreads), njobs);
+    if (dims == 128) kmeans_update_kernel<128, T><<<grid, kUpdateThreads, 0, stream>>>(jobs, bh, device_status_ptr());
+    else if (dims == 64) kmeans_update_kernel<64, T><<<grid, kUpdateThreads, 0, stream>>>(jobs, bh, device_status_ptr());
+    else return kErrUnsupported;
+  }
   if constexpr (std::is_same<T, __nv_bfloat16>::value) {
     bool big = false;
     for (int j = 0; j < njobs; ++j) big = big || jobs.job[j].big_rows > 0;

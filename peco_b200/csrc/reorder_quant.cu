@@ -7,6 +7,8 @@
 // (__fsub_rn/__fdiv_rn/__fmul_rn/__fadd_rn, rintf) so no multiply-add is ever
 // contracted; this reproduces the reference's fp32 torch evaluation bit for
 // bit (peco/quantization.py:111-118, 134-136).
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "../../include/peco_b200.h"
 #include "internal.h"
@@ -66,12 +68,30 @@ inline int grid_for(long long n, int threads) {
 // ---------------------------------------------------------------------------
 // stable counting sort of labels (the argsort of peco/clustering.py:105)
 // ---------------------------------------------------------------------------
-// One CTA per row (head).  Tokens are split into P contiguous partitions, one
-// warp per partition; per-partition histograms give every (partition, label)
-// a base offset in label-major order, and each warp then places its tokens in
-// ascending order.  The result equals a stable argsort: within a label, lower
-// token index first.  Optionally also emits counts [C] and offsets [C+1].
+// A row's tokens are split into contiguous partitions, one warp each;
+// per-partition label counts give every (partition, label) a base offset in
+// label-major order, and each warp then places its tokens in ascending order.
+// The result equals a stable argsort: within a label, lower token index first.
+// Optionally also emits counts [C] and offsets [C+1].  A row is sorted by one
+// thread-block cluster (sort_labels_cluster_kernel, one launch); a long row
+// with segment scratch by the segmented kernels below (three launches).
 constexpr int kSortThreads = 1024;
+
+// Lanes of the warp holding the same label as this lane (labels in
+// [0, 2^nbits), -1 = none), from one ballot per label bit plus one for the
+// sign: a handful of single-cycle votes where __match_any_sync costs hundreds
+// of cycles per call on sm_100a (measured: 14,000 cycles for 8 calls in each
+// of 32 warps of one CTA, against 700 for the votes).
+__device__ __forceinline__ unsigned match_label(int l, int nbits) {
+  const unsigned none = __ballot_sync(0xffffffffu, l < 0);
+  unsigned m = l < 0 ? none : ~none;
+  for (int b = 0; b < nbits; ++b) {
+    const bool bit = (l >> b) & 1;
+    const unsigned bb = __ballot_sync(0xffffffffu, bit);
+    m &= bit ? bb : ~bb;
+  }
+  return m;
+}
 
 struct SortJob {
   const int32_t* labels;
@@ -87,31 +107,29 @@ struct SortJobs {
   SortJob job[2];   // blockIdx.y selects the job (the Q and K sorts of one k-means iteration)
 };
 
-// mode 0: the whole sort of a row in one CTA.  For long rows the sort is
-// split over J.segs CTAs per row, each owning a contiguous token range, in
-// three launches: mode 1 writes each segment's label counts, the scan kernel
-// turns them into per-(segment, label) bases (and the counts and offsets),
-// mode 2 recounts per warp and places the segment's tokens.
+// Long rows with segment scratch: the sort is split over J.segs CTAs per row,
+// each owning a contiguous token range, in three launches: mode 1 writes each
+// segment's label counts, the scan kernel turns them into per-(segment, label)
+// bases (and the counts and offsets), mode 2 recounts per warp and places the
+// segment's tokens.
 __global__ void __launch_bounds__(kSortThreads) stable_sort_labels_kernel(const SortJobs jobs, int mode,
                                                                          unsigned* status) {
   const SortJob J = blockIdx.y ? jobs.job[1] : jobs.job[0];  // no dynamic index into the parameters
-  const int segs = mode ? J.segs : 1;
+  const int segs = J.segs;
   const int row = static_cast<int>(blockIdx.x) / segs, seg = static_cast<int>(blockIdx.x) % segs;
   if (row >= J.rows) return;
   const int32_t* __restrict__ labels = J.labels;
   const long long label_stride = J.label_stride;
   const int tokens = J.tokens, clusters = J.clusters, parts = J.parts;
   int32_t* __restrict__ indices = J.indices;
-  int32_t* __restrict__ counts = J.counts;
-  int32_t* __restrict__ offsets = J.offsets;
   extern __shared__ int32_t sm[];
   int32_t* hist = sm;                         // [parts][clusters]
   int32_t* colsum = sm + parts * clusters;    // [clusters]
-  __shared__ int32_t warp_tot[32];
   const int32_t* lab = labels + row * label_stride;
   int32_t* out_idx = indices + static_cast<long long>(row) * tokens;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const unsigned lt_mask = (1u << lane) - 1u;
+  const int nbits = clusters > 1 ? 32 - __clz(clusters - 1) : 0;
 
   for (int i = threadIdx.x; i < parts * clusters; i += blockDim.x) hist[i] = 0;
   __syncthreads();
@@ -125,6 +143,7 @@ __global__ void __launch_bounds__(kSortThreads) stable_sort_labels_kernel(const 
   // round trip per kSortCache batches.
   constexpr int kSortCache = 8;
   int cached[kSortCache];
+  unsigned cached_peers[kSortCache];  // their match masks, computed once for both passes
   const int p0 = r0 + warp * plen, p1 = min(r1, p0 + plen);
   auto label_at = [&](int t, bool report) {
     int l = (t < p1) ? lab[t] : -1;
@@ -141,7 +160,8 @@ __global__ void __launch_bounds__(kSortThreads) stable_sort_labels_kernel(const 
 #pragma unroll
     for (int i = 0; i < kSortCache; ++i) {
       const int l = cached[i];
-      const unsigned peers = __match_any_sync(0xffffffffu, l);
+      const unsigned peers = match_label(l, nbits);
+      cached_peers[i] = peers;
       if (l >= 0 && (peers & lt_mask) == 0) hist[warp * clusters + l] += __popc(peers);
       __syncwarp();
     }
@@ -153,7 +173,7 @@ __global__ void __launch_bounds__(kSortThreads) stable_sort_labels_kernel(const 
 #pragma unroll
       for (int i = 0; i < kSortCache; ++i) {
         const int l = lb[i];
-        const unsigned peers = __match_any_sync(0xffffffffu, l);
+        const unsigned peers = match_label(l, nbits);
         if (l >= 0 && (peers & lt_mask) == 0) hist[warp * clusters + l] += __popc(peers);
         __syncwarp();
       }
@@ -167,66 +187,24 @@ __global__ void __launch_bounds__(kSortThreads) stable_sort_labels_kernel(const 
     colsum[c] = s;
   }
   __syncthreads();
-  int32_t* segrow = mode ? J.seg + (static_cast<long long>(row) * segs + seg) * clusters : nullptr;
+  int32_t* segrow = J.seg + (static_cast<long long>(row) * segs + seg) * clusters;
   if (mode == 1) {  // this segment's label counts
     for (int c = threadIdx.x; c < clusters; c += blockDim.x) segrow[c] = colsum[c];
     return;
   }
-  if (mode == 2) {  // bases from the scan: hist becomes per-partition base offsets
-    for (int c = threadIdx.x; c < clusters; c += blockDim.x) {
-      int b = segrow[c];
-      for (int p = 0; p < parts; ++p) {
-        const int h = hist[p * clusters + c];
-        hist[p * clusters + c] = b;
-        b += h;
-      }
+  // mode 2: bases from the scan; hist becomes per-partition base offsets
+  for (int c = threadIdx.x; c < clusters; c += blockDim.x) {
+    int b = segrow[c];
+    for (int p = 0; p < parts; ++p) {
+      const int h = hist[p * clusters + c];
+      hist[p * clusters + c] = b;
+      b += h;
     }
-    __syncthreads();
-  } else {
-    // block-wide exclusive scan of colsum (chunked: each thread owns a contiguous run)
-    const int per = (clusters + blockDim.x - 1) / blockDim.x;
-    const int c0 = threadIdx.x * per, c1 = min(clusters, c0 + per);
-    int local = 0;
-    for (int c = c0; c < c1; ++c) local += colsum[c];
-    int incl = local;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int v = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += v;
-    }
-    if (lane == 31) warp_tot[warp] = incl;
-    __syncthreads();
-    if (warp == 0) {
-      int v = warp_tot[lane];
-      int inc = v;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int u = __shfl_up_sync(0xffffffffu, inc, o);
-        if (lane >= o) inc += u;
-      }
-      warp_tot[lane] = inc - v;  // exclusive warp offsets
-    }
-    __syncthreads();
-    int run = warp_tot[warp] + incl - local;  // exclusive prefix for c0
-    for (int c = c0; c < c1; ++c) {
-      const int n = colsum[c];
-      if (counts) counts[static_cast<long long>(row) * clusters + c] = n;
-      if (offsets) offsets[static_cast<long long>(row) * (clusters + 1) + c] = run;
-      int b = run;
-      for (int p = 0; p < parts; ++p) {  // hist becomes per-partition base offsets
-        const int h = hist[p * clusters + c];
-        hist[p * clusters + c] = b;
-        b += h;
-      }
-      run += n;
-    }
-    if (offsets && threadIdx.x == blockDim.x - 1) offsets[static_cast<long long>(row) * (clusters + 1) + clusters] = run;
-    __syncthreads();
-  }  // mode 0
+  }
+  __syncthreads();
   // phase 3: stable placement
   if (warp < parts) {
-    auto place = [&](int t, int l) {
-      const unsigned peers = __match_any_sync(0xffffffffu, l);
+    auto place = [&](int t, int l, unsigned peers) {
       int pos = 0;
       if (l >= 0) pos = hist[warp * clusters + l] + __popc(peers & lt_mask);
       __syncwarp();
@@ -237,13 +215,13 @@ __global__ void __launch_bounds__(kSortThreads) stable_sort_labels_kernel(const 
       __syncwarp();
     };
 #pragma unroll
-    for (int i = 0; i < kSortCache; ++i) place(p0 + 32 * i + lane, cached[i]);
+    for (int i = 0; i < kSortCache; ++i) place(p0 + 32 * i + lane, cached[i], cached_peers[i]);
     for (int base = p0 + 32 * kSortCache; base < p1; base += 32 * kSortCache) {
       int lb[kSortCache];
 #pragma unroll
       for (int i = 0; i < kSortCache; ++i) lb[i] = label_at(base + 32 * i + lane, false);
 #pragma unroll
-      for (int i = 0; i < kSortCache; ++i) place(base + 32 * i + lane, lb[i]);
+      for (int i = 0; i < kSortCache; ++i) place(base + 32 * i + lane, lb[i], match_label(lb[i], nbits));
     }
   }
 }
@@ -304,6 +282,161 @@ __global__ void __launch_bounds__(kSortThreads) sort_segments_scan_kernel(const 
     run += tot[c];
   }
   if (J.offsets && threadIdx.x == blockDim.x - 1) J.offsets[static_cast<long long>(row) * (clusters + 1) + clusters] = run;
+}
+
+// One row per thread-block cluster of kSortCluster CTAs, in one launch.  CTA s
+// of the cluster owns the s-th contiguous segment of the row's tokens and
+// each of its warps a contiguous partition of the segment.  The warps count
+// their labels (shared memory), the CTA sums them into its segment's counts,
+// and after a cluster barrier every CTA reads all segments' counts through
+// distributed shared memory: label totals (their exclusive scan gives the
+// offsets), and the counts of the segments before its own.  Base of
+// (segment s, warp p, label c) = offset[c] + counts of c in segments < s +
+// counts of c in warps < p of segment s: label-major, then token order, so
+// the placement is the stable argsort.  A second cluster barrier keeps every
+// CTA's counts alive until the other CTAs have read them.  Spreading a row
+// over eight SMs is what makes the sort of a short row fast: the whole-row
+// CTA above did all of a row's matching and scattered stores on one SM.
+constexpr int kSortCluster = 8;
+constexpr int kSortClusterThreads = 256;
+constexpr int kSortClusterParts = kSortClusterThreads / 32;
+
+__global__ void __cluster_dims__(kSortCluster, 1, 1) __launch_bounds__(kSortClusterThreads)
+    sort_labels_cluster_kernel(const SortJobs jobs, unsigned* status) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cl = cg::this_cluster();
+  const SortJob J = blockIdx.y ? jobs.job[1] : jobs.job[0];  // no dynamic index into the parameters
+  const int row = static_cast<int>(blockIdx.x) / kSortCluster;
+  if (row >= J.rows) return;  // the whole cluster (one row) leaves together
+  const int seg = static_cast<int>(cl.block_rank());
+  const int tokens = J.tokens, clusters = J.clusters;
+  extern __shared__ int32_t sm[];
+  int32_t* hist = sm;                                         // [parts][clusters]: counts, then bases
+  int32_t* seg_count = sm + kSortClusterParts * clusters;     // [clusters]: this segment's counts
+  int32_t* totals = seg_count + clusters;                     // [clusters]: the row's label counts
+  int32_t* befores = totals + clusters;                       // [clusters]: counts in segments < seg
+  __shared__ int32_t warp_tot[kSortClusterParts];
+  const int32_t* lab = J.labels + row * J.label_stride;
+  int32_t* out_idx = J.indices + static_cast<long long>(row) * tokens;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const unsigned lt_mask = (1u << lane) - 1u;
+  const int nbits = clusters > 1 ? 32 - __clz(clusters - 1) : 0;
+  for (int i = threadIdx.x; i < kSortClusterParts * clusters; i += blockDim.x) hist[i] = 0;
+  const int span = (((tokens + kSortCluster - 1) / kSortCluster) + 31) & ~31;
+  const int r0 = min(tokens, seg * span), r1 = min(tokens, r0 + span);
+  const int plen = (r1 - r0 + kSortClusterParts - 1) / kSortClusterParts;
+  const int p0 = r0 + warp * plen, p1 = min(r1, p0 + plen);
+  auto label_at = [&](int t, bool report) {
+    int l = (t < p1) ? lab[t] : -1;
+    if (l >= clusters || (t < p1 && l < 0)) {
+      if (report) record_status(status, kDevBadIndex);
+      l = -1;
+    }
+    return l;
+  };
+  // the first kCache batches of the partition stay in registers (with their
+  // match masks) for both passes; a longer partition re-reads the rest
+  constexpr int kCache = 4;
+  int cached[kCache];
+  unsigned cached_peers[kCache];
+#pragma unroll
+  for (int i = 0; i < kCache; ++i) cached[i] = label_at(p0 + 32 * i + lane, true);
+  __syncthreads();  // hist zeroed
+  // phase 1: per-warp label counts (one leader lane per distinct label)
+#pragma unroll
+  for (int i = 0; i < kCache; ++i) {
+    const int l = cached[i];
+    const unsigned peers = match_label(l, nbits);
+    cached_peers[i] = peers;
+    if (l >= 0 && (peers & lt_mask) == 0) hist[warp * clusters + l] += __popc(peers);
+    __syncwarp();
+  }
+  for (int base = p0 + 32 * kCache; base < p1; base += 32 * kCache) {
+    int lb[kCache];
+#pragma unroll
+    for (int i = 0; i < kCache; ++i) lb[i] = label_at(base + 32 * i + lane, true);
+#pragma unroll
+    for (int i = 0; i < kCache; ++i) {
+      const unsigned peers = match_label(lb[i], nbits);
+      if (lb[i] >= 0 && (peers & lt_mask) == 0) hist[warp * clusters + lb[i]] += __popc(peers);
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+  // phase 2: this segment's label counts, published to the cluster
+  for (int c = threadIdx.x; c < clusters; c += blockDim.x) {
+    int s = 0;
+#pragma unroll
+    for (int p = 0; p < kSortClusterParts; ++p) s += hist[p * clusters + c];
+    seg_count[c] = s;
+  }
+  cl.sync();
+  // phase 3: label totals over the cluster's segments and the counts of the
+  // segments before this one (each thread a contiguous run of labels); the
+  // exclusive scan of the totals gives the offsets
+  const int per = (clusters + blockDim.x - 1) / blockDim.x;
+  const int c0 = min(clusters, static_cast<int>(threadIdx.x) * per), c1 = min(clusters, c0 + per);
+  int local = 0;
+  for (int c = c0; c < c1; ++c) {
+    int tot = 0, before = 0;
+#pragma unroll
+    for (int g = 0; g < kSortCluster; ++g) {
+      const int n = cl.map_shared_rank(seg_count, g)[c];
+      tot += n;
+      before += g < seg ? n : 0;
+    }
+    totals[c] = tot;
+    befores[c] = before;
+    local += tot;
+  }
+  int incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  int run = incl - local;  // exclusive prefix of c0 within the warp, plus the warps before
+  for (int w2 = 0; w2 < warp; ++w2) run += warp_tot[w2];
+  for (int c = c0; c < c1; ++c) {
+    if (seg == 0) {
+      if (J.counts) J.counts[static_cast<long long>(row) * clusters + c] = totals[c];
+      if (J.offsets) J.offsets[static_cast<long long>(row) * (clusters + 1) + c] = run;
+    }
+    int b = run + befores[c];
+#pragma unroll
+    for (int p = 0; p < kSortClusterParts; ++p) {  // hist becomes per-warp bases
+      const int h = hist[p * clusters + c];
+      hist[p * clusters + c] = b;
+      b += h;
+    }
+    run += totals[c];
+  }
+  if (seg == 0 && J.offsets && c1 == clusters && c0 < c1)
+    J.offsets[static_cast<long long>(row) * (clusters + 1) + clusters] = run;
+  // every CTA has read the others' counts; this CTA's bases are visible to its warps
+  cl.sync();
+  // phase 4: stable placement
+  auto place = [&](int t, int l, unsigned peers) {
+    int pos = 0;
+    if (l >= 0) pos = hist[warp * clusters + l] + __popc(peers & lt_mask);
+    __syncwarp();
+    if (l >= 0) {
+      out_idx[pos] = t;
+      if ((peers & lt_mask) == 0) hist[warp * clusters + l] += __popc(peers);
+    }
+    __syncwarp();
+  };
+#pragma unroll
+  for (int i = 0; i < kCache; ++i) place(p0 + 32 * i + lane, cached[i], cached_peers[i]);
+  for (int base = p0 + 32 * kCache; base < p1; base += 32 * kCache) {
+    int lb[kCache];
+#pragma unroll
+    for (int i = 0; i < kCache; ++i) lb[i] = label_at(base + 32 * i + lane, false);
+#pragma unroll
+    for (int i = 0; i < kCache; ++i) place(base + 32 * i + lane, lb[i], match_label(lb[i], nbits));
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -651,12 +784,13 @@ int launch_stable_sort_jobs(const SortJobInput* in, int njobs, cudaStream_t stre
     if (a.rows < 1 || a.tokens < 1 || a.clusters < 1) return kErrInvalidValue;
     int parts = 32;
     while (parts > 1 && static_cast<long long>(parts) * a.clusters * 4 + a.clusters * 4 > 160 * 1024) parts >>= 1;
-    const size_t need = (static_cast<size_t>(parts) * a.clusters + a.clusters) * sizeof(int32_t);
+    size_t need = (static_cast<size_t>(parts) * a.clusters + a.clusters) * sizeof(int32_t);
     if (need > 200 * 1024) return kErrUnsupported;
+    const bool whole_row = !(a.seg && a.segs > 1);
     smem = need > smem ? need : smem;
     rows = a.rows > rows ? a.rows : rows;
     jobs.job[j] = {a.labels, a.label_stride, a.rows, a.tokens, a.clusters, parts, a.indices, a.counts, a.offsets,
-                   a.seg && a.segs > 1 ? a.segs : 1, a.seg};
+                   whole_row ? 1 : a.segs, a.seg};
     segmented = segmented && a.seg && a.segs > 1;
     max_segs = a.segs > max_segs ? a.segs : max_segs;
     max_clusters = a.clusters > max_clusters ? a.clusters : max_clusters;
@@ -667,7 +801,16 @@ int launch_stable_sort_jobs(const SortJobInput* in, int njobs, cudaStream_t stre
     if (e != cudaSuccess) return static_cast<int>(e);
   }
   if (!segmented) {
-    stable_sort_labels_kernel<<<dim3(rows, njobs), kSortThreads, smem, stream>>>(jobs, 0, device_status_ptr());
+    // one thread-block cluster per row
+    const size_t csmem = static_cast<size_t>(kSortClusterParts + 3) * max_clusters * sizeof(int32_t);
+    if (csmem > 200 * 1024) return kErrUnsupported;
+    if (csmem > 48 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(sort_labels_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(csmem));
+      if (e != cudaSuccess) return static_cast<int>(e);
+    }
+    sort_labels_cluster_kernel<<<dim3(static_cast<unsigned>(rows) * kSortCluster, njobs), kSortClusterThreads, csmem,
+                                 stream>>>(jobs, device_status_ptr());
     return launch_status();
   }
   // long rows: segs CTAs per row (count, scan, place)

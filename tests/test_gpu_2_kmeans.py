@@ -177,6 +177,10 @@ def test_headline_shape_subset():
         init = synthetic.init_centroids(xv, c, w.init)
         lab, cen, cnt, _ = clustering.fit_token_clusters(xv.to(DEV), c, max_iters=w.iters, tol=0,
                                                          init_centroids=init.to(DEV))
+        # few clusters in all: the update runs two warps per cluster; its
+        # centres are exactly the sequential means of the final labels
+        means, _, _ = O.update_centers(xv.float(), lab.cpu(), cen.cpu())
+        assert torch.equal(cen.cpu(), means)
         rl, rc, rn = O.fit_token_clusters(xv, c, w.iters, init)
         mism = (lab.cpu() != rl).float().mean().item()
         assert mism <= 1e-3, mism
@@ -199,6 +203,9 @@ def test_full_headline_pair_reuses_tile_slots():
     qd, kd = q.to(DEV).contiguous(), k.to(DEV).contiguous()
     qb, kb = kmeans_fit_pair(qd, w.seq, nv, qi.to(DEV), kd, w.seq, nv, ki.to(DEV), h, d, iters)
     for xv, init, b, c in ((qv, qi, qb, w.q_clusters), (kv, ki, kb, w.k_clusters)):
+        # 24 heads: one warp per cluster; centres = sequential means of the final labels
+        means, _, _ = O.update_centers(xv.float(), b.labels.cpu(), b.centers.cpu())
+        assert torch.equal(b.centers.cpu(), means)
         for head in (0, h - 1):
             rl, rc, rn = O.fit_token_clusters(xv[head:head + 1], c, iters, init[head:head + 1])
             got = b.labels[head:head + 1].cpu()
