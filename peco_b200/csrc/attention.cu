@@ -146,6 +146,126 @@ __device__ long long block_exclusive_scan(long long v, long long* tmp) {
   return tmp[warp] + incl - v;
 }
 
+// Query groups -> units, by all threads of the block.  The groups are visited
+// in descending order (position k visits group G-1-k); a unit packs
+// consecutive whole groups while their rows fit in kBM and there are at most
+// kMaxGroups of them (empty groups included, but a unit never starts with
+// one); a group of more than kBM rows gets units of its own, one per kBM
+// rows.  As a sequential scan this is a chain of dependent shared-memory
+// steps per group (~180 cycles each on one thread); here every position
+// computes the unit that would start there and the position of the next
+// start, and pointer doubling marks the starts reached from the first one.
+// Writes ugroup[u] = first group << 3 | groups and urows[u] = rows (-1 - i
+// for piece i of a large group) for u < cap; returns the unit count (which
+// may exceed cap).  scratch: 4 (G + 1) ints.
+__device__ int pack_units(const int* gcount, int G, int cap, int* ugroup, int* urows, int* scratch) {
+  int* fvs = scratch;               // [G + 1] first non-empty position >= x (G: none)
+  int* ja = fvs + (G + 1);          // [G + 1] next start, then its doublings
+  int* jb = ja + (G + 1);
+  int* on = jb + (G + 1);           // [G + 1] 1: position starts a unit
+  __shared__ int tmpi[32];
+  __shared__ long long tmpl[32];
+  __shared__ int carry;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  auto size_at = [&](int k) { return gcount[G - 1 - k]; };
+  // 1. fvs: suffix minimum of (non-empty ? x : G), chunks from the top
+  if (tid == 0) carry = G;
+  __syncthreads();
+  for (int hi = G; hi > 0; hi -= blockDim.x) {
+    const int x = hi - 1 - tid;  // descending across threads: the suffix is a prefix in tid
+    int v = (x >= 0 && size_at(x) > 0) ? x : G;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v = min(v, u);
+    }
+    if (lane == 31) tmpi[warp] = v;
+    __syncthreads();
+    int c = carry;
+    for (int w2 = 0; w2 < warp; ++w2) c = min(c, tmpi[w2]);
+    v = min(v, c);
+    if (x >= 0) fvs[x] = v;
+    __syncthreads();
+    if (tid == blockDim.x - 1) carry = v;
+    __syncthreads();
+  }
+  // 2. per position: end of the unit that would start there, next start
+  for (int k = tid; k <= G; k += blockDim.x) {
+    int nx = G;
+    if (k < G && size_at(k) > 0) {
+      int end = k + 1;
+      if (size_at(k) <= kBM) {
+        int rows = 0, ng = 0;
+        end = k;
+        while (end < G && ng < kMaxGroups) {
+          const int n = size_at(end);
+          if (n > kBM || rows + n > kBM) break;
+          rows += n;
+          ++ng;
+          ++end;
+        }
+      }
+      nx = end < G ? fvs[end] : G;
+    }
+    if (k == G) fvs[G] = G;
+    ja[k] = nx;
+    on[k] = 0;
+  }
+  __syncthreads();
+  if (tid == 0) on[fvs[0]] = 1;  // fvs[0] == G: no unit at all (on[G] is a sentinel)
+  __syncthreads();
+  // 3. doubling: after round r every start within 2^(r+1) steps of the first
+  // is marked (marks made during a round only reach further starts sooner)
+  for (int span = 1; span <= G; span <<= 1) {
+    for (int k = tid; k <= G; k += blockDim.x) {
+      const int j = ja[k];
+      if (on[k] && j < G) on[j] = 1;
+      jb[k] = ja[j];
+    }
+    __syncthreads();
+    int* t = ja;
+    ja = jb;
+    jb = t;
+  }
+  // 4. unit numbers: exclusive prefix of the units each start emits
+  if (tid == 0) carry = 0;
+  __syncthreads();
+  for (int k0 = 0; k0 < G; k0 += blockDim.x) {
+    const int k = k0 + tid;
+    int cnt = 0;
+    if (k < G && on[k]) {
+      const int n = size_at(k);
+      cnt = n > kBM ? (n + kBM - 1) / kBM : 1;
+    }
+    const int u0 = carry + static_cast<int>(block_exclusive_scan(cnt, tmpl));
+    if (cnt > 0) {
+      const int q = G - 1 - k, n = size_at(k);
+      if (n > kBM) {
+        for (int i = 0; i < cnt; ++i)
+          if (u0 + i < cap) {
+            ugroup[u0 + i] = (q << 3) | 1;
+            urows[u0 + i] = -1 - i;
+          }
+      } else if (u0 < cap) {
+        int rows = 0, ng = 0, end = k;
+        while (end < G && ng < kMaxGroups) {
+          const int m = size_at(end);
+          if (m > kBM || rows + m > kBM) break;
+          rows += m;
+          ++ng;
+          ++end;
+        }
+        ugroup[u0] = ((G - end) << 3) | ng;  // first group = the last one visited
+        urows[u0] = rows;
+      }
+    }
+    __syncthreads();
+    if (tid == blockDim.x - 1) carry = u0 + cnt;
+    __syncthreads();
+  }
+  return carry;
+}
+
 // Group extents are clamped the way the reference's work map clamps them
 // (sparse_attention.cu:25-31): start_g = min(S, sum_{g'<g} max(0, size_g')).
 // Units of later query groups come first, so the text groups (which attend to
@@ -153,9 +273,9 @@ __device__ long long block_exclusive_scan(long long v, long long* tmp) {
 // least kPlanParts, more when there are few heads): each recomputes the
 // head's prefixes and unit list (cheap) and takes its slice of the key-row
 // map, the padding rows and the units' entry lists; part 0 writes the per-head
-// records.  Dynamic smem: 2 (gk + 1) + 2 gq + 2 max_units ints, then (when
-// ``map_in_smem``) the head's gq x gk map bytes, staged once so the per-unit
-// entry scans read shared rather than global memory.
+// records.  Dynamic smem: 2 (gk + 1) + 2 gq + 2 max_units + 4 (gq + 1) ints,
+// then (when ``map_in_smem``) the head's gq x gk map bytes, staged once so the
+// per-unit entry scans read shared rather than global memory.
 __global__ void __launch_bounds__(1024) attn_plan_kernel(const uint8_t* __restrict__ map,
                                                          const int* __restrict__ q_sizes,
                                                          const int* __restrict__ k_sizes, int* __restrict__ ws,
@@ -168,7 +288,8 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(const uint8_t* __restri
   int* gcount = gstart + g.gq;
   int* ugroup = gcount + g.gq;             // per unit: first group << 3 | groups
   int* urows = ugroup + g.max_units;         // per unit: rows
-  uint8_t* smap = reinterpret_cast<uint8_t*>(urows + g.max_units);
+  int* pack_scratch = urows + g.max_units;   // 4 (gq + 1) ints for pack_units
+  uint8_t* smap = reinterpret_cast<uint8_t*>(pack_scratch + 4 * (g.gq + 1));
   __shared__ long long tmp[32];
   __shared__ long long carry[2];
   __shared__ int n_units;
@@ -230,40 +351,15 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(const uint8_t* __restri
   // start early): consecutive whole groups are packed while the rows fit in
   // kBM and there are at most kMaxGroups of them (a run of groups [lo, lo +
   // ng), empty ones included); a group larger than kBM rows gets units alone.
-  // One thread decides the units (shared memory only); all threads then write
-  // the records.
-  if (tid == 0) {
-    int nu = 0, cur_lo = 0, cur_rows = 0, cur_ng = 0;
+  {
     const int cap = static_cast<int>(g.max_units);
-    auto emit = [&](int code, int rows) {
-      if (nu < cap) {
-        ugroup[nu] = code;
-        urows[nu] = rows;
-      }
-      ++nu;
-    };
-    // per group: the open unit is flushed by a large group, by a fifth group
-    // or by rows beyond kBM; a large group then gets units of its own, any
-    // other group joins the open unit (an empty group never opens one)
-    for (int q = g.gq - 1; q >= 0; --q) {  // groups are visited in descending order
-      const int n = gcount[q];
-      const bool big = n > kBM;
-      const bool flush = cur_ng > 0 && (big || cur_ng == kMaxGroups || cur_rows + n > kBM);
-      if (flush) emit((cur_lo << 3) | cur_ng, cur_rows);
-      cur_rows = flush ? 0 : cur_rows;
-      cur_ng = flush ? 0 : cur_ng;
-      if (big)
-        for (int j = 0; j * kBM < n; ++j) emit((q << 3) | 1, -1 - j);  // piece j of a large group
-      const bool join = !big && (n > 0 || cur_ng > 0);
-      cur_lo = join ? q : cur_lo;
-      cur_rows += join ? n : 0;
-      cur_ng += join ? 1 : 0;
+    const int nu = pack_units(gcount, g.gq, cap, ugroup, urows, pack_scratch);
+    if (tid == 0) {
+      n_units = min(nu, cap);
+      if (part == 0) w[0] = n_units;
     }
-    if (cur_ng > 0) emit((cur_lo << 3) | cur_ng, cur_rows);
-    n_units = min(nu, cap);
-    if (part == 0) w[0] = n_units;
+    __syncthreads();
   }
-  __syncthreads();
   if (part == 0)
     for (int u = tid; u < n_units; u += blockDim.x) {
       const int lo = ugroup[u] >> 3, ng = ugroup[u] & 7;
@@ -1009,7 +1105,8 @@ int launch_attention_plan(const uint8_t* map, const int* q_sizes, const int* k_s
   if ((reinterpret_cast<uintptr_t>(ws) | reinterpret_cast<uintptr_t>(k_blocks) | reinterpret_cast<uintptr_t>(v_blocks)) & 15)
     return kErrInvalidValue;
   const PlanGeom g = plan_geom(sq, sk, gq, gk);
-  size_t smem = sizeof(int) * (2 * static_cast<size_t>(gk + 1) + 2 * static_cast<size_t>(gq) + 2 * g.max_units);
+  size_t smem = sizeof(int) * (2 * static_cast<size_t>(gk + 1) + 2 * static_cast<size_t>(gq) + 2 * g.max_units +
+                               4 * static_cast<size_t>(gq + 1));
   if (smem > 200 * 1024) return kErrUnsupported;
   const size_t map_bytes = static_cast<size_t>(gq) * gk;
   const int map_in_smem = smem + map_bytes <= 160 * 1024 ? 1 : 0;

@@ -658,10 +658,10 @@ struct GatherJobs {
 };
 
 template <int D>
-__global__ void __launch_bounds__(256, 4) quant_gather_kernel(GatherJobs jobs, int bh, int seq, int video, int bits,
+__global__ void __launch_bounds__(256, 6) quant_gather_kernel(GatherJobs jobs, int bh, int seq, int video, int bits,
                                                            unsigned* status) {
   constexpr int G = D / 8;  // lanes per row, 8 elements (16 bytes) each
-  constexpr int R = 4;      // rows in flight per row group
+  constexpr int R = 2;      // rows in flight per row group (with six blocks per SM: measured best)
   // no dynamic index into the kernel parameters (it would copy them to local memory)
   const GatherJob J = blockIdx.y == 0 ? jobs.job[0] : (blockIdx.y == 1 ? jobs.job[1] : jobs.job[2]);
   const bool to_blocks = jobs.plan && blockIdx.y > 0;
@@ -858,7 +858,7 @@ int launch_quant_gather(const void* q, const void* k, const void* v, void* qp, v
   const int threads = 256;
   const int rows_per_block = threads / (dims / 8);
   long long blocks = (rows + rows_per_block - 1) / rows_per_block;
-  const long long cap = static_cast<long long>(kNumSMs) * 8;
+  const long long cap = static_cast<long long>(kNumSMs) * 6;  // blocks per job: six resident per SM
   if (blocks > cap) blocks = cap;
   dim3 grid(static_cast<unsigned>(blocks), 3);
   if (dims == 128)
