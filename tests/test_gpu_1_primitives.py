@@ -242,3 +242,80 @@ def test_select_text_partition_fused(golden):
     assert torch.equal(emap.cpu(), torch.from_numpy(gd["ext_map"]))
     assert torch.equal(eq.cpu(), torch.from_numpy(gd["ext_q_sizes"]))
     assert torch.equal(ek.cpu(), torch.from_numpy(gd["ext_k_sizes"]))
+
+
+def _units_by_rule(sizes, sq):
+    """The planner's packing rule, sequentially: query groups in descending
+    order; consecutive whole groups share a unit while their rows fit in 128
+    and there are at most four (empty groups included, but a unit never starts
+    with one); a group above 128 rows gets one unit per 128 rows.  Returns the
+    (q_start, q_count, first group, groups, bounds) records."""
+    starts, counts, pre = [], [], 0
+    for v in sizes:  # clamped extents
+        v = max(0, v)
+        s0, s1 = min(sq, pre), min(sq, pre + v)
+        starts.append(s0)
+        counts.append(s1 - s0)
+        pre += v
+    units, cur = [], []
+
+    def flush():
+        lo, ng = cur[-1], len(cur)
+        bounds = 0xFFFFFF
+        for m in range(1, ng):
+            bounds = (bounds & ~(0xFF << (8 * (m - 1)))) | ((starts[lo + m] - starts[lo]) << (8 * (m - 1)))
+        units.append((starts[lo], sum(counts[g] for g in cur), lo, ng, bounds))
+        cur.clear()
+
+    for q in range(len(sizes) - 1, -1, -1):
+        n = counts[q]
+        if n > 128:
+            if cur:
+                flush()
+            for i in range((n + 127) // 128):
+                units.append((starts[q] + 128 * i, min(128, n - 128 * i), q, 1, 0xFFFFFF))
+            continue
+        if len(cur) == 4 or sum(counts[g] for g in cur) + n > 128:
+            flush()
+        if n == 0 and not cur:
+            continue
+        cur.append(q)
+    if cur:
+        flush()
+    return units
+
+
+@pytest.mark.parametrize("gq,gk,seed", [(18, 34, 0), (130, 258, 1), (130, 258, 2), (1026, 64, 3)])
+def test_attention_plan_units_follow_the_packing_rule(gq, gk, seed):
+    """The planner packs query groups into units in parallel (next-start
+    pointers and pointer doubling); its unit records must be exactly the ones
+    the sequential packing rule gives, for group sizes with empty groups,
+    groups above 128 rows and sizes past the sequence end (clamped)."""
+    from peco_b200 import _native
+    g = torch.Generator().manual_seed(seed)
+    h = 2
+    kind = torch.randint(0, 4, (h, gq), generator=g)
+    sizes = torch.where(kind == 0, torch.zeros((), dtype=torch.long),
+                        torch.where(kind == 1, torch.randint(129, 400, (h, gq), generator=g),
+                                    torch.randint(1, 90, (h, gq), generator=g)))
+    sq = int(sizes.sum(-1).max()) - 50  # the last groups run past the end and are clamped
+    ks = torch.randint(0, 40, (1, h, gk), generator=g).int()
+    sk = int(ks.sum(-1).max())
+    qs = sizes.view(1, h, gq).int()
+    dmap = torch.rand((1, h, gq, gk), generator=g) < 0.3
+    lib = _native.load()
+    meta = [t.to(DEV).contiguous() for t in (dmap, qs, ks)]
+    stride = int(lib.peco_attention_workspace_stride(sq, sk, gq, gk))
+    ws = torch.zeros(h * stride, dtype=torch.int32, device=DEV)
+    st = lib.peco_attention_plan(*[_native.ptr(t) for t in meta], None, None, _native.ptr(ws), h, sq, sk, 128, gq, gk,
+                                 _native.stream_of(ws.device, *meta, ws))
+    _native.check(st, "peco_attention_plan")
+    ws = ws.view(h, stride).cpu()
+    off_units = (4 + 2 * (gk + 1) + 3) & ~3  # header, then the key row and block prefixes
+    for hh in range(h):
+        want = _units_by_rule(sizes[hh].tolist(), sq)
+        n = int(ws[hh, 0])
+        assert n == len(want)
+        rec = ws[hh, off_units:off_units + 8 * n].view(n, 8)
+        got = [(int(r[0]), int(r[1]), int(r[4]), int(r[5]), int(r[6]) & 0xFFFFFFFF) for r in rec]
+        assert got == want
