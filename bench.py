@@ -55,11 +55,11 @@ def parse_args():
     ap.add_argument("--config", default="hv480")
     ap.add_argument("--top-k", type=int, default=0, help="override the config's top-k key clusters (config 3 sweep)")
     ap.add_argument("--parallel", choices=("heads", "ulysses"), default="heads",
-                    help="heads: every rank runs all heads of its own call (weak scaling); ulysses: one call, "
-                         "tokens sequence-sharded over the ranks and resharded to heads by NCCL all-to-all "
+                    help="heads: one call, its heads split over the ranks (strong scaling); ulysses: one call, "
+                         "tokens sequence-sharded over the ranks and resharded to heads over NVLink peer memory "
                          "(strong scaling, the long-video config)")
     ap.add_argument("--long-steps", type=int, default=10,
-                    help="timed steps of the long-video sub-record (0 skips it)")
+                    help="timed steps of the long-video sub-record, at least about a second's worth (0 skips it)")
     ap.add_argument("--e2e-steps", type=int, default=100)
     ap.add_argument("--cpu-sample-heads", type=int, default=2)
     ap.add_argument("--baselines", choices=("all", "none"), default="all",
@@ -86,15 +86,24 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.lines = []
+        self.first = 0
 
     def start(self):
+        """Start sampling every 100 ms and return once the first sample has
+        arrived (nvidia-smi takes a while to start), so a short timed region
+        that follows is still sampled."""
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200", "-i", str(self.gpu)], stdout=subprocess.PIPE,
+                                          "-lms", "100", "-i", str(self.gpu)], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
             threading.Thread(target=self._read, daemon=True).start()
         except FileNotFoundError:
             self.proc = None
+            return
+        t0 = time.perf_counter()
+        while not self.lines and time.perf_counter() - t0 < 5.0 and self.proc.poll() is None:
+            time.sleep(0.01)
+        self.first = len(self.lines)  # samples before the timed region are not counted
 
     def _read(self):
         for line in self.proc.stdout:
@@ -103,14 +112,15 @@ class ClockSampler:
     def stop(self):
         if self.proc is None:
             return {"samples": 0}
-        time.sleep(0.25)
+        time.sleep(0.12)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
         rows = []
-        for ln in self.lines:
+        # the samples taken during the timed region, plus the one just after it
+        for ln in self.lines[self.first:]:
             parts = [x.strip() for x in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -241,6 +251,15 @@ def run_ulysses(args, world, rank, local, steps=None, warmup=None, config=None):
     for _ in range(warmup):
         call()
     torch.cuda.synchronize()
+    # enough steps for the clock record (samples every 100 ms): the timed
+    # region lasts at least about a second; every rank takes the same count
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    call()
+    e1.record()
+    torch.cuda.synchronize()
+    est = allreduce(e0.elapsed_time(e1), world, "max")
+    steps = max(steps, int(math.ceil(1000.0 / max(est, 1e-3))))
     evs = [{n: torch.cuda.Event(enable_timing=True) for n in ev_names} for _ in range(steps)]
     sampler = ClockSampler(_smi_id(dev))
     barrier(world)
@@ -286,9 +305,11 @@ def run_ulysses(args, world, rank, local, steps=None, warmup=None, config=None):
                         f"CQ={w.q_clusters}, CK={w.k_clusters}, {w.iters} Lloyd iterations, top-{w.top_k}, "
                         f"{w.bits}-bit Base-Offset",
             "parallelism": f"ulysses: tokens sequence-sharded over {world} rank(s), exchanged to {hl} heads per "
-                           f"rank and back ({pdist.last_transport or 'none'}: "
-                           f"{'stores into peer memory over NVLink' if pdist.last_transport == 'peer-memory' else 'point-to-point transfers'}); "
-                           "K's exchange overlaps Q's k-means, V's both",
+                           f"rank and back ("
+                           + ("one rank: no exchange" if world == 1 else
+                              f"{pdist.last_transport}: "
+                              f"{'stores into peer memory over NVLink' if pdist.last_transport == 'peer-memory' else 'point-to-point transfers'}")
+                           + "); K's exchange overlaps Q's k-means, V's both",
             "l2": "flushed before every step (256 MB write), outside the step events",
         },
         "stages": {
