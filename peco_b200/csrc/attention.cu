@@ -86,6 +86,15 @@ struct TileInfo {
   int shift;                  // TMEM lanes below this hold no row of the unit
   uint32_t bounds;            // bytes 0-2: first row (within the unit) of groups 1-3, 0xff = none
 };
+// A split unit's piece, part and part count ride in the tile flags above bit 8
+// (each below 8: kSplitPieces, kSplitParts <= 4).
+__device__ __forceinline__ uint32_t split_flags(int word) {
+  return static_cast<uint32_t>(((word >> 16) & 7) << 6 | ((word >> 8) & 7) << 3 | (word & 7)) << 8;
+}
+__device__ __forceinline__ int split_word(uint32_t flags) {
+  const int f = static_cast<int>(flags >> 8);
+  return ((f >> 6) & 7) << 16 | ((f >> 3) & 7) << 8 | (f & 7);
+}
 
 struct __align__(8) Shared {
   uint64_t q_full[kQBufs], q_empty[kQBufs];
@@ -155,19 +164,30 @@ __device__ long long block_exclusive_scan(long long v, long long* tmp) {
 // steps per group (~180 cycles each on one thread); here every position
 // computes the unit that would start there and the position of the next
 // start, and pointer doubling marks the starts reached from the first one.
-// Writes ugroup[u] = first group << 3 | groups and urows[u] = rows (-1 - i
-// for piece i of a large group) for u < cap; returns the unit count (which
-// may exceed cap).  scratch: 4 (G + 1) ints.
-__device__ int pack_units(const int* gcount, int G, int cap, int* ugroup, int* urows, int* scratch) {
+// Writes ugroup[u] = first group << 3 | groups and urows[u] = rows, or for a
+// piece of a large group -1 - (piece | part << 16 | parts << 24), for u < cap;
+// returns the unit count (which may exceed cap).  With split > 1 the pieces
+// of the first large group visited (at most kSplitPieces of them) become
+// `split` units each, one per key-range part; *n_split is then their piece
+// count (else 0).  scratch: 4 (G + 1) ints.
+__device__ int pack_units(const int* gcount, int G, int cap, int* ugroup, int* urows, int* scratch, int split,
+                          int* n_split) {
   int* fvs = scratch;               // [G + 1] first non-empty position >= x (G: none)
   int* ja = fvs + (G + 1);          // [G + 1] next start, then its doublings
   int* jb = ja + (G + 1);
   int* on = jb + (G + 1);           // [G + 1] 1: position starts a unit
   __shared__ int tmpi[32];
   __shared__ long long tmpl[32];
-  __shared__ int carry;
+  __shared__ int carry, first_big;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   auto size_at = [&](int k) { return gcount[G - 1 - k]; };
+  if (tid == 0) {
+    first_big = G;
+    *n_split = 0;
+  }
+  __syncthreads();
+  for (int k = tid; k < G; k += blockDim.x)
+    if (size_at(k) > kBM) atomicMin(&first_big, k);
   // 1. fvs: suffix minimum of (non-empty ? x : G), chunks from the top
   if (tid == 0) carry = G;
   __syncthreads();
@@ -232,10 +252,15 @@ __device__ int pack_units(const int* gcount, int G, int cap, int* ugroup, int* u
   __syncthreads();
   for (int k0 = 0; k0 < G; k0 += blockDim.x) {
     const int k = k0 + tid;
-    int cnt = 0;
+    int cnt = 0, parts = 1;
     if (k < G && on[k]) {
       const int n = size_at(k);
-      cnt = n > kBM ? (n + kBM - 1) / kBM : 1;
+      const int pieces = (n + kBM - 1) / kBM;
+      if (n > kBM && split > 1 && k == first_big && pieces <= kSplitPieces) {
+        parts = split;
+        *n_split = pieces;
+      }
+      cnt = n > kBM ? pieces * parts : 1;
     }
     const int u0 = carry + static_cast<int>(block_exclusive_scan(cnt, tmpl));
     if (cnt > 0) {
@@ -244,7 +269,7 @@ __device__ int pack_units(const int* gcount, int G, int cap, int* ugroup, int* u
         for (int i = 0; i < cnt; ++i)
           if (u0 + i < cap) {
             ugroup[u0 + i] = (q << 3) | 1;
-            urows[u0 + i] = -1 - i;
+            urows[u0 + i] = parts > 1 ? -1 - ((i / parts) | (i % parts) << 16 | parts << 24) : -1 - i;
           }
       } else if (u0 < cap) {
         int rows = 0, ng = 0, end = k;
@@ -280,7 +305,8 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(const uint8_t* __restri
                                                          const int* __restrict__ q_sizes,
                                                          const int* __restrict__ k_sizes, int* __restrict__ ws,
                                                          const PlanGeom g, unsigned char* k_blocks,
-                                                         unsigned char* v_blocks, int block_bytes, int map_in_smem) {
+                                                         unsigned char* v_blocks, int block_bytes, int map_in_smem,
+                                                         int split) {
   extern __shared__ int plan_sm[];
   int* skp = plan_sm;
   int* sgp = skp + g.gk + 1;
@@ -353,10 +379,14 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(const uint8_t* __restri
   // ng), empty ones included); a group larger than kBM rows gets units alone.
   {
     const int cap = static_cast<int>(g.max_units);
-    const int nu = pack_units(gcount, g.gq, cap, ugroup, urows, pack_scratch);
+    __shared__ int n_split;
+    const int nu = pack_units(gcount, g.gq, cap, ugroup, urows, pack_scratch, split, &n_split);
     if (tid == 0) {
       n_units = min(nu, cap);
-      if (part == 0) w[0] = n_units;
+      if (part == 0) {
+        w[0] = n_units;
+        w[1] = n_split;
+      }
     }
     __syncthreads();
   }
@@ -364,10 +394,19 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(const uint8_t* __restri
     for (int u = tid; u < n_units; u += blockDim.x) {
       const int lo = ugroup[u] >> 3, ng = ugroup[u] & 7;
       int* rec = units + kUnitInts * u;
-      if (urows[u] < 0) {  // piece of a large group
-        const int i = -1 - urows[u];
+      rec[7] = 0;
+      if (urows[u] < 0) {  // piece of a large group (a key-range part of it when split)
+        const int idx = -1 - urows[u];
+        const int i = idx & 0xffff, prt = (idx >> 16) & 0xff, parts = idx >> 24;
         rec[0] = gstart[lo] + i * kBM;
         rec[1] = min(kBM, gcount[lo] - i * kBM);
+        if (parts > 1) {
+          rec[7] = (i << 16) | (prt << 8) | parts;
+          if (prt == 0) {
+            w[g.off_ptab + 2 * i] = rec[0];
+            w[g.off_ptab + 2 * i + 1] = rec[1];
+          }
+        }
       } else {
         rec[0] = gstart[lo];
         rec[1] = urows[u];
@@ -378,7 +417,6 @@ __global__ void __launch_bounds__(1024) attn_plan_kernel(const uint8_t* __restri
       rec[4] = lo;
       rec[5] = ng;
       rec[6] = static_cast<int>(bounds);
-      rec[7] = 0;
     }
   // key row -> row of the key-block image
   int* rows = w + g.off_rows;
@@ -526,7 +564,7 @@ __global__ void pack_key_blocks_kernel(const uint4* __restrict__ k, const uint4*
 // ---------------------------------------------------------------------------
 // main kernel (persistent)
 // ---------------------------------------------------------------------------
-template <int D, int AB>  // AB: 0 = fp16, 1 = bf16
+template <int D, int AB, bool SPLIT>  // AB: 0 = fp16, 1 = bf16; SPLIT: the plan may hold split key ranges
 __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_constant__ CUtensorMap qmap,
                                                                   const AttnArgs args) {
   using L = Layout<D>;
@@ -538,7 +576,6 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
   volatile int* abort_flag = &sh.abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const PlanGeom& g = args.g;
-  const long long total_units = static_cast<long long>(args.bh) * g.max_units;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kQBufs; ++i) {
@@ -587,6 +624,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
     int entry = 0;     // info entries pushed
     int qloads = 0;    // Q tiles loaded
     // lane i < 16 writes mask word i (group i / 4, word i % 4)
+    int unit_split = 0;  // split word of the unit being issued
     auto push_info = [&](uint32_t my_word, int unit, uint32_t flags, int shift, uint32_t bounds) {
       const int slot = entry % kRing;
       if (ok && entry >= kRing) ok = mbar_wait_warp(&sh.info_empty[slot], ((entry / kRing) - 1) & 1, abort_flag, args.status);
@@ -595,7 +633,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
         if (lane < 4 * kMaxGroups) ti.mask[lane >> 2][lane & 3] = my_word;
         if (lane == 0) {
           ti.unit = unit;
-          ti.flags = flags;
+          ti.flags = SPLIT ? (flags | split_flags(unit_split)) : flags;
           ti.shift = shift;
           ti.bounds = bounds;
         }
@@ -605,6 +643,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
       __syncwarp();
       ++entry;
     };
+    const long long total_units = static_cast<long long>(args.bh) * g.max_units;
     for (;;) {
       // ---- claim a unit
       int got = 0;
@@ -628,7 +667,17 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
         if (lane == 0) record_status(args.status, kDevBadIndex);
         nent = nblk = 0;
       }
-      if (nblk == 0) {
+      // a split unit walks only its part of the key tiles
+      const int ntiles_all = (nblk + kTileBlocks - 1) / kTileBlocks;
+      int t_begin = 0, t_end = ntiles_all;
+      const int parts = SPLIT ? (rec2.w & 0xff) : 1, prt = SPLIT ? ((rec2.w >> 8) & 0xff) : 0;
+      if (SPLIT) unit_split = rec2.w;
+      if (SPLIT && parts > 1) {
+        const int per = (ntiles_all + parts - 1) / parts;
+        t_begin = min(ntiles_all, prt * per);
+        t_end = min(ntiles_all, t_begin + per);
+      }
+      if (nblk == 0 || t_begin >= t_end) {
         push_info(0u, static_cast<int>(v), kEmpty, shift, bounds);  // no key at all: rows are zero
         if (!ok) break;
         continue;
@@ -653,8 +702,13 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
         }
       };
       load_window(0);
-      const int ntiles = (nblk + kTileBlocks - 1) / kTileBlocks;
-      for (int t = 0; t < ntiles && ok; ++t) {
+      // a later part: move the window up to its first tile's blocks
+      for (; SPLIT;) {
+        const int passed = __popc(__ballot_sync(0xffffffffu, wend <= t_begin * kTileBlocks));
+        if (passed > 32 - kTileBlocks && w0 + 32 < nent) load_window(w0 + passed);
+        else break;
+      }
+      for (int t = t_begin; t < t_end && ok; ++t) {
         const int p0 = t * kTileBlocks;
         const int before = __popc(__ballot_sync(0xffffffffu, wend <= p0));
         if (before > 32 - kTileBlocks && w0 + 32 < nent) load_window(w0 + before);
@@ -711,7 +765,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
                     static_cast<uint32_t>(rn) * L::kBlockBytes, &sh.slot_full[sl]);
         }
         __syncwarp();
-        if (t == 0) {
+        if (t == t_begin) {
           // first tile of the unit: its Q tile, once the previous unit's last
           // QK has released the buffer (its K/V are already in flight)
           const int qb = qloads % kQBufs, qu = qloads / kQBufs;
@@ -740,7 +794,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
           const unsigned bb = __shfl_sync(0xffffffffu, bytes, 4 * wi + e);
           my_word |= ((bb >> (8 * gi)) & 0xffu) << (8 * e);
         }
-        push_info(my_word, static_cast<int>(v), (t == 0 ? kFirst : 0u) | (t == ntiles - 1 ? kLast : 0u), shift,
+        push_info(my_word, static_cast<int>(v), (t == t_begin ? kFirst : 0u) | (t == t_end - 1 ? kLast : 0u), shift,
                   bounds);
         ++tile;
         if (*abort_flag) ok = false;
@@ -852,6 +906,23 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
       }
       return static_cast<T*>(args.out) + (static_cast<long long>(head) * args.out_rows + orow) * D + (D / 2) * half;
     };
+    // a split unit's partial results for this thread's row: O (fp32,
+    // unnormalised, kPartCols columns) and (max, sum) in the workspace;
+    // split = 0 for a whole unit
+    auto part_row = [&](int v, int sp, int row_shift, int& split, float*& ml) -> float* {
+      const int head = v % args.bh;
+      const int* wh = args.ws + static_cast<long long>(head) * g.stride;
+      split = (sp & 0xff) > 1 ? 1 : 0;
+      ml = nullptr;
+      if (!split) return nullptr;
+      const int rr = r - row_shift;
+      const int piece = sp >> 16, prt = (sp >> 8) & 0xff;
+      if (rr < 0 || piece >= kSplitPieces || prt >= kSplitParts) return nullptr;
+      const long long row = static_cast<long long>(piece * kSplitParts + prt) * kUnitRows + rr;
+      float* wf = reinterpret_cast<float*>(const_cast<int*>(wh));
+      ml = wf + g.off_ml + 2 * row;
+      return wf + g.off_part + row * kPartCols;
+    };
     for (;;) {
       const int slot = entry % kRing;
       ok = mbar_wait_warp(&sh.info_full[slot], (entry / kRing) & 1, abort_flag, args.status);
@@ -873,10 +944,21 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
       ++entry;
       if (ti.flags & kEnd) break;
       if (ti.flags & kEmpty) {
-        T* dst = out_row(ti.unit);
-        if (dst) {
+        int split;
+        float* ml;
+        split = 0;
+        if (SPLIT) part_row(ti.unit, split_word(ti.flags), ti.shift, split, ml);
+        if (SPLIT && split) {  // a key-range part with no tile: contributes nothing
+          if (half == 0 && ml) {
+            ml[0] = -INFINITY;
+            ml[1] = 0.0f;
+          }
+        } else {
+          T* dst = out_row(ti.unit);
+          if (dst) {
 #pragma unroll
-          for (int c = 0; c < D / 16; ++c) reinterpret_cast<uint4*>(dst)[c] = make_uint4(0, 0, 0, 0);
+            for (int c = 0; c < D / 16; ++c) reinterpret_cast<uint4*>(dst)[c] = make_uint4(0, 0, 0, 0);
+          }
         }
         __syncwarp();
         continue;
@@ -990,7 +1072,11 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
         if (!ok) break;
         tc_fence_after();
         // merge factors: half 1 hands (m, l) to half 0, which returns the
-        // scale of each accumulator with 1/L folded in
+        // scale of each accumulator with 1/L folded in (a split part keeps O
+        // unnormalised and records its max and sum instead)
+        int split = 0;
+        float* ml = nullptr;
+        float* prow = (!SPLIT || idle) ? nullptr : part_row(ti.unit, split_word(ti.flags), ti.shift, split, ml);
         float a0, a1;
         if (half == 1) {
           sh.xch[r] = make_float2(m, l);
@@ -1010,14 +1096,18 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
           const float e1 = o.x == -INFINITY ? 0.0f : exp2_approx(o.x - mm);
           const float tot = l * e0 + o.y * e1;
           const float inv = tot > 0.0f ? 1.0f / tot : 0.0f;
-          a0 = e0 * inv;
-          a1 = e1 * inv;
+          a0 = (SPLIT && split) ? e0 : e0 * inv;
+          a1 = (SPLIT && split) ? e1 : e1 * inv;
+          if (SPLIT && split && ml) {
+            ml[0] = mm;
+            ml[1] = tot;
+          }
           sh.xch[r] = make_float2(a0, a1);
           __syncwarp();
           if (lane == 0) mbar_arrive(&sh.xch_back[quarter]);
         }
         ++units_done;
-        T* dst = idle ? nullptr : out_row(ti.unit);
+        T* dst = (idle || (SPLIT && split)) ? nullptr : out_row(ti.unit);
         __syncwarp();
 #pragma unroll
         for (int c = 0; c < D / 64 && !idle; ++c) {
@@ -1025,6 +1115,17 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_attention_tc(const __grid_
           uint32_t v0[32], v1[32];
           tmem_ld32_sync(tmem + 256 + lane_off + (D / 2) * half + c * 32, v0);
           tmem_ld32_sync(tmem + 384 + lane_off + (D / 2) * half + c * 32, v1);
+          if (SPLIT && split && prow) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              float4 f;
+              f.x = __uint_as_float(v0[j]) * a0 + __uint_as_float(v1[j]) * a1;
+              f.y = __uint_as_float(v0[j + 1]) * a0 + __uint_as_float(v1[j + 1]) * a1;
+              f.z = __uint_as_float(v0[j + 2]) * a0 + __uint_as_float(v1[j + 2]) * a1;
+              f.w = __uint_as_float(v0[j + 3]) * a0 + __uint_as_float(v1[j + 3]) * a1;
+              reinterpret_cast<float4*>(prow + (D / 2) * half + c * 32)[j / 4] = f;
+            }
+          }
           if (dst) {
 #pragma unroll
             for (int j = 0; j < 32; j += 8) {
@@ -1069,16 +1170,84 @@ int num_sms() {
   return n > 0 ? n : kNumSMs;
 }
 
+// Merge the key-range parts of every split piece: per row, max M = max_p M_p,
+// sum L = sum_p L_p 2^(M_p - M), O = sum_p O_p 2^(M_p - M) / L (a row no part
+// attended stays zero), written through the same output mapping as the main
+// kernel's epilogue.  Grid (kSplitPieces, BH, D / 8): one thread per (row,
+// 8 output columns), so every thread's loads are in flight together.
+template <int D, int AB>
+__global__ void __launch_bounds__(kUnitRows) split_combine_kernel(const AttnArgs a) {
+  using T = typename std::conditional<AB == 1, __nv_bfloat16, __half>::type;
+  const PlanGeom& g = a.g;
+  const int piece = blockIdx.x, head = blockIdx.y, rr = threadIdx.x, c = 8 * static_cast<int>(blockIdx.z);
+  const int* wh = a.ws + static_cast<long long>(head) * g.stride;
+  if (piece >= min(wh[1], kSplitPieces)) return;
+  const int q_start = wh[g.off_ptab + 2 * piece], q_count = min(max(wh[g.off_ptab + 2 * piece + 1], 0), kUnitRows);
+  if (rr >= q_count) return;
+  const float* wf = reinterpret_cast<const float*>(wh);
+  float mp[kSplitParts], lp[kSplitParts];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int p = 0; p < kSplitParts; ++p) {
+    const long long row = static_cast<long long>(piece * kSplitParts + p) * kUnitRows + rr;
+    mp[p] = wf[g.off_ml + 2 * row];
+    lp[p] = wf[g.off_ml + 2 * row + 1];
+    mx = fmaxf(mx, mp[p]);
+  }
+  float wgt[kSplitParts];
+  float tot = 0.0f;
+#pragma unroll
+  for (int p = 0; p < kSplitParts; ++p) {
+    wgt[p] = (mx == -INFINITY || mp[p] == -INFINITY) ? 0.0f : exp2f(mp[p] - mx);
+    tot += lp[p] * wgt[p];
+  }
+  const float inv = tot > 0.0f ? 1.0f / tot : 0.0f;
+  const int prow = q_start + rr;
+  long long orow = prow;
+  if (a.perm && prow < a.video) orow = a.perm[static_cast<long long>(head) * a.video + prow];
+  if (orow < 0 || orow >= a.out_rows) {
+    record_status(a.status, kDevBadIndex);
+    return;
+  }
+  float acc[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
+#pragma unroll
+  for (int p = 0; p < kSplitParts; ++p) {
+    if (wgt[p] == 0.0f) continue;
+    const float* src = wf + g.off_part + (static_cast<long long>(piece * kSplitParts + p) * kUnitRows + rr) * kPartCols + c;
+    const float4 x0 = reinterpret_cast<const float4*>(src)[0], x1 = reinterpret_cast<const float4*>(src)[1];
+    const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] += xs[e] * wgt[p];
+  }
+  uint4 pk;
+  uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+  for (int e = 0; e < 4; ++e)
+    pw[e] = AB ? pack_bf16x2(acc[2 * e] * inv, acc[2 * e + 1] * inv) : pack_f16x2(acc[2 * e] * inv, acc[2 * e + 1] * inv);
+  T* dst = static_cast<T*>(a.out) + (static_cast<long long>(head) * a.out_rows + orow) * D;
+  reinterpret_cast<uint4*>(dst)[c / 8] = pk;
+}
+
 template <int D, int AB>
 int launch_main(const void* q, const AttnArgs& a, cudaStream_t stream) {
   CUtensorMap qmap;
   if (!make_rows_map(&qmap, q, static_cast<long long>(a.bh) * a.g.sq, D, kBM, AB)) return kErrTensorMap;
   const int smem = Layout<D>::kSmem;
-  cudaError_t e = cudaFuncSetAttribute(sparse_attention_tc<D, AB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  const bool split = attention_split_parts(a.bh) > 1;
+  cudaError_t e = split ? cudaFuncSetAttribute(sparse_attention_tc<D, AB, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)
+                        : cudaFuncSetAttribute(sparse_attention_tc<D, AB, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return static_cast<int>(e);
   const long long total = static_cast<long long>(a.bh) * a.g.max_units;
   const int grid = static_cast<int>(total < num_sms() ? total : num_sms());
-  sparse_attention_tc<D, AB><<<grid, kThreads, smem, stream>>>(qmap, a);
+  if (split) sparse_attention_tc<D, AB, true><<<grid, kThreads, smem, stream>>>(qmap, a);
+  else sparse_attention_tc<D, AB, false><<<grid, kThreads, smem, stream>>>(qmap, a);
+  if (split) {  // the planner split key ranges: merge the parts
+    const int rc = launch_status();
+    if (rc) return rc;
+    split_combine_kernel<D, AB><<<dim3(kSplitPieces, a.bh, D / 8), kUnitRows, 0, stream>>>(a);
+  }
   return launch_status();
 }
 
@@ -1119,7 +1288,8 @@ int launch_attention_plan(const uint8_t* map, const int* q_sizes, const int* k_s
   // per-unit map scans fill the GPU
   const int parts = max(kPlanParts, min(64, num_sms() / bh));
   attn_plan_kernel<<<dim3(bh, parts), 1024, smem, stream>>>(map, q_sizes, k_sizes, ws, g, static_cast<unsigned char*>(k_blocks),
-                                               static_cast<unsigned char*>(v_blocks), kKeyBlockRows * d * 2, map_in_smem);
+                                               static_cast<unsigned char*>(v_blocks), kKeyBlockRows * d * 2, map_in_smem,
+                                               attention_split_parts(bh));
   return launch_status();
 }
 

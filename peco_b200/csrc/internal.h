@@ -70,23 +70,37 @@ constexpr int kKeyBlockRows = 8;
 constexpr int kUnitRows = 128;  // query rows per attention work unit
 
 // Per-head plan workspace (int32), written by the planner kernel:
-//   [0] unit count, [1..3] reserved
+//   [0] unit count, [1] split pieces, [2..3] reserved
 //   kp    [gk+1]            clamped row start of every key cluster
 //   gp    [gk+1]            first key block of every key cluster
-//   units [max_units][4]    q_start, q_count, entry count, block count
+//   units [max_units][8]    q_start, q_count, entry count, block count, first
+//                           group, groups, group bounds, split (piece << 16 |
+//                           part << 8 | parts; 0 = whole)
 //   rows  [sk]              key row -> row in the key-block image (-1: unused)
 //   ent   [max_units][gk]   int2 entries, one per selected key cluster:
 //                           (first block - first position, end position << 4 | rows in last block)
+//   ptab  [2 kSplitPieces]  q_start, q_count of every split piece
+//   part  [kSplitPieces][kSplitParts][kUnitRows][kPartCols] floats: the split
+//         parts' unnormalised outputs, then [..][kUnitRows][2]: their max and sum
 // The last int of the last head's region is the work counter of the
 // persistent attention kernel.
 // ints per work unit in the plan: q_start, q_count, entries, blocks, first
-// query group, groups, group bounds, padding
+// query group, groups, group bounds, split
 constexpr int kUnitInts = 8;
+
+// Calls with few heads split the key range of their first large query group
+// (the text rows, which attend every key) over kSplitParts units, so that
+// group's long key walk runs on several CTAs; a combine kernel merges the
+// parts' partial softmax results.
+constexpr int kSplitPieces = 4;    // 128-row pieces of that group that may split
+constexpr int kSplitParts = 4;     // key-range parts per piece
+constexpr int kPartCols = 128;     // partial output columns (D <= 128)
+inline int attention_split_parts(int bh) { return bh <= 4 ? kSplitParts : 1; }
 
 struct PlanGeom {
   int sq, sk, gq, gk;
   long long max_units, blocks;
-  long long off_kp, off_gp, off_units, off_rows, off_ent, stride;
+  long long off_kp, off_gp, off_units, off_rows, off_ent, off_ptab, off_part, off_ml, stride;
 };
 
 __host__ __device__ inline PlanGeom plan_geom(int sq, int sk, int gq, int gk) {
@@ -95,14 +109,17 @@ __host__ __device__ inline PlanGeom plan_geom(int sq, int sk, int gq, int gk) {
   g.sk = sk;
   g.gq = gq;
   g.gk = gk;
-  g.max_units = (static_cast<long long>(sq) + kUnitRows - 1) / kUnitRows + gq;
+  g.max_units = (static_cast<long long>(sq) + kUnitRows - 1) / kUnitRows + gq + kSplitPieces * (kSplitParts - 1);
   g.blocks = (static_cast<long long>(sk) + kKeyBlockRows - 1) / kKeyBlockRows + gk;
   g.off_kp = 4;
   g.off_gp = g.off_kp + gk + 1;
   g.off_units = (g.off_gp + gk + 1 + 3) & ~3LL;
   g.off_rows = g.off_units + kUnitInts * g.max_units;
   g.off_ent = (g.off_rows + sk + 3) & ~3LL;
-  g.stride = (g.off_ent + 2 * g.max_units * gk + 1 + 3) & ~3LL;
+  g.off_ptab = (g.off_ent + 2 * g.max_units * gk + 3) & ~3LL;
+  g.off_part = g.off_ptab + 2 * kSplitPieces;
+  g.off_ml = g.off_part + static_cast<long long>(kSplitPieces) * kSplitParts * kUnitRows * kPartCols;
+  g.stride = (g.off_ml + 2LL * kSplitPieces * kSplitParts * kUnitRows + 1 + 3) & ~3LL;
   return g;
 }
 

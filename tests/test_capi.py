@@ -46,14 +46,19 @@ def test_pure_host_functions(lib):
     assert l.peco_library_version() == 1
     assert b"no error" in l.peco_error_string(0)
     assert b"workspace" in l.peco_error_string(20005)
-    # plan workspace: header, two cluster prefixes, units (8 ints each), the key-row map
-    # and one int2 entry per (unit, key cluster); key blocks: one 8-row block
-    # per started 8 rows plus one padding block per cluster at most
+    # plan workspace: header, two cluster prefixes, units (8 ints each; up to
+    # 4 x 3 extra units from split key ranges), the key-row map, one int2 entry
+    # per (unit, key cluster), the split-piece table and the split parts'
+    # partial results (4 pieces x 4 parts x 128 rows x (128 + 2) floats); key
+    # blocks: one 8-row block per started 8 rows plus one padding block per
+    # cluster at most
+    partials = 4 * 4 * 128 * (128 + 2)
     for sq, sk, gq, gk in ((11776, 11776, 130, 258), (119056, 119056, 1026, 2050), (64, 80, 64, 64), (1, 1, 1, 1)):
-        units = (sq + 127) // 128 + gq
+        units = (sq + 127) // 128 + gq + 4 * 3
         stride = l.peco_attention_workspace_stride(sq, sk, gq, gk)
-        assert stride % 4 == 0 and stride >= 4 + 2 * (gk + 1) + 8 * units + sk + 2 * units * gk + 1
-        assert stride <= 4 + 2 * (gk + 1) + 8 * units + sk + 2 * units * gk + 16
+        least = 4 + 2 * (gk + 1) + 8 * units + sk + 2 * units * gk + 8 + partials + 1
+        assert stride % 4 == 0 and stride >= least
+        assert stride <= least + 16
         assert l.peco_key_block_rows(sk, gk) == 8 * ((sk + 7) // 8 + gk)
     assert l.peco_attention_workspace_stride(1, 1, 0, 1) == -1
 

@@ -244,12 +244,14 @@ def test_select_text_partition_fused(golden):
     assert torch.equal(ek.cpu(), torch.from_numpy(gd["ext_k_sizes"]))
 
 
-def _units_by_rule(sizes, sq):
+def _units_by_rule(sizes, sq, split=1):
     """The planner's packing rule, sequentially: query groups in descending
     order; consecutive whole groups share a unit while their rows fit in 128
     and there are at most four (empty groups included, but a unit never starts
-    with one); a group above 128 rows gets one unit per 128 rows.  Returns the
-    (q_start, q_count, first group, groups, bounds) records."""
+    with one); a group above 128 rows gets one unit per 128 rows, and with
+    ``split`` > 1 the pieces of the first such group (at most four pieces)
+    get ``split`` units each, one per key-range part.  Returns the (q_start,
+    q_count, first group, groups, bounds, split word) records."""
     starts, counts, pre = [], [], 0
     for v in sizes:  # clamped extents
         v = max(0, v)
@@ -264,16 +266,22 @@ def _units_by_rule(sizes, sq):
         bounds = 0xFFFFFF
         for m in range(1, ng):
             bounds = (bounds & ~(0xFF << (8 * (m - 1)))) | ((starts[lo + m] - starts[lo]) << (8 * (m - 1)))
-        units.append((starts[lo], sum(counts[g] for g in cur), lo, ng, bounds))
+        units.append((starts[lo], sum(counts[g] for g in cur), lo, ng, bounds, 0))
         cur.clear()
 
+    first_big = True
     for q in range(len(sizes) - 1, -1, -1):
         n = counts[q]
         if n > 128:
             if cur:
                 flush()
-            for i in range((n + 127) // 128):
-                units.append((starts[q] + 128 * i, min(128, n - 128 * i), q, 1, 0xFFFFFF))
+            pieces = (n + 127) // 128
+            parts = split if first_big and split > 1 and pieces <= 4 else 1
+            first_big = False
+            for i in range(pieces):
+                for p in range(parts):
+                    word = (i << 16) | (p << 8) | parts if parts > 1 else 0
+                    units.append((starts[q] + 128 * i, min(128, n - 128 * i), q, 1, 0xFFFFFF, word))
             continue
         if len(cur) == 4 or sum(counts[g] for g in cur) + n > 128:
             flush()
@@ -313,9 +321,9 @@ def test_attention_plan_units_follow_the_packing_rule(gq, gk, seed):
     ws = ws.view(h, stride).cpu()
     off_units = (4 + 2 * (gk + 1) + 3) & ~3  # header, then the key row and block prefixes
     for hh in range(h):
-        want = _units_by_rule(sizes[hh].tolist(), sq)
+        want = _units_by_rule(sizes[hh].tolist(), sq, split=4 if h <= 4 else 1)  # few heads: split key ranges
         n = int(ws[hh, 0])
         assert n == len(want)
         rec = ws[hh, off_units:off_units + 8 * n].view(n, 8)
-        got = [(int(r[0]), int(r[1]), int(r[4]), int(r[5]), int(r[6]) & 0xFFFFFFFF) for r in rec]
+        got = [(int(r[0]), int(r[1]), int(r[4]), int(r[5]), int(r[6]) & 0xFFFFFFFF, int(r[7])) for r in rec]
         assert got == want
