@@ -1235,7 +1235,7 @@ int launch_main(const void* q, const AttnArgs& a, cudaStream_t stream) {
   CUtensorMap qmap;
   if (!make_rows_map(&qmap, q, static_cast<long long>(a.bh) * a.g.sq, D, kBM, AB)) return kErrTensorMap;
   const int smem = Layout<D>::kSmem;
-  const bool split = attention_split_parts(a.bh) > 1;
+  const bool split = attention_split_parts(a.bh, a.g.sk) > 1;
   cudaError_t e = split ? cudaFuncSetAttribute(sparse_attention_tc<D, AB, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)
                         : cudaFuncSetAttribute(sparse_attention_tc<D, AB, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return static_cast<int>(e);
@@ -1289,7 +1289,7 @@ int launch_attention_plan(const uint8_t* map, const int* q_sizes, const int* k_s
   const int parts = max(kPlanParts, min(64, num_sms() / bh));
   attn_plan_kernel<<<dim3(bh, parts), 1024, smem, stream>>>(map, q_sizes, k_sizes, ws, g, static_cast<unsigned char*>(k_blocks),
                                                static_cast<unsigned char*>(v_blocks), kKeyBlockRows * d * 2, map_in_smem,
-                                               attention_split_parts(bh));
+                                               attention_split_parts(bh, sk));
   return launch_status();
 }
 

@@ -95,7 +95,11 @@ constexpr int kUnitInts = 8;
 constexpr int kSplitPieces = 4;    // 128-row pieces of that group that may split
 constexpr int kSplitParts = 4;     // key-range parts per piece
 constexpr int kPartCols = 128;     // partial output columns (D <= 128)
-inline int attention_split_parts(int bh) { return bh <= 4 ? kSplitParts : 1; }
+// Split only short sequences: there the text units' key walk is about twice
+// a CTA's average share at <= 4 heads; at 119k keys it is barely above it and
+// the four parts' separate streams over the keys cost more L2 reuse than the
+// balance gains (measured: +5.6% attention at 3 heads).
+inline int attention_split_parts(int bh, int sk) { return bh <= 4 && sk <= 32768 ? kSplitParts : 1; }
 
 struct PlanGeom {
   int sq, sk, gq, gk;
