@@ -1229,7 +1229,13 @@ int launch_assign_t(AssignJobs jobs, const void* const (&x_hi)[2], const void* c
     if (j < jobs.njobs) {
       const CenterGeom g = center_geom(jobs.job[j].clusters, D);
       jobs.items[j] = static_cast<long long>(jobs.bh) * ((jobs.job[j].tokens + kTileM - 1) / kTileM);
-      jobs.cost[j] = static_cast<long long>(g.nchunks) * g.nc;
+      // a token tile costs a fixed part (tile load, hand-offs, labels) plus a
+      // part per centroid column; counting the fixed part (~410 columns'
+      // worth, from per-tile periods at C = 128 and 256) moves CTAs from K to
+      // Q groups.  Measured on HV-480: 12 heads -12 us per call (Q5/K7 CTAs
+      // per head instead of Q4/K8), 6 heads +4-9 us, 3 and 24 heads no
+      // change; so it is counted for 9-16 heads only
+      jobs.cost[j] = (jobs.bh > 8 && jobs.bh <= 16 ? 410LL : 0LL) + static_cast<long long>(g.nchunks) * g.nc;
       total_cost += jobs.items[j] * jobs.cost[j];
     } else {
       jobs.items[j] = 0;
@@ -1248,6 +1254,24 @@ int launch_assign_t(AssignJobs jobs, const void* const (&x_hi)[2], const void* c
       const long long share = nt * jobs.cost[j] * sms / total_cost;
       jobs.split[j] = static_cast<int>(share < 1 ? 1 : (share > nt ? nt : share));
       ctas += static_cast<long long>(jobs.bh) * jobs.split[j];
+    }
+    // with the fixed tile cost counted (9-16 heads), SMs left over go to the
+    // group with the larger remainder, a CTA per head at a time
+    for (int pass = 0; pass < 2 && jobs.bh > 8 && jobs.bh <= 16; ++pass) {
+      int best = -1;
+      long long best_frac = -1;
+      for (int j = 0; j < jobs.njobs; ++j) {
+        const long long nt = (jobs.job[j].tokens + kTileM - 1) / kTileM;
+        const long long frac = (nt * jobs.cost[j] * sms) % total_cost;
+        if (jobs.split[j] < nt && frac > best_frac) {
+          best = j;
+          best_frac = frac;
+        }
+      }
+      if (best >= 0 && ctas + jobs.bh <= sms) {
+        ++jobs.split[best];
+        ctas += jobs.bh;
+      }
     }
     if (ctas <= sms) jobs.ncta = static_cast<int>(ctas);
     else jobs.split[0] = jobs.split[1] = 0;
