@@ -197,6 +197,29 @@ __global__ void __launch_bounds__(kRowThreads) select_row_kernel(const float* __
   }
 }
 
+// Text rows of the extended map and the extended size vectors of one head,
+// by the threads first, first + step, ... (a block or a warp).
+__device__ __forceinline__ void write_text_partition(int head, int first, int step, uint8_t* __restrict__ map,
+                                                     const int32_t* __restrict__ q_sizes,
+                                                     const int32_t* __restrict__ k_sizes, int32_t* __restrict__ q_ext,
+                                                     int32_t* __restrict__ k_ext, int cq, int ck, int valid_text,
+                                                     int text_length) {
+  const int cols = ck + 2;
+  uint8_t* base = map + static_cast<long long>(head) * (cq + 2) * cols;
+  for (int c = first; c < cols; c += step) {
+    base[static_cast<long long>(cq) * cols + c] = c < cols - 1 ? 1 : 0;       // valid text row
+    base[static_cast<long long>(cq + 1) * cols + c] = c == cols - 1 ? 1 : 0;  // padding row
+  }
+  for (int c = first; c < cq; c += step) q_ext[static_cast<long long>(head) * (cq + 2) + c] = q_sizes[static_cast<long long>(head) * cq + c];
+  for (int c = first; c < ck; c += step) k_ext[static_cast<long long>(head) * (ck + 2) + c] = k_sizes[static_cast<long long>(head) * ck + c];
+  if (first == 0) {
+    q_ext[static_cast<long long>(head) * (cq + 2) + cq] = valid_text;
+    q_ext[static_cast<long long>(head) * (cq + 2) + cq + 1] = text_length - valid_text;
+    k_ext[static_cast<long long>(head) * (ck + 2) + ck] = valid_text;
+    k_ext[static_cast<long long>(head) * (ck + 2) + ck + 1] = text_length - valid_text;
+  }
+}
+
 // The same row computation with one WARP per (query cluster, head) for up to
 // 256 key clusters: element i = r * 32 + lane lives in register r of a lane,
 // so the bitonic sort runs on shuffles (partner lanes) and register swaps
@@ -208,7 +231,9 @@ __global__ void __launch_bounds__(256) select_row_warp_kernel(const float* __res
                                                               const int32_t* __restrict__ q_sizes,
                                                               const int32_t* __restrict__ k_sizes,
                                                               uint8_t* __restrict__ map, int cq, int ck, float top_p,
-                                                              int minimum, int extend, int out_cols, int rows) {
+                                                              int minimum, int extend, int out_cols, int rows,
+                                                              int32_t* __restrict__ q_ext, int32_t* __restrict__ k_ext,
+                                                              int valid_text, int text_length) {
   const int wid = static_cast<int>((static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
   const int lane = threadIdx.x & 31;
   if (wid >= rows) return;
@@ -302,27 +327,17 @@ __global__ void __launch_bounds__(256) select_row_warp_kernel(const float* __res
     row[ck] = 1;      // every video query sees the valid text keys
     row[ck + 1] = 0;  // ... never the padding keys
   }
+  // the warp of query cluster 0 also writes its head's text partition (one
+  // launch less than a kernel of its own)
+  if (extend && g == 0)
+    write_text_partition(head, lane, 32, map, q_sizes, k_sizes, q_ext, k_ext, cq, ck, valid_text, text_length);
 }
 
-// Text rows of the extended map and the extended size vectors.
 __global__ void text_partition_kernel(uint8_t* __restrict__ map, const int32_t* __restrict__ q_sizes,
                                       const int32_t* __restrict__ k_sizes, int32_t* __restrict__ q_ext,
                                       int32_t* __restrict__ k_ext, int cq, int ck, int valid_text, int text_length) {
-  const int head = blockIdx.x;
-  const int cols = ck + 2;
-  uint8_t* base = map + static_cast<long long>(head) * (cq + 2) * cols;
-  for (int c = threadIdx.x; c < cols; c += blockDim.x) {
-    base[static_cast<long long>(cq) * cols + c] = c < cols - 1 ? 1 : 0;       // valid text row
-    base[static_cast<long long>(cq + 1) * cols + c] = c == cols - 1 ? 1 : 0;  // padding row
-  }
-  for (int c = threadIdx.x; c < cq; c += blockDim.x) q_ext[static_cast<long long>(head) * (cq + 2) + c] = q_sizes[static_cast<long long>(head) * cq + c];
-  for (int c = threadIdx.x; c < ck; c += blockDim.x) k_ext[static_cast<long long>(head) * (ck + 2) + c] = k_sizes[static_cast<long long>(head) * ck + c];
-  if (threadIdx.x == 0) {
-    q_ext[static_cast<long long>(head) * (cq + 2) + cq] = valid_text;
-    q_ext[static_cast<long long>(head) * (cq + 2) + cq + 1] = text_length - valid_text;
-    k_ext[static_cast<long long>(head) * (ck + 2) + ck] = valid_text;
-    k_ext[static_cast<long long>(head) * (ck + 2) + ck + 1] = text_length - valid_text;
-  }
+  write_text_partition(blockIdx.x, threadIdx.x, blockDim.x, map, q_sizes, k_sizes, q_ext, k_ext, cq, ck, valid_text,
+                       text_length);
 }
 
 }  // namespace
@@ -365,13 +380,17 @@ int launch_select(const float* qc, const float* kc, const int32_t* qs, const int
     const int rows = bh * cq;
     const int wgrid = (rows + 7) / 8;  // 8 warps (rows) per block
     if (np2 <= 32) {
-      select_row_warp_kernel<1><<<wgrid, 256, 0, stream>>>(logits, qs, ks, map, cq, ck, top_p, minimum, extend, out_cols, rows);
+      select_row_warp_kernel<1><<<wgrid, 256, 0, stream>>>(logits, qs, ks, map, cq, ck, top_p, minimum, extend, out_cols, rows,
+                                                            q_ext, k_ext, valid_text, text_length);
     } else if (np2 == 64) {
-      select_row_warp_kernel<2><<<wgrid, 256, 0, stream>>>(logits, qs, ks, map, cq, ck, top_p, minimum, extend, out_cols, rows);
+      select_row_warp_kernel<2><<<wgrid, 256, 0, stream>>>(logits, qs, ks, map, cq, ck, top_p, minimum, extend, out_cols, rows,
+                                                            q_ext, k_ext, valid_text, text_length);
     } else if (np2 == 128) {
-      select_row_warp_kernel<4><<<wgrid, 256, 0, stream>>>(logits, qs, ks, map, cq, ck, top_p, minimum, extend, out_cols, rows);
+      select_row_warp_kernel<4><<<wgrid, 256, 0, stream>>>(logits, qs, ks, map, cq, ck, top_p, minimum, extend, out_cols, rows,
+                                                            q_ext, k_ext, valid_text, text_length);
     } else if (np2 == 256) {
-      select_row_warp_kernel<8><<<wgrid, 256, 0, stream>>>(logits, qs, ks, map, cq, ck, top_p, minimum, extend, out_cols, rows);
+      select_row_warp_kernel<8><<<wgrid, 256, 0, stream>>>(logits, qs, ks, map, cq, ck, top_p, minimum, extend, out_cols, rows,
+                                                            q_ext, k_ext, valid_text, text_length);
     } else {
       select_row_kernel<<<dim3(cq, bh), kRowThreads, row_smem, stream>>>(logits, qs, ks, map, cq, ck, np2, top_p,
                                                                          minimum, extend, out_cols);
@@ -382,7 +401,7 @@ int launch_select(const float* qc, const float* kc, const int32_t* qs, const int
     e = cudaFreeAsync(scratch, stream);
     if (!rc && e != cudaSuccess) rc = static_cast<int>(e);
   }
-  if (rc || !extend) return rc;
+  if (rc || !extend || np2 <= 256) return rc;  // the warp kernel wrote the text partition
   text_partition_kernel<<<bh, 256, 0, stream>>>(map, qs, ks, q_ext, k_ext, cq, ck, valid_text, text_length);
   return launch_status();
 }
