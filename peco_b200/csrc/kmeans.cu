@@ -128,10 +128,20 @@ __device__ __forceinline__ void write_image(unsigned char* img_head, const Cente
 // Norms and image of a set of centroids: one warp per padded centroid row
 // (rows past C get a zero image).  centers [B, C, D]; norms [B, C];
 // image [B, nchunks * b_bytes].
+struct PrepJob {
+  const float* centers;
+  float* norms;
+  unsigned char* image;
+  int C;
+};
+struct PrepJobs {
+  PrepJob job[2];   // blockIdx.y selects the job (the Q and K centres of one fit)
+};
 template <int D>
-__global__ void center_prep_kernel(const float* __restrict__ centers, float* __restrict__ norms,
-                                   unsigned char* __restrict__ image, int bh, int C) {
+__global__ void center_prep_kernel(const PrepJobs jobs, int bh) {
   constexpr int E = D / 32;
+  const PrepJob J = blockIdx.y ? jobs.job[1] : jobs.job[0];  // no dynamic index into the parameters
+  const int C = J.C;
   const CenterGeom g = center_geom(C, D);
   const int padded = g.nchunks * g.nc;
   const long long w = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
@@ -140,14 +150,14 @@ __global__ void center_prep_kernel(const float* __restrict__ centers, float* __r
   const int head = static_cast<int>(w / padded), c = static_cast<int>(w % padded);
   float v[E];
 #pragma unroll
-  for (int e = 0; e < E; ++e) v[e] = c < C ? centers[(static_cast<long long>(head) * C + c) * D + lane * E + e] : 0.0f;
-  if (image) write_image<E>(image + static_cast<long long>(head) * g.nchunks * g.b_bytes, g, c, lane * E, v);
-  if (c < C && norms) {
+  for (int e = 0; e < E; ++e) v[e] = c < C ? J.centers[(static_cast<long long>(head) * C + c) * D + lane * E + e] : 0.0f;
+  if (J.image) write_image<E>(J.image + static_cast<long long>(head) * g.nchunks * g.b_bytes, g, c, lane * E, v);
+  if (c < C && J.norms) {
     float s = 0.0f;
 #pragma unroll
     for (int e = 0; e < E; ++e) s = fmaf(v[e], v[e], s);
     s = warp_sum(s);
-    if (lane == 0) norms[static_cast<long long>(head) * C + c] = s;
+    if (lane == 0) J.norms[static_cast<long long>(head) * C + c] = s;
   }
 }
 
@@ -1297,14 +1307,25 @@ int launch_assign_t(AssignJobs jobs, const void* const (&x_hi)[2], const void* c
 }
 
 // norms and bf16 hi/lo image of [bh, C, D] centroids
-int launch_prep(const float* centers, float* norms, unsigned char* image, int bh, int C, int dims, cudaStream_t stream) {
-  const CenterGeom g = center_geom(C, dims);
-  const long long threads = static_cast<long long>(bh) * g.nchunks * g.nc * 32;
-  const int blocks = static_cast<int>((threads + 255) / 256);
-  if (dims == 128) center_prep_kernel<128><<<blocks, 256, 0, stream>>>(centers, norms, image, bh, C);
-  else if (dims == 64) center_prep_kernel<64><<<blocks, 256, 0, stream>>>(centers, norms, image, bh, C);
+// norms and image of one or two sets of centres, one launch
+int launch_prep_jobs(const PrepJobs& jobs, int njobs, int bh, int dims, cudaStream_t stream) {
+  long long blocks = 1;
+  for (int j = 0; j < njobs; ++j) {
+    const CenterGeom g = center_geom(jobs.job[j].C, dims);
+    const long long b = (static_cast<long long>(bh) * g.nchunks * g.nc * 32 + 255) / 256;
+    blocks = b > blocks ? b : blocks;
+  }
+  const dim3 grid(static_cast<unsigned>(blocks), njobs);
+  if (dims == 128) center_prep_kernel<128><<<grid, 256, 0, stream>>>(jobs, bh);
+  else if (dims == 64) center_prep_kernel<64><<<grid, 256, 0, stream>>>(jobs, bh);
   else return kErrUnsupported;
   return launch_status();
+}
+
+int launch_prep(const float* centers, float* norms, unsigned char* image, int bh, int C, int dims, cudaStream_t stream) {
+  PrepJobs jobs{};
+  jobs.job[0] = {centers, norms, image, C};
+  return launch_prep_jobs(jobs, 1, bh, dims, stream);
 }
 
 long long image_bytes_per_head(int C, int dims) {
@@ -1369,6 +1390,7 @@ int kmeans_fit_bf16(int njobs, const KmeansProblem* probs, int bh, int dims, int
   const void* xs[2] = {probs[0].x, njobs > 1 ? probs[1].x : probs[0].x};
   const void* none[2] = {nullptr, nullptr};
   long long rows[2] = {0, 0};
+  PrepJobs prep{};
   for (int j = 0; j < njobs; ++j) {
     const KmeansProblem& p = probs[j];
     if (p.clusters < 1 || p.tokens < 1 || p.clusters > p.tokens || p.head_rows < p.tokens) return kErrInvalidValue;
@@ -1376,10 +1398,11 @@ int kmeans_fit_bf16(int njobs, const KmeansProblem* probs, int bh, int dims, int
     maxc = max(maxc, p.clusters);
     // the token map covers every head's rows up to the last token
     rows[j] = static_cast<long long>(bh - 1) * p.head_rows + p.tokens;
-    // norms and image of the initial centres
-    rc = launch_prep(p.centers_a, p.norms, p.image, bh, p.clusters, dims, stream);
-    if (rc) return rc;
+    // norms and image of the initial centres (both problems in one launch below)
+    prep.job[j] = {p.centers_a, p.norms, p.image, p.clusters};
   }
+  rc = launch_prep_jobs(prep, njobs, bh, dims, stream);
+  if (rc) return rc;
   for (int it = 0; it < iters; ++it) {
     AssignJobs aj{};
     aj.njobs = njobs;
